@@ -1,0 +1,152 @@
+/*
+ * marian_cuda.h -- C ABI of libmarian_cuda.so, the B200 (sm_100a) backend for
+ * marian-edge's Q8 greedy translation path.
+ *
+ * The ABI mirrors the engine seam a marian-edge backend calls.  Each entry
+ * point names the reference interface it replaces (paths are relative to the
+ * marian-edge repository):
+ *
+ *   mc_create / mc_load_marian_bin   Q8CpuEngine::from_bytes
+ *                                    (crates/marian-cpu/src/q8_engine.rs:175-184)
+ *                                    + MarianBinaryModel::parse
+ *                                    (crates/marian-cpu/src/legacy_q8.rs:179-422)
+ *   mc_translate_token_ids           CpuTokenEngine::translate_token_ids
+ *                                    (crates/marian-cpu/src/backend.rs:48-57,
+ *                                    q8_engine.rs:353-466)
+ *   mc_submit / mc_step / mc_poll    the scheduler's worker loop
+ *                                    (crates/marian-core/src/scheduler.rs:494-659)
+ *                                    as a device-side continuous batcher
+ *   mc_is_ready                      TranslationBackend::is_ready
+ *                                    (crates/marian-core/src/backend.rs:16-18)
+ *   mc_q8_gemm                       Q8Linear::run_into's integer GEMM and
+ *                                    epilogue (crates/marian-cpu/src/q8_gemm.rs:380-448)
+ *
+ * Conventions
+ *   - All pointers are plain host pointers unless a parameter says "device".
+ *     The caller owns every buffer it passes; the engine owns its device
+ *     memory.
+ *   - An engine is not thread-safe; like a TranslationBackend it is created,
+ *     used and destroyed on one thread (marian-core/src/backend.rs:3-7).
+ *   - Every call returns an mc_status.  On failure mc_last_error() holds a
+ *     message.  MC_INVALID_INPUT and MC_MODEL leave the engine usable; after
+ *     MC_INFERENCE with a device fault, MC_CUDA or MC_DEVICE_TIMEOUT the engine
+ *     reports mc_is_ready() == 0 (marian-core/src/scheduler.rs:616-621).
+ */
+#ifndef MARIAN_CUDA_H
+#define MARIAN_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    MC_OK = 0,
+    MC_INVALID_INPUT = 1,   /* BackendError::InvalidInput  (marian-core/src/types.rs:63) */
+    MC_MODEL = 2,           /* BackendError::Model         (types.rs:67) */
+    MC_INFERENCE = 3,       /* BackendError::Inference     (types.rs:69) */
+    MC_DEVICE_TIMEOUT = 4,  /* a bounded device wait gave up */
+    MC_CUDA = 5             /* a CUDA runtime call failed */
+} mc_status;
+
+typedef struct mc_engine mc_engine;
+
+typedef struct {
+    int32_t device;              /* CUDA device ordinal */
+    uint32_t max_inflight;       /* decode slots (default 1024) */
+    uint32_t max_encode_tokens;  /* packed source tokens per encoder pass (default 65536) */
+    uint32_t page_tokens;        /* tokens per KV-cache page (default 16) */
+    uint32_t kv_pages;           /* pages per cache pool; 0 = enough for every slot at full length */
+    uint32_t max_length_factor;  /* Architecture::max_length_factor, 1..8 (default 3) */
+} mc_config;
+
+typedef struct {
+    int32_t dim, heads, ffn_dim;
+    int32_t encoder_layers, decoder_layers;
+    int32_t decoder_kind;        /* 0 = SSRU (reference graph), 1 = self+cross attention */
+    int32_t source_vocab, target_vocab;
+    uint64_t weight_bytes;       /* int8 + f32 bytes resident on the device */
+} mc_model_info;
+
+/* Fills *cfg with the defaults above. */
+void mc_config_default(mc_config *cfg);
+
+/* Creates an engine on cfg->device (CUDA context, stream, status word). */
+mc_status mc_create(const mc_config *cfg, mc_engine **out);
+
+/* Parses a Marian binary v1 model (legacy_q8.rs:179-422 rules), validates the
+ * Q8 tensor schema (q8_engine.rs:1007-1048; SSRU or self-attention decoder)
+ * and uploads it.  Sizes the activation buffers and caches. */
+mc_status mc_load_marian_bin(mc_engine *e, const uint8_t *bytes, size_t len);
+
+mc_status mc_model_info_get(const mc_engine *e, mc_model_info *info);
+
+void mc_destroy(mc_engine *e);
+
+/* Copies the last error message (NUL-terminated, truncated to cap) and
+ * returns its full length. */
+size_t mc_last_error(const mc_engine *e, char *buf, size_t cap);
+
+/* 1 while the engine can accept work; 0 after a terminal device failure. */
+int32_t mc_is_ready(const mc_engine *e);
+
+/* Static batch translation, CpuTokenEngine::translate_token_ids semantics:
+ * tokens[n_tokens] packed, offsets[batch+1] (offsets[0] = 0, last =
+ * n_tokens, each source non-empty and ending in EOS = 0), max_output_tokens
+ * [batch].  force_len (nullable) is the fixed-length harness rule: token 0 is
+ * excluded while step < force_len[b] - 1 and the row stops after
+ * min(max_output_tokens[b], force_len[b]) tokens.  Output: out_offsets
+ * [batch+1] and out_tokens (EOS included when generated), capacity
+ * out_capacity tokens. */
+mc_status mc_translate_token_ids(mc_engine *e, const int32_t *tokens, size_t n_tokens,
+                                 const uint32_t *offsets, uint32_t batch,
+                                 const uint32_t *max_output_tokens, const uint32_t *force_len,
+                                 int32_t *out_tokens, size_t out_capacity,
+                                 uint32_t *out_offsets);
+
+/* Continuous batching.  mc_submit queues one request (tokens end in EOS);
+ * mc_step admits queued requests into free decode slots (one packed encoder
+ * pass) and runs one decode step over every active slot; mc_poll returns
+ * finished requests: ids[i], lengths[i] and their tokens packed in order
+ * into tokens (capacity token_capacity). */
+mc_status mc_submit(mc_engine *e, uint64_t request_id, const int32_t *tokens, uint32_t n_tokens,
+                    uint32_t max_output_tokens, uint32_t force_len);
+mc_status mc_step(mc_engine *e, uint32_t *active_after, uint32_t *queued_after);
+mc_status mc_poll(mc_engine *e, uint64_t *ids, uint32_t *lengths, uint32_t max_results,
+                  int32_t *tokens, size_t token_capacity, uint32_t *n_results);
+
+/* Per-layer capture for parity tests: runs the encoder and the first decode
+ * step of a static batch and copies (host buffers, padded [B, Lmax, dim]
+ * layout as the reference uses, nullable): the encoder output, the cross
+ * keys/values [decoder_layers, B, Lmax, dim] and the final decoder state of
+ * step 0 [B, dim]. */
+mc_status mc_trace_first_step(mc_engine *e, const int32_t *tokens, size_t n_tokens,
+                              const uint32_t *offsets, uint32_t batch, float *encoder_output,
+                              float *cross_key, float *cross_value, float *decoder_state);
+
+/* The engine's stream (a cudaStream_t), for callers that time or order work. */
+void *mc_stream(const mc_engine *e);
+
+/* Device-level Q8 GEMM (benchmark / operator API), Q8Linear::run_into's
+ * integer GEMM and epilogue.  a: device int8 [m, k] (centred activations,
+ * i.e. the reference's u8 minus 127), w: device int8 [n, k] (canonical
+ * [out, in]).  k must be a multiple of 16 and both bases 16-byte aligned.
+ * mode 0 writes the raw int32 accumulators to out [m, n]; mode 1 writes
+ * f32 out = acc * (row_scale[m] * col_scale[n]) + bias[n], then ReLU when
+ * relu != 0, then + residual[m, n]; row_scale, bias and residual are
+ * nullable device pointers.  Runs on stream (a cudaStream_t, 0 = default). */
+mc_status mc_q8_gemm(const int8_t *a, const int8_t *w, int32_t m, int32_t n, int32_t k,
+                     const float *row_scale, const float *col_scale, const float *bias,
+                     const float *residual, int32_t relu, int32_t mode, void *out,
+                     void *stream);
+
+/* Reads and clears the status word the operator API's kernels write on the
+ * current device (non-finite quantizer input, wait timeout); synchronizes. */
+mc_status mc_op_status(uint32_t *status_bits);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,75 @@
+// ops_capi.cu -- operator-level C ABI (device pointers): the Q8 GEMM and the
+// status word its kernels report into.
+#include <cstring>
+#include <mutex>
+
+#include "marian_cuda.h"
+#include "q8_gemm.cuh"
+
+namespace {
+
+std::mutex g_status_mutex;
+uint32_t* g_status[64] = {nullptr};
+
+// The operator API's per-device status word (allocated once per device).
+uint32_t* op_status_word() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_status_mutex);
+  if (!g_status[dev]) {
+    uint32_t* p = nullptr;
+    if (cudaMalloc(&p, sizeof(uint32_t)) != cudaSuccess) return nullptr;
+    if (cudaMemset(p, 0, sizeof(uint32_t)) != cudaSuccess) return nullptr;
+    g_status[dev] = p;
+  }
+  return g_status[dev];
+}
+
+}  // namespace
+
+extern "C" mc_status mc_q8_gemm(const int8_t* a, const int8_t* w, int32_t m, int32_t n, int32_t k,
+                                const float* row_scale, const float* col_scale, const float* bias,
+                                const float* residual, int32_t relu, int32_t mode, void* out,
+                                void* stream) {
+  if (m < 0 || n <= 0 || k <= 0 || (k % 16) != 0 || !a || !w || !out || (mode != 0 && mode != 1) ||
+      (mode == 1 && !col_scale))
+    return MC_INVALID_INPUT;
+  if (m == 0) return MC_OK;
+  uint32_t* status = op_status_word();
+  if (!status) return MC_CUDA;
+  mc::GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  const int bn = mc::pick_bn(m, n);
+  mc::GemmGroup& g = p.g[0];
+  if (!mc::encode_tmap_i8(&g.tmap_a, a, (uint64_t)m, (uint64_t)k, 128) ||
+      !mc::encode_tmap_i8(&g.tmap_b, w, (uint64_t)n, (uint64_t)k, (uint32_t)bn))
+    return MC_INVALID_INPUT;
+  g.col_scale = col_scale;
+  g.row_scale = row_scale;
+  g.bias = bias;
+  g.residual = residual;
+  g.ldr = n;
+  g.out = out;
+  g.n = n;
+  g.ldo = n;
+  g.col_off = 0;
+  g.mode = mode == 0 ? mc::kEpiI32 : mc::kEpiF32;
+  g.relu = relu != 0;
+  p.m = m;
+  p.k = k;
+  p.num_groups = 1;
+  p.max_n = n;
+  p.status = status;
+  cudaError_t e = mc::launch_q8_gemm(p, bn, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MC_OK : MC_CUDA;
+}
+
+extern "C" mc_status mc_op_status(uint32_t* status_bits) {
+  uint32_t* status = op_status_word();
+  if (!status || !status_bits) return MC_CUDA;
+  if (cudaDeviceSynchronize() != cudaSuccess) return MC_CUDA;
+  if (cudaMemcpy(status_bits, status, sizeof(uint32_t), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return MC_CUDA;
+  if (cudaMemset(status, 0, sizeof(uint32_t)) != cudaSuccess) return MC_CUDA;
+  return MC_OK;
+}

@@ -1,0 +1,70 @@
+// q8_gemm.cuh -- host interface of the tcgen05 int8 GEMM.
+//
+// Y[m, n] = epilogue( sum_k A[m, k] * W[n, k] ) with A int8 [M, K] (activations
+// already quantized and centred, i.e. the reference's u8 minus 127) and W int8
+// [N, K] (canonical [out, in] weights, legacy_q8.rs:82-87).  The int32
+// accumulation is exact, as q8_gemm.rs:539-553 requires.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mc {
+
+enum GemmMode : int32_t {
+  kEpiI32 = 0,     // raw int32 accumulators
+  kEpiF32 = 1,     // acc*scale + bias (+ReLU) (+residual), q8_gemm.rs:438-446
+  kEpiQ8 = 2,      // quantize(relu?(acc*scale + bias), alpha) for the next linear
+  kEpiArgmax = 3,  // masked argmax over n of acc*scale + bias (q8_engine.rs:749-790)
+};
+
+// One linear of a grouped launch.  Tensor maps come first so they keep the
+// 64-byte alignment the TMA unit requires of a kernel-parameter map.
+struct alignas(64) GemmGroup {
+  CUtensorMap tmap_a;          // A [rows, K] int8, box {128, 128}, 128-byte swizzle
+  CUtensorMap tmap_b;          // W [N, K] int8, box {128, BN}, 128-byte swizzle
+  const float* col_scale;      // [N]: 1/(alpha_a * w_mult) per output column
+  const float* row_scale;      // [M] or null: extra per-row factor (microbench)
+  const float* bias;           // [N] or null
+  const float* residual;       // [M, ldr] or null (kEpiF32)
+  void* out;                   // float / int8 / int32 output base
+  const int32_t* row_map;      // [M] destination row per source row, or null
+  unsigned long long* argmax;  // [dest rows] packed (value, index) maxima (kEpiArgmax)
+  const uint32_t* cand_bits;   // [ceil(N/32)] candidate bitmask (kEpiArgmax)
+  const uint8_t* eos_mask;     // [M] 1 = token 0 excluded for this row (kEpiArgmax)
+  int32_t n;                   // output columns of this group
+  int32_t ldo;                 // output row stride (elements)
+  int32_t col_off;             // first output column of this group
+  int32_t ldr;                 // residual row stride
+  float alpha;                 // next linear's activation alpha (kEpiQ8)
+  int32_t mode;
+  int32_t relu;
+  int32_t pad_;
+};
+
+constexpr int kMaxGemmGroups = 3;
+
+struct GemmParams {
+  GemmGroup g[kMaxGemmGroups];
+  int32_t m;           // rows of A actually used
+  int32_t k;           // inner dimension (multiple of 16)
+  int32_t num_groups;
+  int32_t max_n;       // max over groups of n
+  uint32_t* status;    // device status word (error bits)
+};
+
+// Encodes a 2-D int8 tensor map over a row-major [rows, cols] matrix with a
+// {128, box_rows} box and the 128-byte swizzle.  Returns false when the
+// driver rejects it (alignment, stride or size).
+bool encode_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                    uint32_t box_rows);
+
+// Picks the N tile (64, 128 or 256) for a launch.
+int pick_bn(int m, int max_n);
+
+// Launches the grouped GEMM.  The tensor maps in p must have been encoded with
+// box_rows == 128 for A and box_rows == bn for B.
+cudaError_t launch_q8_gemm(const GemmParams& p, int bn, cudaStream_t stream);
+
+}  // namespace mc
