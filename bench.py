@@ -1,0 +1,373 @@
+#!/usr/bin/env python
+"""Throughput benchmark of the Q8 greedy translation path on B200.
+
+Metric: target tokens/s (greedy, EOS masked until round(1.2 x src) so the work
+is fixed), whole job over all GPUs.  Workload per step: 20,000 requests with
+lognormal(ln 24, 0.8) source lengths clipped to 4..256 tokens (EOS included),
+Zipf(1.1) ids, all queued at once and served by the continuous batcher
+(1024 decode slots, 16-token KV pages) on the benchmark model shape
+(d=512, 8 heads, 6 encoder layers, 2 self+cross-attention decoder layers,
+FFN 2048, vocabulary 32000, random init, seed 0).  Each rank owns a full model
+replica and its own request stream (request-sharded; no collective on the
+data path).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
+
+The reference arm times the CPU restatement of marian-edge's Q8 engine (the
+Rust reference cannot be built on this image) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "marian-edge_b200"))
+
+from marian_cuda import workloads as W  # noqa: E402
+
+METRIC = "target tokens/sec per box (greedy)"
+UNIT = "tokens/s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
+    p.add_argument("--model", default="graph_b", choices=list(W.SHAPES))
+    p.add_argument("--requests", type=int, default=20000, help="requests per step per GPU")
+    p.add_argument("--max-inflight", type=int, default=1024)
+    p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-latency", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def config_dict(args, world):
+    return {"workload": "continuous-batching stream: %d requests/GPU/step, lognormal(ln24,0.8) src "
+                        "4..256 tok, Zipf(1.1) ids, out=round(1.2*src) EOS-masked" % args.requests,
+            "model_shape": args.model, "d_model": W.SHAPES[args.model].dim,
+            "decoder": W.SHAPES[args.model].decoder_kind, "max_inflight": args.max_inflight,
+            "page_tokens": 16, "parallelism": "replica x%d (request-sharded)" % world,
+            "l2": "no flush: each step streams > 1 GB of KV-cache pages and activations (L2 is 126 MB)"}
+
+
+def step_batches(args, rank, count, base_seed):
+    vocab = W.SHAPES[args.model].vocab
+    return [W.stream_batch(n=args.requests, vocab=vocab, seed=base_seed + 7919 * rank + s) for s in range(count)]
+
+
+# ---- clocks sampler ------------------------------------------------------------
+class Clocks:
+    def __init__(self, device):
+        self.device = device
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), "--query-gpu=clocks.sm,clocks.max.sm,power.draw,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            out, _ = self.proc.communicate(timeout=10)
+            for line in out.strip().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 7:
+                    self.samples.append(parts)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[3 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ---- CPU side (oracle) ---------------------------------------------------------
+def cpu_translate_sample(model_bytes, batches, seconds, threads):
+    """Time the CPU restatement of the reference's Q8 engine on host threads.
+
+    Each thread is one engine worker (the reference's worker pool,
+    marian-core/src/scheduler.rs:179-226) translating reference-legal batches
+    (B <= 256, B*Lmax^2 <= 65536, marian-cpu/src/backend.rs:223-243) of the
+    same request distribution until the time budget is spent.
+    """
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    om = O.OracleModel(model_bytes)
+    work = []
+    for b in batches:
+        for g in W.legal_cpu_batches(b, max_batch=16):
+            work.append(W.subset(b, g))
+    lock = threading.Lock()
+    state = {"next": 0, "tokens": 0, "requests": 0}
+    deadline = time.perf_counter() + seconds
+
+    def worker():
+        while time.perf_counter() < deadline:
+            with lock:
+                i = state["next"]
+                state["next"] += 1
+            if i >= len(work):
+                return
+            sb = work[i]
+            toks, offs = om.translate(sb.tokens, sb.offsets, sb.max_out, sb.force_len)
+            with lock:
+                state["tokens"] += int(offs[-1])
+                state["requests"] += sb.size
+    t0 = time.perf_counter()
+    ts = [threading.Thread(target=worker) for _ in range(threads)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    el = time.perf_counter() - t0
+    return state["tokens"] / el, state["requests"], state["tokens"], el
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ---- reference arm ---------------------------------------------------------------
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    model_bytes = W.synthetic_model(W.SHAPES[args.model], seed=0)
+    threads = host_threads()
+    per_step = max(2.0, args.cpu_seconds / max(1, args.steps))
+    batches = step_batches(args, 0, 1, 1000)
+    for _ in range(args.warmup):
+        cpu_translate_sample(model_bytes, batches, 0.5, threads)
+    vals, reqs, toks, secs = [], 0, 0, 0.0
+    for _ in range(args.steps):
+        v, r, t, s = cpu_translate_sample(model_bytes, batches, per_step, threads)
+        vals.append(v)
+        reqs += r
+        toks += t
+        secs += s
+    value = toks / secs if secs else 0.0
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * secs / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "s8xs8->s32, f32",
+            "data": "synthetic (seeded random-init model and token streams)",
+            "config": config_dict(args, 1),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{reqs} requests ({toks} target tokens) of the same stream over "
+                                       f"{secs:.1f} s, reference-legal CPU batches, {threads} worker threads"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---- CUDA arm --------------------------------------------------------------------
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def run_cuda(args):
+    import torch
+    import torch.distributed as dist
+    from marian_cuda import _lib as L
+    from marian_cuda.backend import CudaEngine
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    model_bytes = W.synthetic_model(W.SHAPES[args.model], seed=0)
+    eng = CudaEngine(model_bytes, device=local, max_inflight=args.max_inflight, max_encode_tokens=65536)
+    lib = L.load()
+    stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
+    warm = step_batches(args, rank, max(1, args.warmup), 100)
+    timed = step_batches(args, rank, args.steps, 1000)
+
+    def run(batch):
+        out, off = eng.translate_token_ids(batch.tokens, batch.offsets, batch.max_out, batch.force_len)
+        return int(off[-1])
+
+    for i in range(args.warmup):
+        run(warm[i % len(warm)])
+
+    # kernel-class profile on one extra (untimed) step of the same stream
+    lib.mc_profile(eng.handle, 1)
+    run(warm[0])
+    prof = {}
+    for k, name in enumerate(L.KERNEL_KINDS):
+        n, ms, fl, by = C.c_uint64(), C.c_double(), C.c_double(), C.c_double()
+        lib.mc_profile_read(eng.handle, k, C.byref(n), C.byref(ms), C.byref(fl), C.byref(by))
+        if n.value:
+            prof[name] = {"launches": n.value, "ms": ms.value, "flops": fl.value, "bytes": by.value}
+    lib.mc_profile(eng.handle, 0)
+
+    torch.cuda.synchronize()
+    barrier()
+    launches0 = lib.mc_launch_count(eng.handle)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    tokens = 0
+    h2d = d2h = 0
+    with Clocks(local) as clocks:
+        torch.cuda.synchronize()
+        start.record(stream)
+        t0 = time.perf_counter()
+        for b in timed:
+            n = run(b)
+            tokens += n
+            h2d += b.tokens.nbytes + b.offsets.nbytes + b.max_out.nbytes + b.force_len.nbytes
+            d2h += 4 * n + 4 * (b.size + 1)
+        end.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    barrier()
+    launches = lib.mc_launch_count(eng.handle) - launches0
+    dev_ms = start.elapsed_time(end)
+    max_ms = max_over_ranks(dev_ms)
+    max_wall = max_over_ranks(wall)
+    all_tokens = sum_over_ranks(float(tokens))
+
+    latency = None
+    if not args.no_latency and rank == 0:
+        latency = poisson_latency(eng, args)
+
+    if rank == 0:
+        peaks, peak_kind = load_peaks()
+        dominant = max(prof.items(), key=lambda kv: kv[1]["ms"]) if prof else None
+        roofline = None
+        if dominant:
+            name, r = dominant
+            per_launch_s = r["ms"] / 1000.0 / r["launches"]
+            if name.startswith("gemm"):
+                peak = 2.0 * peaks["bf16_tflops"]  # dense int8 tensor rate = 2 x bf16
+                achieved = r["flops"] / r["launches"] / per_launch_s / 1e12
+                roofline = {"kernel": name, "bound": "tensor", "achieved": achieved, "peak": peak,
+                            "unit": "TOP/s", "frac": achieved / peak,
+                            "peak_source": f"2 x {peak_kind} bf16 dense TFLOP/s (int8 rate is twice bf16)"}
+            else:
+                peak = peaks["hbm_gbs"]
+                achieved = r["bytes"] / r["launches"] / per_launch_s / 1e9
+                roofline = {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": peak,
+                            "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} HBM copy GB/s"}
+            roofline["traffic"] = None
+            roofline["avg_launch_us"] = per_launch_s * 1e6
+            roofline["share_of_profiled_time"] = r["ms"] / sum(v["ms"] for v in prof.values())
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            threads = host_threads()
+            v, reqs, toks, secs = cpu_translate_sample(model_bytes, timed[:1], args.cpu_seconds, threads)
+            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                   "sample": f"{reqs} requests ({toks} target tokens) of step 0's stream in {secs:.1f} s, "
+                             f"reference-legal CPU batches, {threads} worker threads"}
+        line = {"metric": METRIC, "value": all_tokens / (max_ms / 1000.0), "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "s8xs8->s32 GEMMs, f32 activations/attention/KV",
+                "data": "synthetic (seeded random-init model weights and token streams)",
+                "config": config_dict(args, world),
+                "e2e": {"value": all_tokens / max_wall, "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
+                        "d2h_bytes_per_step": d2h // args.steps,
+                        "path": "mc_translate_token_ids from host numpy buffers, host wall clock"},
+                "gpu_launches": int(launches), "roofline": roofline, "cpu_baseline": cpu,
+                "clocks": clocks.summary(), "kernel_profile": prof, "target_tokens": int(all_tokens)}
+        if latency:
+            line["latency_ms"] = latency
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def poisson_latency(eng, args, n=4000, rate=2000.0):
+    """p50/p99 request latency (arrival -> last token) for Poisson arrivals."""
+    batch = W.stream_batch(n=n, vocab=W.SHAPES[args.model].vocab, seed=4242)
+    arrivals = W.poisson_arrivals(n, rate, seed=4242)
+    lat = {}
+    t0 = time.perf_counter()
+    nxt = 0
+    while len(lat) < n:
+        now = time.perf_counter() - t0
+        while nxt < n and arrivals[nxt] <= now:
+            s, e = batch.offsets[nxt], batch.offsets[nxt + 1]
+            eng.submit(nxt, batch.tokens[s:e], int(batch.max_out[nxt]), int(batch.force_len[nxt]))
+            nxt += 1
+        active, queued = eng.step()
+        now = time.perf_counter() - t0
+        for rid, _ in eng.poll():
+            lat[rid] = now - arrivals[rid]
+        if active == 0 and queued == 0 and nxt < n:
+            time.sleep(max(0.0, min(0.001, arrivals[nxt] - now)))
+    v = np.array(list(lat.values())) * 1000.0
+    return {"p50": float(np.percentile(v, 50)), "p99": float(np.percentile(v, 99)), "requests": n,
+            "arrival_rate_per_s": rate}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_cuda(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -129,6 +129,38 @@ mc_status mc_trace_first_step(mc_engine *e, const int32_t *tokens, size_t n_toke
 /* The engine's stream (a cudaStream_t), for callers that time or order work. */
 void *mc_stream(const mc_engine *e);
 
+/* Kernel classes for the optional per-launch timing of mc_profile.  (The
+ * reference measures its hot spots with a CPU microbenchmark instead,
+ * crates/marian-cpu/benches/hotspots.rs:45-185.) */
+enum {
+    MC_K_EMBED = 0,        /* embedding + positions (+ quantized copies) */
+    MC_K_GEMM_QKV = 1,     /* Q/K/V, SSRU W/Wf and cross-attention Q projections */
+    MC_K_GEMM_OUT = 2,     /* attention output projections */
+    MC_K_GEMM_FFN1 = 3,    /* FFN W1 (+ReLU, quantized for W2) */
+    MC_K_GEMM_FFN2 = 4,    /* FFN W2 */
+    MC_K_GEMM_CROSSKV = 5, /* cross keys/values into the paged cache */
+    MC_K_GEMM_VOCAB = 6,   /* tied vocabulary projection + masked argmax */
+    MC_K_ATTN_ENC = 7,     /* packed varlen encoder self-attention */
+    MC_K_ATTN_SELF = 8,    /* decode self-attention over the paged cache */
+    MC_K_ATTN_CROSS = 9,   /* decode cross-attention over the paged cache */
+    MC_K_LAYERNORM = 10,   /* residual + LayerNorm (+ quantized copies) */
+    MC_K_SSRU = 11,        /* SSRU state update + LayerNorm */
+    MC_K_FINALIZE = 12,    /* token selection bookkeeping */
+    MC_KERNEL_KINDS = 13
+};
+
+/* Enables (1) or disables (0) per-launch CUDA-event timing on the engine
+ * stream and clears the counters. */
+mc_status mc_profile(mc_engine *e, int32_t enable);
+
+/* Reads the counters of one kernel class: launches, total device
+ * milliseconds, and the algorithmic flops and bytes of those launches. */
+mc_status mc_profile_read(const mc_engine *e, int32_t kind, uint64_t *launches, double *ms,
+                          double *flops, double *bytes);
+
+/* Number of kernels the engine has launched since creation. */
+uint64_t mc_launch_count(const mc_engine *e);
+
 /* Device-level Q8 GEMM (benchmark / operator API), Q8Linear::run_into's
  * integer GEMM and epilogue.  a: device int8 [m, k] (centred activations,
  * i.e. the reference's u8 minus 127), w: device int8 [n, k] (canonical

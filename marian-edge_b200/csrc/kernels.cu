@@ -1,0 +1,470 @@
+// kernels.cu -- embedding, residual LayerNorm, SSRU, attention and token
+// selection kernels of the Q8 greedy path (sm_100a).
+//
+// Built with --fmad=false: every expression below rounds after each
+// multiply and each add, matching the reference's Rust f32 arithmetic
+// (crates/marian-cpu/src/tensor.rs).  exp() is evaluated in double precision
+// and rounded once to f32, i.e. the correctly rounded expf in all but
+// double-rounding corner cases; the reference's libm expf is correctly
+// rounded to within a few thousandths of an ulp, so the two agree except on
+// rare inputs.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mc {
+
+namespace {
+
+constexpr float kLnEps = 1.0e-6f;  // tensor.rs:3
+
+__device__ __forceinline__ float exp_f32(float x) {
+  return static_cast<float>(exp(static_cast<double>(x)));
+}
+
+__device__ __forceinline__ void store_quant4(const QuantOut& q, long long elem, float a, float b,
+                                             float c, float d, uint32_t* status) {
+  for (int i = 0; i < q.count; ++i) {
+    const float al = q.alpha[i];
+    const uint32_t w = (uint32_t)(uint8_t)quantize_one(a, al, status) |
+                       ((uint32_t)(uint8_t)quantize_one(b, al, status) << 8) |
+                       ((uint32_t)(uint8_t)quantize_one(c, al, status) << 16) |
+                       ((uint32_t)(uint8_t)quantize_one(d, al, status) << 24);
+    *reinterpret_cast<uint32_t*>(q.base + i * q.stride + elem) = w;
+  }
+}
+
+// ---- embeddings ----------------------------------------------------------------
+__global__ void embed_encoder_kernel(const int32_t* __restrict__ tokens,
+                                     const int32_t* __restrict__ pos_idx, int n_tokens,
+                                     const int8_t* __restrict__ emb, float emb_mult,
+                                     float emb_scale, const float* __restrict__ positions, int d,
+                                     float* __restrict__ x, QuantOut q, uint32_t* status) {
+  const int vec_per_row = d >> 2;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)n_tokens * vec_per_row) return;
+  const int t = static_cast<int>(idx / vec_per_row);
+  const int c = static_cast<int>(idx % vec_per_row) * 4;
+  const int tok = tokens[t];
+  const int p = pos_idx[t];
+  const char4 e = *reinterpret_cast<const char4*>(emb + (size_t)tok * d + c);
+  const float4 pe = *reinterpret_cast<const float4*>(positions + (size_t)p * d + c);
+  float4 v;
+  v.x = (float)e.x / emb_mult * emb_scale + pe.x;
+  v.y = (float)e.y / emb_mult * emb_scale + pe.y;
+  v.z = (float)e.z / emb_mult * emb_scale + pe.z;
+  v.w = (float)e.w / emb_mult * emb_scale + pe.w;
+  const long long elem = (long long)t * d + c;
+  *reinterpret_cast<float4*>(x + elem) = v;
+  store_quant4(q, elem, v.x, v.y, v.z, v.w, status);
+}
+
+__global__ void embed_decoder_kernel(int rows, const int32_t* __restrict__ row_slot,
+                                     const int32_t* __restrict__ slot_prev,
+                                     const int32_t* __restrict__ slot_step,
+                                     const int32_t* __restrict__ slot_force,
+                                     const int8_t* __restrict__ emb, float emb_mult,
+                                     float emb_scale, const float* __restrict__ positions, int d,
+                                     float* __restrict__ x, QuantOut q, uint8_t* eos_mask,
+                                     const int32_t* __restrict__ self_pages, int pages_per_slot,
+                                     int page_tokens, int32_t* self_row_map, uint32_t* status) {
+  const int vec_per_row = d >> 2;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)rows * vec_per_row) return;
+  const int r = static_cast<int>(idx / vec_per_row);
+  const int c = static_cast<int>(idx % vec_per_row) * 4;
+  const int slot = row_slot[r];
+  const int prev = slot_prev[slot];
+  const int t = slot_step[slot];
+  if (t < 0 || t >= kMaxPosition) {
+    flag_status(status, kStatusBadIndex);
+    return;
+  }
+  const float4 pe = *reinterpret_cast<const float4*>(positions + (size_t)t * d + c);
+  float4 v = pe;
+  if (prev >= 0) {
+    const char4 e = *reinterpret_cast<const char4*>(emb + (size_t)prev * d + c);
+    v.x = (float)e.x / emb_mult * emb_scale + pe.x;
+    v.y = (float)e.y / emb_mult * emb_scale + pe.y;
+    v.z = (float)e.z / emb_mult * emb_scale + pe.z;
+    v.w = (float)e.w / emb_mult * emb_scale + pe.w;
+  }
+  const long long elem = (long long)r * d + c;
+  *reinterpret_cast<float4*>(x + elem) = v;
+  store_quant4(q, elem, v.x, v.y, v.z, v.w, status);
+  if (c == 0) {
+    const int force = slot_force[slot];
+    eos_mask[r] = (force > 0 && t + 1 < force) ? 1 : 0;
+    if (self_pages) {
+      const int page = self_pages[(size_t)slot * pages_per_slot + t / page_tokens];
+      self_row_map[r] = page * page_tokens + t % page_tokens;
+    }
+  }
+}
+
+// ---- LayerNorm (normalize_row, tensor.rs:372-385), one thread per row --------
+// The row is first written as a + r (or the SSRU's ReLU + residual), summed
+// left to right, then centred squares are summed left to right, exactly as
+// the reference's Iterator::sum does.
+__device__ __forceinline__ void normalize_row_out(float* __restrict__ o, const float* __restrict__ gamma,
+                                                  const float* __restrict__ beta, int d, float sum,
+                                                  const QuantOut& q, long long qrow,
+                                                  uint32_t* status) {
+  const float fd = (float)d;
+  const float mean = sum / fd;
+  float var = 0.0f;
+  for (int i = 0; i < d; i += 4) {
+    const float4 v = *reinterpret_cast<const float4*>(o + i);
+    float c0 = v.x - mean, c1 = v.y - mean, c2 = v.z - mean, c3 = v.w - mean;
+    var = var + c0 * c0;
+    var = var + c1 * c1;
+    var = var + c2 * c2;
+    var = var + c3 * c3;
+  }
+  var = var / fd;
+  const float inv_std = 1.0f / sqrtf(var + kLnEps);
+  for (int i = 0; i < d; i += 4) {
+    float4 v = *reinterpret_cast<const float4*>(o + i);
+    const float4 g = *reinterpret_cast<const float4*>(gamma + i);
+    const float4 b = *reinterpret_cast<const float4*>(beta + i);
+    v.x = (v.x - mean) * inv_std * g.x + b.x;
+    v.y = (v.y - mean) * inv_std * g.y + b.y;
+    v.z = (v.z - mean) * inv_std * g.z + b.z;
+    v.w = (v.w - mean) * inv_std * g.w + b.w;
+    *reinterpret_cast<float4*>(o + i) = v;
+    store_quant4(q, qrow + i, v.x, v.y, v.z, v.w, status);
+  }
+}
+
+__global__ void residual_ln_kernel(const float* __restrict__ a, int lda, const float* __restrict__ r,
+                                   int ldr, const float* __restrict__ gamma,
+                                   const float* __restrict__ beta, int rows, int d,
+                                   float* __restrict__ out, QuantOut q, uint32_t* status) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const float* ar = a + (size_t)row * lda;
+  const float* rr = r + (size_t)row * ldr;
+  float* o = out + (size_t)row * d;
+  float sum = 0.0f;
+  for (int i = 0; i < d; i += 4) {
+    const float4 x = *reinterpret_cast<const float4*>(ar + i);
+    const float4 y = *reinterpret_cast<const float4*>(rr + i);
+    float4 v;
+    v.x = x.x + y.x;
+    v.y = x.y + y.y;
+    v.z = x.z + y.z;
+    v.w = x.w + y.w;
+    *reinterpret_cast<float4*>(o + i) = v;
+    sum = sum + v.x;
+    sum = sum + v.y;
+    sum = sum + v.z;
+    sum = sum + v.w;
+  }
+  normalize_row_out(o, gamma, beta, d, sum, q, (long long)row * d, status);
+}
+
+__global__ void ssru_kernel(const float* __restrict__ cf, int ld, int fcol, float* __restrict__ state,
+                            const int32_t* __restrict__ row_slot, const float* __restrict__ residual,
+                            const float* __restrict__ gamma, const float* __restrict__ beta,
+                            int rows, int d, float* __restrict__ out, QuantOut q,
+                            uint32_t* status) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const int slot = row_slot[row];
+  const float* cand = cf + (size_t)row * ld;
+  const float* fpre = cand + fcol;
+  float* st = state + (size_t)slot * d;
+  const float* res = residual + (size_t)row * d;
+  float* o = out + (size_t)row * d;
+  float sum = 0.0f;
+  for (int i = 0; i < d; ++i) {
+    const float gate = 1.0f / (1.0f + exp_f32(-fpre[i]));
+    const float next = gate * st[i] + (1.0f - gate) * cand[i];
+    st[i] = next;
+    const float v = fmaxf(next, 0.0f) + res[i];
+    o[i] = v;
+    sum = sum + v;
+  }
+  normalize_row_out(o, gamma, beta, d, sum, q, (long long)row * d, status);
+}
+
+// ---- attention (attention_into, tensor.rs:251-318) ------------------------------
+// Encoder: one CTA per (sequence, head); K and V of that head are staged in
+// shared memory (K rows padded by one float so 32 lanes reading 32 different
+// keys hit 32 different banks); each warp takes one query at a time.
+constexpr int kEncWarps = 4;
+
+__global__ void attn_encoder_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ cu,
+                                    int d, int heads, int max_len, int8_t* __restrict__ out_q,
+                                    float alpha, uint32_t* status) {
+  extern __shared__ float sm[];
+  const int b = blockIdx.x;
+  const int h = blockIdx.y;
+  const int hd = d / heads;
+  const int start = cu[b];
+  const int len = cu[b + 1] - start;
+  if (len <= 0 || len > max_len) {
+    if (threadIdx.x == 0 && len > max_len) flag_status(status, kStatusBadIndex);
+    return;
+  }
+  const int ld = 3 * d;
+  float* ks = sm;                                 // [max_len][hd + 1]
+  float* vs = ks + (size_t)max_len * (hd + 1);     // [max_len][hd]
+  float* qs = vs + (size_t)max_len * hd;          // [warps][hd]
+  float* ps = qs + kEncWarps * hd;                // [warps][max_len]
+  for (int idx = threadIdx.x; idx < len * hd; idx += blockDim.x) {
+    const int j = idx / hd, i = idx % hd;
+    const float* row = qkv + (size_t)(start + j) * ld + h * hd + i;
+    ks[j * (hd + 1) + i] = row[d];
+    vs[j * hd + i] = row[2 * d];
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float scale = 1.0f / sqrtf((float)hd);
+  float* qw = qs + warp * hd;
+  float* pw = ps + warp * max_len;
+  for (int qi = warp; qi < len; qi += kEncWarps) {
+    const float* qrow = qkv + (size_t)(start + qi) * ld + h * hd;
+    for (int i = lane; i < hd; i += 32) qw[i] = qrow[i];
+    __syncwarp();
+    float mx = -INFINITY;
+    for (int j = lane; j < len; j += 32) {
+      const float* kr = ks + j * (hd + 1);
+      float dot = 0.0f;
+      for (int i = 0; i < hd; ++i) dot = dot + qw[i] * kr[i];
+      const float s = dot * scale;
+      pw[j] = s;
+      mx = fmaxf(mx, s);
+    }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int j = lane; j < len; j += 32) pw[j] = exp_f32(pw[j] - mx);
+    __syncwarp();
+    float inv = 0.0f;
+    if (lane == 0) {
+      float sum = 0.0f;
+      for (int j = 0; j < len; ++j) sum = sum + pw[j];
+      inv = 1.0f / sum;
+    }
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    for (int j = lane; j < len; j += 32) pw[j] = pw[j] * inv;
+    __syncwarp();
+    for (int i = lane; i < hd; i += 32) {
+      float acc = 0.0f;
+      for (int j = 0; j < len; ++j) acc = acc + vs[j * hd + i] * pw[j];
+      out_q[(size_t)(start + qi) * d + h * hd + i] = quantize_one(acc, alpha, status);
+    }
+    __syncwarp();
+  }
+}
+
+// Decode: one CTA per active row, one warp per head.  Each lane scores its
+// own keys with a sequential dot product; one lane sums the exponentials in
+// key order; each lane then accumulates up to four output dimensions over the
+// keys in order.  Cache rows are found through the slot's page table.
+__global__ void attn_decode_kernel(const float* __restrict__ q, int ldq,
+                                   const int32_t* __restrict__ row_slot,
+                                   const int32_t* __restrict__ slot_len, int len_add,
+                                   const int32_t* __restrict__ page_table, int pages_per_slot,
+                                   int page_tokens, const float* __restrict__ k_pool,
+                                   const float* __restrict__ v_pool, int d, int heads,
+                                   int8_t* __restrict__ out_q, float alpha, uint32_t* status) {
+  extern __shared__ float sm[];
+  const int r = blockIdx.x;
+  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hd = d / heads;
+  const int slot = row_slot[r];
+  const int len = slot_len[slot] + len_add;
+  if (len <= 0 || len > kMaxSeq || len > pages_per_slot * page_tokens) {
+    if (threadIdx.x == 0) flag_status(status, kStatusBadIndex);
+    return;
+  }
+  float* qw = sm + h * hd;                        // [heads][hd]
+  float* pw = sm + heads * hd + h * kMaxSeq;      // [heads][kMaxSeq]
+  int* rows_s = reinterpret_cast<int*>(sm + heads * hd + heads * kMaxSeq);  // [kMaxSeq]
+  const int32_t* pages = page_table + (size_t)slot * pages_per_slot;
+  for (int j = threadIdx.x; j < len; j += blockDim.x)
+    rows_s[j] = pages[j / page_tokens] * page_tokens + j % page_tokens;
+  for (int i = lane; i < hd; i += 32) qw[i] = q[(size_t)r * ldq + h * hd + i];
+  __syncthreads();
+  const float scale = 1.0f / sqrtf((float)hd);
+  float mx = -INFINITY;
+  for (int j = lane; j < len; j += 32) {
+    const float* kr = k_pool + (size_t)rows_s[j] * d + h * hd;
+    float dot = 0.0f;
+    for (int i = 0; i < hd; i += 4) {
+      const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
+      dot = dot + qw[i] * k4.x;
+      dot = dot + qw[i + 1] * k4.y;
+      dot = dot + qw[i + 2] * k4.z;
+      dot = dot + qw[i + 3] * k4.w;
+    }
+    const float s = dot * scale;
+    pw[j] = s;
+    mx = fmaxf(mx, s);
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  for (int j = lane; j < len; j += 32) pw[j] = exp_f32(pw[j] - mx);
+  __syncwarp();
+  float inv = 0.0f;
+  if (lane == 0) {
+    float sum = 0.0f;
+    for (int j = 0; j < len; ++j) sum = sum + pw[j];
+    inv = 1.0f / sum;
+  }
+  inv = __shfl_sync(0xffffffffu, inv, 0);
+  for (int j = lane; j < len; j += 32) pw[j] = pw[j] * inv;
+  __syncwarp();
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const int nd = (hd + 31) / 32;
+  for (int j = 0; j < len; ++j) {
+    const float p = pw[j];
+    const float* vr = v_pool + (size_t)rows_s[j] * d + h * hd;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = lane + 32 * u;
+      if (u < nd && i < hd) acc[u] = acc[u] + vr[i] * p;
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int i = lane + 32 * u;
+    if (u < nd && i < hd) out_q[(size_t)r * d + h * hd + i] = quantize_one(acc[u], alpha, status);
+  }
+}
+
+// ---- token selection ----------------------------------------------------------
+__global__ void finalize_kernel(int rows, const int32_t* __restrict__ row_slot,
+                                unsigned long long* __restrict__ best, int32_t* slot_prev,
+                                int32_t* slot_step, const int32_t* __restrict__ slot_limit,
+                                int32_t* step_tokens, uint8_t* done, uint32_t* status) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const int slot = row_slot[r];
+  const unsigned long long key = best[r];
+  best[r] = 0ull;
+  int token = 0;
+  if (key == 0ull) {
+    flag_status(status, kStatusBadIndex);  // no candidate scored
+  } else {
+    token = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
+  }
+  const int t = slot_step[slot];
+  slot_step[slot] = t + 1;
+  slot_prev[slot] = token;
+  step_tokens[r] = token;
+  done[r] = (token == 0 || t + 1 >= slot_limit[slot]) ? 1 : 0;
+}
+
+__global__ void init_slots_kernel(int n, const int32_t* slots, const int32_t* limits,
+                                  const int32_t* force, const int32_t* src_len, int32_t* slot_prev,
+                                  int32_t* slot_step, int32_t* slot_limit, int32_t* slot_force,
+                                  int32_t* slot_src, float* ssru_state, int layers, int max_slots,
+                                  int d) {
+  const int i = blockIdx.x;
+  if (i >= n) return;
+  const int s = slots[i];
+  if (threadIdx.x == 0) {
+    slot_prev[s] = -1;
+    slot_step[s] = 0;
+    slot_limit[s] = limits[i];
+    slot_force[s] = force[i];
+    slot_src[s] = src_len[i];
+  }
+  if (ssru_state)
+    for (int l = 0; l < layers; ++l)
+      for (int k = threadIdx.x; k < d; k += blockDim.x)
+        ssru_state[((size_t)l * max_slots + s) * d + k] = 0.0f;
+}
+
+inline unsigned blocks_for(long long n, int threads) {
+  return static_cast<unsigned>((n + threads - 1) / threads);
+}
+
+}  // namespace
+
+void launch_embed_encoder(const int32_t* tokens, const int32_t* pos_idx, int n_tokens,
+                          const int8_t* emb, float emb_mult, float emb_scale,
+                          const float* positions, int d, float* x, const QuantOut& q,
+                          uint32_t* status, cudaStream_t s) {
+  if (n_tokens <= 0) return;
+  const long long n = (long long)n_tokens * (d / 4);
+  embed_encoder_kernel<<<blocks_for(n, 256), 256, 0, s>>>(tokens, pos_idx, n_tokens, emb, emb_mult,
+                                                          emb_scale, positions, d, x, q, status);
+}
+
+void launch_embed_decoder(int rows, const int32_t* row_slot, const int32_t* slot_prev,
+                          const int32_t* slot_step, const int32_t* slot_force, const int8_t* emb,
+                          float emb_mult, float emb_scale, const float* positions, int d, float* x,
+                          const QuantOut& q, uint8_t* eos_mask, const int32_t* self_pages,
+                          int pages_per_slot, int page_tokens, int32_t* self_row_map,
+                          uint32_t* status, cudaStream_t s) {
+  if (rows <= 0) return;
+  const long long n = (long long)rows * (d / 4);
+  embed_decoder_kernel<<<blocks_for(n, 256), 256, 0, s>>>(
+      rows, row_slot, slot_prev, slot_step, slot_force, emb, emb_mult, emb_scale, positions, d, x,
+      q, eos_mask, self_pages, pages_per_slot, page_tokens, self_row_map, status);
+}
+
+void launch_residual_ln(const float* a, int lda, const float* r, int ldr, const float* gamma,
+                        const float* beta, int rows, int d, float* out, const QuantOut& q,
+                        uint32_t* status, cudaStream_t s) {
+  if (rows <= 0) return;
+  residual_ln_kernel<<<blocks_for(rows, 32), 32, 0, s>>>(a, lda, r, ldr, gamma, beta, rows, d, out, q,
+                                                         status);
+}
+
+void launch_ssru(const float* cf, int ld, int fcol, float* state, const int32_t* row_slot,
+                 const float* residual, const float* gamma, const float* beta, int rows, int d,
+                 float* out, const QuantOut& q, uint32_t* status, cudaStream_t s) {
+  if (rows <= 0) return;
+  ssru_kernel<<<blocks_for(rows, 32), 32, 0, s>>>(cf, ld, fcol, state, row_slot, residual, gamma, beta,
+                                                  rows, d, out, q, status);
+}
+
+cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens, int batch,
+                                int max_len, int d, int heads, int8_t* out_q, float alpha,
+                                uint32_t* status, cudaStream_t s) {
+  if (batch <= 0) return cudaSuccess;
+  const int hd = d / heads;
+  const size_t smem = sizeof(float) * ((size_t)max_len * (hd + 1) + (size_t)max_len * hd +
+                                       kEncWarps * hd + kEncWarps * (size_t)max_len);
+  cudaError_t e = cudaFuncSetAttribute(attn_encoder_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  attn_encoder_kernel<<<dim3(batch, heads), kEncWarps * 32, smem, s>>>(qkv, cu_seqlens, d, heads,
+                                                                       max_len, out_q, alpha, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t* row_slot,
+                               const int32_t* slot_len, int len_add, const int32_t* page_table,
+                               int pages_per_slot, int page_tokens, const float* k_pool,
+                               const float* v_pool, int d, int heads, int8_t* out_q, float alpha,
+                               uint32_t* status, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  const int hd = d / heads;
+  const size_t smem = sizeof(float) * ((size_t)heads * hd + (size_t)heads * kMaxSeq + kMaxSeq);
+  attn_decode_kernel<<<rows, heads * 32, smem, s>>>(q, ldq, row_slot, slot_len, len_add, page_table,
+                                                    pages_per_slot, page_tokens, k_pool, v_pool, d,
+                                                    heads, out_q, alpha, status);
+  return cudaGetLastError();
+}
+
+void launch_finalize(int rows, const int32_t* row_slot, unsigned long long* best,
+                     int32_t* slot_prev, int32_t* slot_step, const int32_t* slot_limit,
+                     int32_t* step_tokens, uint8_t* done, uint32_t* status, cudaStream_t s) {
+  if (rows <= 0) return;
+  finalize_kernel<<<blocks_for(rows, 128), 128, 0, s>>>(rows, row_slot, best, slot_prev, slot_step,
+                                                        slot_limit, step_tokens, done, status);
+}
+
+void launch_init_slots(int n, const int32_t* slots, const int32_t* limits, const int32_t* force,
+                       const int32_t* src_len, int32_t* slot_prev, int32_t* slot_step,
+                       int32_t* slot_limit, int32_t* slot_force, int32_t* slot_src,
+                       float* ssru_state, int layers, int max_slots, int d, cudaStream_t s) {
+  if (n <= 0) return;
+  init_slots_kernel<<<n, 128, 0, s>>>(n, slots, limits, force, src_len, slot_prev, slot_step,
+                                      slot_limit, slot_force, slot_src, ssru_state, layers,
+                                      max_slots, d);
+}
+
+}  // namespace mc

@@ -1,0 +1,87 @@
+// kernels.cuh -- launchers for the non-GEMM kernels of the Q8 greedy path.
+//
+// Floating-point kernels are compiled with --fmad=false so every a*b+c keeps
+// two roundings, as the reference's Rust does; reductions whose order the
+// reference fixes (LayerNorm sums, attention dot products, softmax sums,
+// attention output accumulation) are evaluated in that same sequential order
+// by one thread each.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mc {
+
+constexpr int kMaxQuantOut = 8;
+constexpr int kMaxPosition = 4096;   // marian-model/src/manifest.rs:13
+constexpr int kMaxSeq = 256;         // source tokens and generation steps
+
+// Quantized copies of one f32 activation, one per consuming linear (each
+// linear has its own static activation alpha).  Copy i lives at
+// base + i * stride (int8, centred).
+struct QuantOut {
+  int8_t* base;
+  long long stride;
+  int count;
+  float alpha[kMaxQuantOut];
+};
+
+// q8_engine.rs:586-603: x = (emb[tok] / qm) * scale + pos[p] for packed tokens.
+void launch_embed_encoder(const int32_t* tokens, const int32_t* pos_idx, int n_tokens,
+                          const int8_t* emb, float emb_mult, float emb_scale,
+                          const float* positions, int d, float* x, const QuantOut& q,
+                          uint32_t* status, cudaStream_t s);
+
+// q8_engine.rs:605-630 for one decode step of the active rows.  Also writes
+// the per-row EOS mask (harness rule) and the self-attention cache row of
+// this step (when self_pages != nullptr).
+void launch_embed_decoder(int rows, const int32_t* row_slot, const int32_t* slot_prev,
+                          const int32_t* slot_step, const int32_t* slot_force, const int8_t* emb,
+                          float emb_mult, float emb_scale, const float* positions, int d, float* x,
+                          const QuantOut& q, uint8_t* eos_mask, const int32_t* self_pages,
+                          int pages_per_slot, int page_tokens, int32_t* self_row_map,
+                          uint32_t* status, cudaStream_t s);
+
+// tensor.rs:132-155: out = LN(a + r) (eps 1e-6) plus quantized copies.
+void launch_residual_ln(const float* a, int lda, const float* r, int ldr, const float* gamma,
+                        const float* beta, int rows, int d, float* out, const QuantOut& q,
+                        uint32_t* status, cudaStream_t s);
+
+// tensor.rs:184-218: SSRU gate/state update, ReLU + residual, LN, quantized
+// copies.  cand/fpre are [rows, ld] with the candidate at column 0 and the
+// forget pre-activation at column fcol; state is [slots, d] indexed by slot.
+void launch_ssru(const float* cf, int ld, int fcol, float* state, const int32_t* row_slot,
+                 const float* residual, const float* gamma, const float* beta, int rows, int d,
+                 float* out, const QuantOut& q, uint32_t* status, cudaStream_t s);
+
+// tensor.rs:251-318 for packed varlen sequences (no padding): qkv is
+// [tokens, 3d] (Q | K | V), cu_seqlens [batch+1].  Output quantized with
+// the output projection's alpha into out_q [tokens, d].
+cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens, int batch,
+                                int max_len, int d, int heads, int8_t* out_q, float alpha,
+                                uint32_t* status, cudaStream_t s);
+
+// tensor.rs:251-318 with one query per row over a paged cache: keys of row r
+// are cache rows page_table[slot][j / page_tokens] * page_tokens +
+// j % page_tokens for j < slot_len[slot] + len_add.
+cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t* row_slot,
+                               const int32_t* slot_len, int len_add, const int32_t* page_table,
+                               int pages_per_slot, int page_tokens, const float* k_pool,
+                               const float* v_pool, int d, int heads, int8_t* out_q, float alpha,
+                               uint32_t* status, cudaStream_t s);
+
+// Turns the packed per-row maxima into tokens (q8_engine.rs:437-449):
+// advances each slot's step/previous token, reports the token and whether
+// the row finished (token 0 or its limit), and clears the maxima.
+void launch_finalize(int rows, const int32_t* row_slot, unsigned long long* best,
+                     int32_t* slot_prev, int32_t* slot_step, const int32_t* slot_limit,
+                     int32_t* step_tokens, uint8_t* done, uint32_t* status, cudaStream_t s);
+
+// Initializes newly admitted slots: prev = -1, step = 0, limit, force_len,
+// source length, SSRU states zeroed (state pools [layers][slots][d]).
+void launch_init_slots(int n, const int32_t* slots, const int32_t* limits, const int32_t* force,
+                       const int32_t* src_len, int32_t* slot_prev, int32_t* slot_step,
+                       int32_t* slot_limit, int32_t* slot_force, int32_t* slot_src,
+                       float* ssru_state, int layers, int max_slots, int d, cudaStream_t s);
+
+}  // namespace mc

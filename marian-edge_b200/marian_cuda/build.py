@@ -23,7 +23,7 @@ LIB = os.path.join(PKG, "libmarian_cuda.so")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3", "-I", INCLUDE, "-I", CSRC,
+FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--fmad=false", "-Xcompiler", "-fPIC,-O3", "-I", INCLUDE, "-I", CSRC,
          "--expt-relaxed-constexpr"]
 
 
