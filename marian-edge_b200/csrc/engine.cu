@@ -38,6 +38,7 @@ struct DevLinear {
   float* bias = nullptr;       // [out] or null
   int in = 0, out = 0;
   float alpha = 1.0f;          // this linear's own activation alpha
+  float scale = 1.0f;          // 1 / (alpha * weight quant_mult)
   CUtensorMap tmap_b[3];       // W tensor maps for BN = 64, 128, 256
 };
 
@@ -108,6 +109,11 @@ struct mc_engine {
   QBuf enc_q[kMaxQuantOut];
   QBuf enc_o, enc_h;
   int32_t *enc_tokens = nullptr, *enc_pos = nullptr, *enc_cu = nullptr, *enc_cross_rows = nullptr;
+  int32_t* enc_seq_ids = nullptr;  // admitted sequences grouped by length bucket
+  struct Bucket {
+    int offset, count, max_len;
+  };
+  std::vector<Bucket> buckets;
 
   // decoder buffers (capacity rmax rows = slots)
   int rmax = 0;
@@ -274,6 +280,7 @@ mc_status upload_linear(mc_engine* e, const std::string& wname, const char* bnam
   CK(dalloc(e, &L->w, w.i8.size()));
   CK(cudaMemcpyAsync(L->w, w.i8.data(), w.i8.size(), cudaMemcpyHostToDevice, e->stream));
   const float inv = 1.0f / (L->alpha * w.quant_mult);  // q8_gemm.rs:438
+  L->scale = inv;
   std::vector<float> cs(L->out, inv);
   CK(dalloc(e, &L->col_scale, cs.size()));
   CK(cudaMemcpyAsync(L->col_scale, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, e->stream));
@@ -349,7 +356,8 @@ mc_status gemm(mc_engine* e, int kind, int m, const GroupSpec* specs, int n_grou
     GemmGroup& g = p.g[i];
     g.tmap_a = s.a->tmap;
     g.tmap_b = s.w->tmap_b[bn_index(bn)];
-    g.col_scale = s.w->col_scale;
+    g.col_scale = nullptr;  // per-tensor weight scale (q8_gemm.rs:438)
+    g.uniform_scale = s.w->scale;
     g.bias = s.w->bias;
     g.out = s.out;
     g.row_map = s.row_map;
@@ -442,9 +450,12 @@ mc_status run_encoder(mc_engine* e, int T, int batch, int max_len, double sum_le
         {&e->enc_q[1], &a.wk, kEpiF32, e->enc_qkv, 3 * d, d, nullptr, false, 0.f},
         {&e->enc_q[2], &a.wv, kEpiF32, e->enc_qkv, 3 * d, 2 * d, nullptr, false, 0.f}};
     if ((st = gemm(e, MC_K_GEMM_QKV, T, qkv, 3))) return st;
-    PROFILED(MC_K_ATTN_ENC, 4.0 * sum_len_sq * d, rows_d * (12 + 1),
-             CK(launch_attn_encoder(e->enc_qkv, e->enc_cu, batch, max_len, d, e->heads, e->enc_o.p,
-                                    a.wo.alpha, e->d_status, e->stream)));
+    PROFILED(MC_K_ATTN_ENC, 4.0 * sum_len_sq * d, rows_d * (12 + 1), {
+      for (const auto& bk : e->buckets)
+        CK(launch_attn_encoder(e->enc_qkv, e->enc_cu, e->enc_seq_ids + bk.offset, bk.count,
+                               bk.max_len, d, e->heads, e->enc_o.p, a.wo.alpha, e->d_status,
+                               e->stream));
+    });
     ++e->launches;
     GroupSpec wo = {&e->enc_o, &a.wo, kEpiF32, e->enc_proj, d, 0, nullptr, false, 0.f};
     if ((st = gemm(e, MC_K_GEMM_OUT, T, &wo, 1))) return st;
@@ -621,6 +632,7 @@ mc_status allocate_buffers(mc_engine* e) {
   CK(dalloc(e, &e->enc_pos, T));
   CK(dalloc(e, &e->enc_cu, T + 1));
   CK(dalloc(e, &e->enc_cross_rows, T));
+  CK(dalloc(e, &e->enc_seq_ids, R));
 
   CK(dalloc(e, &e->dec_a, (size_t)R * d));
   CK(dalloc(e, &e->dec_b, (size_t)R * d));
@@ -756,6 +768,14 @@ mc_status check_status(mc_engine* e) {
 mc_status admit(mc_engine* e, std::vector<Request*>* admitted) {
   int T = 0, max_len = 0;
   const int pt = e->page_tokens;
+  // Admission granularity: an encoder pass over a handful of sources costs
+  // nearly as much launch latency as one over hundreds, so wait until an
+  // eighth of the slots are free -- unless nothing is running or the whole
+  // queue fits (which keeps latency low under light load).
+  const size_t free_slots = e->free_slots.size();
+  if (!e->active.empty() && free_slots < (size_t)std::max(1, e->rmax / 8) &&
+      e->queue.size() > free_slots)
+    return MC_OK;
   while (!e->queue.empty() && !e->free_slots.empty()) {
     Request* r = e->queue.front();
     const int L = (int)r->tokens.size();
@@ -794,7 +814,7 @@ mc_status admit(mc_engine* e, std::vector<Request*>* admitted) {
   // staging: tokens[T] pos[T] rows[T] cu[B+1] slots[B] limits[B] force[B] src[B]
   int32_t* h = e->h_i32;
   int32_t *tok = h, *pos = h + T, *rows = h + 2 * T, *cu = h + 3 * T, *slots = cu + B + 1,
-          *lims = slots + B, *force = lims + B, *src = force + B;
+          *lims = slots + B, *force = lims + B, *src = force + B, *seq_ids = src + B;
   int t = 0;
   double sum_len_sq = 0;
   cu[0] = 0;
@@ -813,7 +833,21 @@ mc_status admit(mc_engine* e, std::vector<Request*>* admitted) {
     force[b] = (int32_t)r->force;
     src[b] = L;
   }
+  // length buckets for the encoder attention (shared memory follows length)
+  e->buckets.clear();
+  {
+    const int bounds[4] = {32, 64, 128, kMaxSeq};
+    int off = 0, lo = 0;
+    for (int hi : bounds) {
+      const int start = off;
+      for (int b = 0; b < B; ++b)
+        if (src[b] > lo && src[b] <= hi) seq_ids[off++] = b;
+      if (off > start) e->buckets.push_back({start, off - start, hi});
+      lo = hi;
+    }
+  }
   cudaStream_t s = e->stream;
+  CK(cudaMemcpyAsync(e->enc_seq_ids, seq_ids, B * 4, cudaMemcpyHostToDevice, s));
   CK(cudaMemcpyAsync(e->enc_tokens, tok, T * 4, cudaMemcpyHostToDevice, s));
   CK(cudaMemcpyAsync(e->enc_pos, pos, T * 4, cudaMemcpyHostToDevice, s));
   CK(cudaMemcpyAsync(e->enc_cross_rows, rows, T * 4, cudaMemcpyHostToDevice, s));
@@ -980,7 +1014,8 @@ extern "C" mc_status mc_load_marian_bin(mc_engine* e, const uint8_t* bytes, size
     v.in = d;
     v.out = e->vtgt;
     if (!(err = activation_scale(m, "decoder_Wemb", &v.alpha)).empty()) return fail(e, MC_MODEL, err);
-    std::vector<float> cs(e->vtgt, 1.0f / (v.alpha * e->dec_emb_mult));  // q8_engine.rs:772
+    v.scale = 1.0f / (v.alpha * e->dec_emb_mult);  // q8_engine.rs:772
+    std::vector<float> cs(e->vtgt, v.scale);
     CK(dalloc(e, &v.col_scale, cs.size()));
     CK(h2d(e, v.col_scale, cs.data(), cs.size() * 4));
     if ((st = upload_f32(e, "decoder_ff_logit_out_b", &v.bias))) return st;

@@ -101,128 +101,154 @@ __global__ void embed_decoder_kernel(int rows, const int32_t* __restrict__ row_s
   }
 }
 
-// ---- LayerNorm (normalize_row, tensor.rs:372-385), one thread per row --------
-// The row is first written as a + r (or the SSRU's ReLU + residual), summed
-// left to right, then centred squares are summed left to right, exactly as
-// the reference's Iterator::sum does.
-__device__ __forceinline__ void normalize_row_out(float* __restrict__ o, const float* __restrict__ gamma,
-                                                  const float* __restrict__ beta, int d, float sum,
-                                                  const QuantOut& q, long long qrow,
-                                                  uint32_t* status) {
-  const float fd = (float)d;
-  const float mean = sum / fd;
-  float var = 0.0f;
-  for (int i = 0; i < d; i += 4) {
-    const float4 v = *reinterpret_cast<const float4*>(o + i);
-    float c0 = v.x - mean, c1 = v.y - mean, c2 = v.z - mean, c3 = v.w - mean;
-    var = var + c0 * c0;
-    var = var + c1 * c1;
-    var = var + c2 * c2;
-    var = var + c3 * c3;
-  }
-  var = var / fd;
-  const float inv_std = 1.0f / sqrtf(var + kLnEps);
-  for (int i = 0; i < d; i += 4) {
-    float4 v = *reinterpret_cast<const float4*>(o + i);
-    const float4 g = *reinterpret_cast<const float4*>(gamma + i);
-    const float4 b = *reinterpret_cast<const float4*>(beta + i);
-    v.x = (v.x - mean) * inv_std * g.x + b.x;
-    v.y = (v.y - mean) * inv_std * g.y + b.y;
-    v.z = (v.z - mean) * inv_std * g.z + b.z;
-    v.w = (v.w - mean) * inv_std * g.w + b.w;
-    *reinterpret_cast<float4*>(o + i) = v;
-    store_quant4(q, qrow + i, v.x, v.y, v.z, v.w, status);
-  }
-}
+// ---- LayerNorm (normalize_row, tensor.rs:372-385) ------------------------------
+// kLnRows rows per CTA are staged in shared memory with coalesced loads (row
+// stride d + 1 so the per-row threads below hit distinct banks).  One thread
+// per row then sums the row left to right and sums the centred squares left
+// to right, exactly as the reference's Iterator::sum; the normalized rows and
+// their quantized copies are written back coalesced.
+constexpr int kLnRows = 32;
+constexpr int kLnThreads = 128;
 
-__global__ void residual_ln_kernel(const float* __restrict__ a, int lda, const float* __restrict__ r,
-                                   int ldr, const float* __restrict__ gamma,
-                                   const float* __restrict__ beta, int rows, int d,
-                                   float* __restrict__ out, QuantOut q, uint32_t* status) {
-  const int row = blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= rows) return;
-  const float* ar = a + (size_t)row * lda;
-  const float* rr = r + (size_t)row * ldr;
-  float* o = out + (size_t)row * d;
-  float sum = 0.0f;
-  for (int i = 0; i < d; i += 4) {
-    const float4 x = *reinterpret_cast<const float4*>(ar + i);
-    const float4 y = *reinterpret_cast<const float4*>(rr + i);
+__device__ __forceinline__ void ln_stats_and_store(float* tile, int nrows, int d, int row0,
+                                                   const float* __restrict__ gamma,
+                                                   const float* __restrict__ beta,
+                                                   float* __restrict__ out, const QuantOut& q,
+                                                   uint32_t* status) {
+  __shared__ float s_mean[kLnRows], s_inv[kLnRows];
+  const int ld = d + 1;
+  if (threadIdx.x < nrows) {
+    const float* row = tile + threadIdx.x * ld;
+    float sum = 0.0f;
+#pragma unroll 16
+    for (int i = 0; i < d; ++i) sum = sum + row[i];
+    const float fd = (float)d;
+    const float mean = sum / fd;
+    float var = 0.0f;
+#pragma unroll 16
+    for (int i = 0; i < d; ++i) {
+      const float c = row[i] - mean;
+      var = var + c * c;
+    }
+    var = var / fd;
+    s_mean[threadIdx.x] = mean;
+    s_inv[threadIdx.x] = 1.0f / sqrtf(var + kLnEps);
+  }
+  __syncthreads();
+  const int vec = d >> 2;
+  for (int idx = threadIdx.x; idx < nrows * vec; idx += blockDim.x) {
+    const int rr = idx / vec, c = (idx % vec) * 4;
+    const float* t = tile + rr * ld + c;
+    const float mean = s_mean[rr], inv = s_inv[rr];
+    const float4 g = *reinterpret_cast<const float4*>(gamma + c);
+    const float4 b = *reinterpret_cast<const float4*>(beta + c);
     float4 v;
-    v.x = x.x + y.x;
-    v.y = x.y + y.y;
-    v.z = x.z + y.z;
-    v.w = x.w + y.w;
-    *reinterpret_cast<float4*>(o + i) = v;
-    sum = sum + v.x;
-    sum = sum + v.y;
-    sum = sum + v.z;
-    sum = sum + v.w;
+    v.x = (t[0] - mean) * inv * g.x + b.x;
+    v.y = (t[1] - mean) * inv * g.y + b.y;
+    v.z = (t[2] - mean) * inv * g.z + b.z;
+    v.w = (t[3] - mean) * inv * g.w + b.w;
+    const long long elem = (long long)(row0 + rr) * d + c;
+    *reinterpret_cast<float4*>(out + elem) = v;
+    store_quant4(q, elem, v.x, v.y, v.z, v.w, status);
   }
-  normalize_row_out(o, gamma, beta, d, sum, q, (long long)row * d, status);
 }
 
-__global__ void ssru_kernel(const float* __restrict__ cf, int ld, int fcol, float* __restrict__ state,
-                            const int32_t* __restrict__ row_slot, const float* __restrict__ residual,
-                            const float* __restrict__ gamma, const float* __restrict__ beta,
-                            int rows, int d, float* __restrict__ out, QuantOut q,
-                            uint32_t* status) {
-  const int row = blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= rows) return;
-  const int slot = row_slot[row];
-  const float* cand = cf + (size_t)row * ld;
-  const float* fpre = cand + fcol;
-  float* st = state + (size_t)slot * d;
-  const float* res = residual + (size_t)row * d;
-  float* o = out + (size_t)row * d;
-  float sum = 0.0f;
-  for (int i = 0; i < d; ++i) {
-    const float gate = 1.0f / (1.0f + exp_f32(-fpre[i]));
-    const float next = gate * st[i] + (1.0f - gate) * cand[i];
-    st[i] = next;
-    const float v = fmaxf(next, 0.0f) + res[i];
-    o[i] = v;
-    sum = sum + v;
+__global__ void __launch_bounds__(kLnThreads) residual_ln_kernel(
+    const float* __restrict__ a, int lda, const float* __restrict__ r, int ldr,
+    const float* __restrict__ gamma, const float* __restrict__ beta, int rows, int d,
+    float* __restrict__ out, QuantOut q, uint32_t* status) {
+  extern __shared__ float tile[];  // [kLnRows][d + 1]
+  const int row0 = blockIdx.x * kLnRows;
+  const int nrows = min(kLnRows, rows - row0);
+  const int vec = d >> 2, ld = d + 1;
+  for (int idx = threadIdx.x; idx < nrows * vec; idx += blockDim.x) {
+    const int rr = idx / vec, c = (idx % vec) * 4;
+    const float4 x = *reinterpret_cast<const float4*>(a + (size_t)(row0 + rr) * lda + c);
+    const float4 y = *reinterpret_cast<const float4*>(r + (size_t)(row0 + rr) * ldr + c);
+    float* t = tile + rr * ld + c;
+    t[0] = x.x + y.x;
+    t[1] = x.y + y.y;
+    t[2] = x.z + y.z;
+    t[3] = x.w + y.w;
   }
-  normalize_row_out(o, gamma, beta, d, sum, q, (long long)row * d, status);
+  __syncthreads();
+  ln_stats_and_store(tile, nrows, d, row0, gamma, beta, out, q, status);
+}
+
+// tensor.rs:184-218: gate and state update per element (coalesced), then the
+// LayerNorm of ReLU(state) + residual as above.
+__global__ void __launch_bounds__(kLnThreads) ssru_kernel(
+    const float* __restrict__ cf, int ld_cf, int fcol, float* __restrict__ state,
+    const int32_t* __restrict__ row_slot, const float* __restrict__ residual,
+    const float* __restrict__ gamma, const float* __restrict__ beta, int rows, int d,
+    float* __restrict__ out, QuantOut q, uint32_t* status) {
+  extern __shared__ float tile[];
+  const int row0 = blockIdx.x * kLnRows;
+  const int nrows = min(kLnRows, rows - row0);
+  const int ld = d + 1;
+  for (int idx = threadIdx.x; idx < nrows * d; idx += blockDim.x) {
+    const int rr = idx / d, c = idx % d;
+    const int row = row0 + rr;
+    const float* cand = cf + (size_t)row * ld_cf;
+    const float gate = 1.0f / (1.0f + exp_f32(-cand[fcol + c]));
+    float* st = state + (size_t)row_slot[row] * d + c;
+    const float next = gate * st[0] + (1.0f - gate) * cand[c];
+    st[0] = next;
+    tile[rr * ld + c] = fmaxf(next, 0.0f) + residual[(size_t)row * d + c];
+  }
+  __syncthreads();
+  ln_stats_and_store(tile, nrows, d, row0, gamma, beta, out, q, status);
 }
 
 // ---- attention (attention_into, tensor.rs:251-318) ------------------------------
-// Encoder: one CTA per (sequence, head); K and V of that head are staged in
-// shared memory (K rows padded by one float so 32 lanes reading 32 different
-// keys hit 32 different banks); each warp takes one query at a time.
-constexpr int kEncWarps = 4;
+constexpr int kEncQueryChunk = 32;  // queries per CTA (grid.z splits long sequences)
 
+// Encoder: one CTA per (sequence, head, 32-query chunk); K and V of that head are staged in
+// shared memory (K rows padded by one float so 32 lanes reading 32 different
+// keys hit 32 different banks); each warp takes one query at a time.  The
+// host launches one grid per length bucket so shared memory (and therefore
+// occupancy) follows the bucket's longest sequence, not the batch's.
 __global__ void attn_encoder_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ cu,
-                                    int d, int heads, int max_len, int8_t* __restrict__ out_q,
-                                    float alpha, uint32_t* status) {
+                                    const int32_t* __restrict__ seq_ids, int d, int heads,
+                                    int max_len, int8_t* __restrict__ out_q, float alpha,
+                                    uint32_t* status) {
   extern __shared__ float sm[];
-  const int b = blockIdx.x;
+  const int b = seq_ids[blockIdx.x];
   const int h = blockIdx.y;
   const int hd = d / heads;
+  const int warps = blockDim.x >> 5;
   const int start = cu[b];
   const int len = cu[b + 1] - start;
   if (len <= 0 || len > max_len) {
     if (threadIdx.x == 0 && len > max_len) flag_status(status, kStatusBadIndex);
     return;
   }
+  if ((int)blockIdx.z * kEncQueryChunk >= len) return;  // no queries in this chunk
   const int ld = 3 * d;
   float* ks = sm;                                 // [max_len][hd + 1]
   float* vs = ks + (size_t)max_len * (hd + 1);     // [max_len][hd]
   float* qs = vs + (size_t)max_len * hd;          // [warps][hd]
-  float* ps = qs + kEncWarps * hd;                // [warps][max_len]
-  for (int idx = threadIdx.x; idx < len * hd; idx += blockDim.x) {
-    const int j = idx / hd, i = idx % hd;
+  float* ps = qs + warps * hd;                    // [warps][max_len]
+  const int vec = hd >> 2;
+  for (int idx = threadIdx.x; idx < len * vec; idx += blockDim.x) {
+    const int j = idx / vec, i = (idx % vec) * 4;
     const float* row = qkv + (size_t)(start + j) * ld + h * hd + i;
-    ks[j * (hd + 1) + i] = row[d];
-    vs[j * hd + i] = row[2 * d];
+    const float4 k4 = *reinterpret_cast<const float4*>(row + d);
+    const float4 v4 = *reinterpret_cast<const float4*>(row + 2 * d);
+    float* kd = ks + j * (hd + 1) + i;
+    kd[0] = k4.x;
+    kd[1] = k4.y;
+    kd[2] = k4.z;
+    kd[3] = k4.w;
+    *reinterpret_cast<float4*>(vs + j * hd + i) = v4;
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float scale = 1.0f / sqrtf((float)hd);
   float* qw = qs + warp * hd;
   float* pw = ps + warp * max_len;
-  for (int qi = warp; qi < len; qi += kEncWarps) {
+  const int q_end = min(len, (int)(blockIdx.z + 1) * kEncQueryChunk);
+  for (int qi = blockIdx.z * kEncQueryChunk + warp; qi < q_end; qi += warps) {
     const float* qrow = qkv + (size_t)(start + qi) * ld + h * hd;
     for (int i = lane; i < hd; i += 32) qw[i] = qrow[i];
     __syncwarp();
@@ -230,10 +256,11 @@ __global__ void attn_encoder_kernel(const float* __restrict__ qkv, const int32_t
     for (int j = lane; j < len; j += 32) {
       const float* kr = ks + j * (hd + 1);
       float dot = 0.0f;
+#pragma unroll 16
       for (int i = 0; i < hd; ++i) dot = dot + qw[i] * kr[i];
-      const float s = dot * scale;
-      pw[j] = s;
-      mx = fmaxf(mx, s);
+      const float sc = dot * scale;
+      pw[j] = sc;
+      mx = fmaxf(mx, sc);
     }
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     for (int j = lane; j < len; j += 32) pw[j] = exp_f32(pw[j] - mx);
@@ -241,16 +268,28 @@ __global__ void attn_encoder_kernel(const float* __restrict__ qkv, const int32_t
     float inv = 0.0f;
     if (lane == 0) {
       float sum = 0.0f;
+      #pragma unroll 8
       for (int j = 0; j < len; ++j) sum = sum + pw[j];
       inv = 1.0f / sum;
     }
     inv = __shfl_sync(0xffffffffu, inv, 0);
     for (int j = lane; j < len; j += 32) pw[j] = pw[j] * inv;
     __syncwarp();
-    for (int i = lane; i < hd; i += 32) {
-      float acc = 0.0f;
-      for (int j = 0; j < len; ++j) acc = acc + vs[j * hd + i] * pw[j];
-      out_q[(size_t)(start + qi) * d + h * hd + i] = quantize_one(acc, alpha, status);
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 4
+    for (int j = 0; j < len; ++j) {
+      const float p = pw[j];
+      const float* vr = vs + j * hd;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = lane + 32 * u;
+        if (i < hd) acc[u] = acc[u] + vr[i] * p;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = lane + 32 * u;
+      if (i < hd) out_q[(size_t)(start + qi) * d + h * hd + i] = quantize_one(acc[u], alpha, status);
     }
     __syncwarp();
   }
@@ -290,6 +329,7 @@ __global__ void attn_decode_kernel(const float* __restrict__ q, int ldq,
   for (int j = lane; j < len; j += 32) {
     const float* kr = k_pool + (size_t)rows_s[j] * d + h * hd;
     float dot = 0.0f;
+#pragma unroll 16
     for (int i = 0; i < hd; i += 4) {
       const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
       dot = dot + qw[i] * k4.x;
@@ -307,6 +347,7 @@ __global__ void attn_decode_kernel(const float* __restrict__ q, int ldq,
   float inv = 0.0f;
   if (lane == 0) {
     float sum = 0.0f;
+    #pragma unroll 8
     for (int j = 0; j < len; ++j) sum = sum + pw[j];
     inv = 1.0f / sum;
   }
@@ -315,6 +356,7 @@ __global__ void attn_decode_kernel(const float* __restrict__ q, int ldq,
   __syncwarp();
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   const int nd = (hd + 31) / 32;
+#pragma unroll 4
   for (int j = 0; j < len; ++j) {
     const float p = pw[j];
     const float* vr = v_pool + (size_t)rows_s[j] * d + h * hd;
@@ -408,30 +450,41 @@ void launch_residual_ln(const float* a, int lda, const float* r, int ldr, const 
                         const float* beta, int rows, int d, float* out, const QuantOut& q,
                         uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return;
-  residual_ln_kernel<<<blocks_for(rows, 32), 32, 0, s>>>(a, lda, r, ldr, gamma, beta, rows, d, out, q,
-                                                         status);
+  const size_t smem = sizeof(float) * kLnRows * (d + 1);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(residual_ln_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  residual_ln_kernel<<<blocks_for(rows, kLnRows), kLnThreads, smem, s>>>(a, lda, r, ldr, gamma, beta,
+                                                                         rows, d, out, q, status);
 }
 
 void launch_ssru(const float* cf, int ld, int fcol, float* state, const int32_t* row_slot,
                  const float* residual, const float* gamma, const float* beta, int rows, int d,
                  float* out, const QuantOut& q, uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return;
-  ssru_kernel<<<blocks_for(rows, 32), 32, 0, s>>>(cf, ld, fcol, state, row_slot, residual, gamma, beta,
-                                                  rows, d, out, q, status);
+  const size_t smem = sizeof(float) * kLnRows * (d + 1);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(ssru_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  ssru_kernel<<<blocks_for(rows, kLnRows), kLnThreads, smem, s>>>(cf, ld, fcol, state, row_slot, residual,
+                                                                  gamma, beta, rows, d, out, q, status);
 }
 
-cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens, int batch,
-                                int max_len, int d, int heads, int8_t* out_q, float alpha,
-                                uint32_t* status, cudaStream_t s) {
-  if (batch <= 0) return cudaSuccess;
+cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens,
+                                const int32_t* seq_ids, int n_seqs, int max_len, int d, int heads,
+                                int8_t* out_q, float alpha, uint32_t* status, cudaStream_t s) {
+  if (n_seqs <= 0) return cudaSuccess;
   const int hd = d / heads;
+  const int warps = max_len <= 32 ? 2 : 4;
   const size_t smem = sizeof(float) * ((size_t)max_len * (hd + 1) + (size_t)max_len * hd +
-                                       kEncWarps * hd + kEncWarps * (size_t)max_len);
-  cudaError_t e = cudaFuncSetAttribute(attn_encoder_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
-  attn_encoder_kernel<<<dim3(batch, heads), kEncWarps * 32, smem, s>>>(qkv, cu_seqlens, d, heads,
-                                                                       max_len, out_q, alpha, status);
+                                       (size_t)warps * hd + (size_t)warps * max_len);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(attn_encoder_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  const int chunks = (max_len + kEncQueryChunk - 1) / kEncQueryChunk;
+  attn_encoder_kernel<<<dim3(n_seqs, heads, chunks), warps * 32, smem, s>>>(qkv, cu_seqlens, seq_ids, d, heads,
+                                                                    max_len, out_q, alpha, status);
   return cudaGetLastError();
 }
 

@@ -55,11 +55,12 @@ void launch_ssru(const float* cf, int ld, int fcol, float* state, const int32_t*
                  float* out, const QuantOut& q, uint32_t* status, cudaStream_t s);
 
 // tensor.rs:251-318 for packed varlen sequences (no padding): qkv is
-// [tokens, 3d] (Q | K | V), cu_seqlens [batch+1].  Output quantized with
-// the output projection's alpha into out_q [tokens, d].
-cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens, int batch,
-                                int max_len, int d, int heads, int8_t* out_q, float alpha,
-                                uint32_t* status, cudaStream_t s);
+// [tokens, 3d] (Q | K | V), cu_seqlens [batch+1]; this launch covers the
+// n_seqs sequences listed in seq_ids, none longer than max_len.  Output
+// quantized with the output projection's alpha into out_q [tokens, d].
+cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens,
+                                const int32_t* seq_ids, int n_seqs, int max_len, int d, int heads,
+                                int8_t* out_q, float alpha, uint32_t* status, cudaStream_t s);
 
 // tensor.rs:251-318 with one query per row over a paged cache: keys of row r
 // are cache rows page_table[slot][j / page_tokens] * page_tokens +

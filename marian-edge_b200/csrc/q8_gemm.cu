@@ -27,7 +27,8 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 128;  // bytes of K per stage (= int8 elements)
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, each half the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 __device__ __forceinline__ unsigned long long pack_argmax(float v, int32_t n) {
   v = v + 0.0f;  // -0 -> +0: equal logits must compare equal (strict '>')
@@ -50,14 +51,16 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
   }
   if (g.mode == kEpiArgmax) {
     const bool mask_eos = g.eos_mask != nullptr && g.eos_mask[row] != 0;
+    uint32_t cand = g.cand_bits[nb >> 5];  // nb is a multiple of 32
+    if (nb == 0 && mask_eos) cand &= ~1u;
+    const float uscale = g.row_scale ? __fmul_rn(row_scale, g.uniform_scale) : g.uniform_scale;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int n = nb + j;
       if (n >= n_end) break;
-      if (!((g.cand_bits[n >> 5] >> (n & 31)) & 1u)) continue;
-      if (n == 0 && mask_eos) continue;
-      float scale = g.col_scale[n];
-      if (g.row_scale) scale = __fmul_rn(row_scale, scale);
+      if (!((cand >> j) & 1u)) continue;
+      float scale = uscale;
+      if (g.col_scale) scale = g.row_scale ? __fmul_rn(row_scale, g.col_scale[n]) : g.col_scale[n];
       const float logit = dequant(static_cast<int32_t>(r[j]), scale, g.bias ? g.bias[n] : 0.0f);
       if (logit > best) {  // strict: the lowest index wins ties
         best = logit;
@@ -71,7 +74,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
   for (int j = 0; j < 32; ++j) {
     const int n = nb + j;
     if (n < n_end) {
-      float scale = g.col_scale[n];
+      float scale = g.col_scale ? g.col_scale[n] : g.uniform_scale;
       if (g.row_scale) scale = __fmul_rn(row_scale, scale);
       float x = dequant(static_cast<int32_t>(r[j]), scale, g.bias ? g.bias[n] : 0.0f);
       if (g.relu) x = fmaxf(x, 0.0f);
@@ -182,8 +185,10 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
       mma_commit(&accum_bar);
     }
   } else {
-    // Epilogue warps 2..5 cover TMEM lane quarters (warp % 4).
+    // Epilogue warps 2..9: warp % 4 selects the TMEM lane quarter (rows),
+    // (warp - 2) / 4 the half of the tile's columns.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     const int row = m0 + row_in_tile;
     const bool row_ok = row < p.m;
@@ -196,8 +201,9 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
       float best = -INFINITY;
       int best_n = -1;
       const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+      constexpr int kHalf = BN / 2 >= 32 ? BN / 2 : 32;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = half * kHalf; c0 < BN && c0 < (half + 1) * kHalf; c0 += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(lane_base + c0, r);
         tmem_ld_wait();

@@ -24,7 +24,8 @@ enum GemmMode : int32_t {
 struct alignas(64) GemmGroup {
   CUtensorMap tmap_a;          // A [rows, K] int8, box {128, 128}, 128-byte swizzle
   CUtensorMap tmap_b;          // W [N, K] int8, box {128, BN}, 128-byte swizzle
-  const float* col_scale;      // [N]: 1/(alpha_a * w_mult) per output column
+  const float* col_scale;      // [N]: 1/(alpha_a * w_mult) per output column, or null
+                               // to use uniform_scale for every column
   const float* row_scale;      // [M] or null: extra per-row factor (microbench)
   const float* bias;           // [N] or null
   const float* residual;       // [M, ldr] or null (kEpiF32)
@@ -40,7 +41,7 @@ struct alignas(64) GemmGroup {
   float alpha;                 // next linear's activation alpha (kEpiQ8)
   int32_t mode;
   int32_t relu;
-  int32_t pad_;
+  float uniform_scale;         // used when col_scale is null (per-tensor scale)
 };
 
 constexpr int kMaxGemmGroups = 3;
