@@ -107,8 +107,8 @@ __global__ void embed_decoder_kernel(int rows, const int32_t* __restrict__ row_s
 // per row then sums the row left to right and sums the centred squares left
 // to right, exactly as the reference's Iterator::sum; the normalized rows and
 // their quantized copies are written back coalesced.
-constexpr int kLnRows = 32;
-constexpr int kLnThreads = 128;
+constexpr int kLnRows = 8;
+constexpr int kLnThreads = 256;
 
 __device__ __forceinline__ void ln_stats_and_store(float* tile, int nrows, int d, int row0,
                                                    const float* __restrict__ gamma,
@@ -136,6 +136,7 @@ __device__ __forceinline__ void ln_stats_and_store(float* tile, int nrows, int d
   }
   __syncthreads();
   const int vec = d >> 2;
+#pragma unroll 4
   for (int idx = threadIdx.x; idx < nrows * vec; idx += blockDim.x) {
     const int rr = idx / vec, c = (idx % vec) * 4;
     const float* t = tile + rr * ld + c;
@@ -161,6 +162,7 @@ __global__ void __launch_bounds__(kLnThreads) residual_ln_kernel(
   const int row0 = blockIdx.x * kLnRows;
   const int nrows = min(kLnRows, rows - row0);
   const int vec = d >> 2, ld = d + 1;
+#pragma unroll 4
   for (int idx = threadIdx.x; idx < nrows * vec; idx += blockDim.x) {
     const int rr = idx / vec, c = (idx % vec) * 4;
     const float4 x = *reinterpret_cast<const float4*>(a + (size_t)(row0 + rr) * lda + c);
@@ -186,6 +188,7 @@ __global__ void __launch_bounds__(kLnThreads) ssru_kernel(
   const int row0 = blockIdx.x * kLnRows;
   const int nrows = min(kLnRows, rows - row0);
   const int ld = d + 1;
+#pragma unroll 4
   for (int idx = threadIdx.x; idx < nrows * d; idx += blockDim.x) {
     const int rr = idx / d, c = idx % d;
     const int row = row0 + rr;
@@ -201,63 +204,66 @@ __global__ void __launch_bounds__(kLnThreads) ssru_kernel(
 }
 
 // ---- attention (attention_into, tensor.rs:251-318) ------------------------------
-constexpr int kEncQueryChunk = 32;  // queries per CTA (grid.z splits long sequences)
+// Encoder: one CTA of 8 warps per (sequence, head, 32-query chunk).  K and V
+// of the head are staged in shared memory (K rows padded to HD + 1 floats so
+// the 32 lanes, each scoring a different key, hit different banks).  A warp
+// takes one query at a time: lanes score keys with in-order dot products,
+// lane 0 sums the exponentials in key order, and each lane accumulates two
+// output dimensions over the keys in order -- the reference's operation
+// order throughout.  The host launches one grid per length bucket so shared
+// memory follows the bucket's longest sequence.
+constexpr int kEncWarps = 8;
 
-// Encoder: one CTA per (sequence, head, 32-query chunk); K and V of that head are staged in
-// shared memory (K rows padded by one float so 32 lanes reading 32 different
-// keys hit 32 different banks); each warp takes one query at a time.  The
-// host launches one grid per length bucket so shared memory (and therefore
-// occupancy) follows the bucket's longest sequence, not the batch's.
-__global__ void attn_encoder_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ cu,
-                                    const int32_t* __restrict__ seq_ids, int d, int heads,
-                                    int max_len, int8_t* __restrict__ out_q, float alpha,
-                                    uint32_t* status) {
+template <int HD>
+__global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
+    const float* __restrict__ qkv, const int32_t* __restrict__ cu,
+    const int32_t* __restrict__ seq_ids, int d, int max_len, int8_t* __restrict__ out_q,
+    float alpha, uint32_t* status) {
   extern __shared__ float sm[];
   const int b = seq_ids[blockIdx.x];
   const int h = blockIdx.y;
-  const int hd = d / heads;
-  const int warps = blockDim.x >> 5;
   const int start = cu[b];
   const int len = cu[b + 1] - start;
   if (len <= 0 || len > max_len) {
     if (threadIdx.x == 0 && len > max_len) flag_status(status, kStatusBadIndex);
     return;
   }
-  if ((int)blockIdx.z * kEncQueryChunk >= len) return;  // no queries in this chunk
+  const int q0 = blockIdx.z * 32;
+  if (q0 >= len) return;
   const int ld = 3 * d;
-  float* ks = sm;                                 // [max_len][hd + 1]
-  float* vs = ks + (size_t)max_len * (hd + 1);     // [max_len][hd]
-  float* qs = vs + (size_t)max_len * hd;          // [warps][hd]
-  float* ps = qs + warps * hd;                    // [warps][max_len]
-  const int vec = hd >> 2;
-  for (int idx = threadIdx.x; idx < len * vec; idx += blockDim.x) {
-    const int j = idx / vec, i = (idx % vec) * 4;
-    const float* row = qkv + (size_t)(start + j) * ld + h * hd + i;
+  constexpr int KLD = HD + 1;
+  float* ks = sm;                                 // [max_len][HD + 1]
+  float* vs = ks + (size_t)max_len * KLD;          // [max_len][HD]
+  float* qs = vs + (size_t)max_len * HD;          // [warps][HD]
+  float* ps = qs + kEncWarps * HD;                // [warps][max_len]
+  constexpr int kVec = HD / 4;
+  for (int idx = threadIdx.x; idx < len * kVec; idx += blockDim.x) {
+    const int j = idx / kVec, i = (idx % kVec) * 4;
+    const float* row = qkv + (size_t)(start + j) * ld + h * HD + i;
     const float4 k4 = *reinterpret_cast<const float4*>(row + d);
-    const float4 v4 = *reinterpret_cast<const float4*>(row + 2 * d);
-    float* kd = ks + j * (hd + 1) + i;
+    float* kd = ks + j * KLD + i;
     kd[0] = k4.x;
     kd[1] = k4.y;
     kd[2] = k4.z;
     kd[3] = k4.w;
-    *reinterpret_cast<float4*>(vs + j * hd + i) = v4;
+    *reinterpret_cast<float4*>(vs + j * HD + i) = *reinterpret_cast<const float4*>(row + 2 * d);
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float scale = 1.0f / sqrtf((float)hd);
-  float* qw = qs + warp * hd;
+  const float scale = 1.0f / sqrtf((float)HD);
+  float* qw = qs + warp * HD;
   float* pw = ps + warp * max_len;
-  const int q_end = min(len, (int)(blockIdx.z + 1) * kEncQueryChunk);
-  for (int qi = blockIdx.z * kEncQueryChunk + warp; qi < q_end; qi += warps) {
-    const float* qrow = qkv + (size_t)(start + qi) * ld + h * hd;
-    for (int i = lane; i < hd; i += 32) qw[i] = qrow[i];
+  const int q_end = min(len, q0 + 32);
+  for (int qi = q0 + warp; qi < q_end; qi += kEncWarps) {
+    const float* qrow = qkv + (size_t)(start + qi) * ld + h * HD;
+    for (int i = lane; i < HD; i += 32) qw[i] = qrow[i];
     __syncwarp();
     float mx = -INFINITY;
     for (int j = lane; j < len; j += 32) {
-      const float* kr = ks + j * (hd + 1);
+      const float* kr = ks + j * KLD;
       float dot = 0.0f;
-#pragma unroll 16
-      for (int i = 0; i < hd; ++i) dot = dot + qw[i] * kr[i];
+#pragma unroll
+      for (int i = 0; i < HD; ++i) dot = dot + qw[i] * kr[i];
       const float sc = dot * scale;
       pw[j] = sc;
       mx = fmaxf(mx, sc);
@@ -268,29 +274,25 @@ __global__ void attn_encoder_kernel(const float* __restrict__ qkv, const int32_t
     float inv = 0.0f;
     if (lane == 0) {
       float sum = 0.0f;
-      #pragma unroll 8
+#pragma unroll 8
       for (int j = 0; j < len; ++j) sum = sum + pw[j];
       inv = 1.0f / sum;
     }
     inv = __shfl_sync(0xffffffffu, inv, 0);
     for (int j = lane; j < len; j += 32) pw[j] = pw[j] * inv;
     __syncwarp();
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 4
+    const bool has1 = lane + 32 < HD;
+    float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll 8
     for (int j = 0; j < len; ++j) {
       const float p = pw[j];
-      const float* vr = vs + j * hd;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = lane + 32 * u;
-        if (i < hd) acc[u] = acc[u] + vr[i] * p;
-      }
+      const float* vr = vs + j * HD + lane;
+      acc0 = acc0 + vr[0] * p;
+      if (has1) acc1 = acc1 + vr[32] * p;
     }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = lane + 32 * u;
-      if (i < hd) out_q[(size_t)(start + qi) * d + h * hd + i] = quantize_one(acc[u], alpha, status);
-    }
+    int8_t* o = out_q + (size_t)(start + qi) * d + h * HD + lane;
+    o[0] = quantize_one(acc0, alpha, status);
+    if (has1) o[32] = quantize_one(acc1, alpha, status);
     __syncwarp();
   }
 }
@@ -326,6 +328,7 @@ __global__ void attn_decode_kernel(const float* __restrict__ q, int ldq,
   __syncthreads();
   const float scale = 1.0f / sqrtf((float)hd);
   float mx = -INFINITY;
+#pragma unroll 2
   for (int j = lane; j < len; j += 32) {
     const float* kr = k_pool + (size_t)rows_s[j] * d + h * hd;
     float dot = 0.0f;
@@ -354,23 +357,36 @@ __global__ void attn_decode_kernel(const float* __restrict__ q, int ldq,
   inv = __shfl_sync(0xffffffffu, inv, 0);
   for (int j = lane; j < len; j += 32) pw[j] = pw[j] * inv;
   __syncwarp();
-  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  const int nd = (hd + 31) / 32;
-#pragma unroll 4
-  for (int j = 0; j < len; ++j) {
-    const float p = pw[j];
-    const float* vr = v_pool + (size_t)rows_s[j] * d + h * hd;
+  // Each lane owns output dims lane and lane + 32 (head width <= 64).  V
+  // values of 16 keys are fetched into registers before the 16 in-order
+  // accumulations, so 32 loads per lane are in flight instead of one.
+  const bool has1 = lane + 32 < hd;
+  const float* vbase = v_pool + h * hd + lane;
+  float acc0 = 0.0f, acc1 = 0.0f;
+  int j = 0;
+  for (; j + 16 <= len; j += 16) {
+    float v0[16], v1[16];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = lane + 32 * u;
-      if (u < nd && i < hd) acc[u] = acc[u] + vr[i] * p;
+    for (int u = 0; u < 16; ++u) {
+      const float* vr = vbase + (size_t)rows_s[j + u] * d;
+      v0[u] = vr[0];
+      v1[u] = has1 ? vr[32] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const float p = pw[j + u];
+      acc0 = acc0 + v0[u] * p;
+      acc1 = acc1 + v1[u] * p;
     }
   }
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int i = lane + 32 * u;
-    if (u < nd && i < hd) out_q[(size_t)r * d + h * hd + i] = quantize_one(acc[u], alpha, status);
+  for (; j < len; ++j) {
+    const float* vr = vbase + (size_t)rows_s[j] * d;
+    const float p = pw[j];
+    acc0 = acc0 + vr[0] * p;
+    if (has1) acc1 = acc1 + vr[32] * p;
   }
+  out_q[(size_t)r * d + h * hd + lane] = quantize_one(acc0, alpha, status);
+  if (has1) out_q[(size_t)r * d + h * hd + lane + 32] = quantize_one(acc1, alpha, status);
 }
 
 // ---- token selection ----------------------------------------------------------
@@ -468,24 +484,35 @@ void launch_ssru(const float* cf, int ld, int fcol, float* state, const int32_t*
                                                                   gamma, beta, rows, d, out, q, status);
 }
 
-cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens,
-                                const int32_t* seq_ids, int n_seqs, int max_len, int d, int heads,
-                                int8_t* out_q, float alpha, uint32_t* status, cudaStream_t s) {
-  if (n_seqs <= 0) return cudaSuccess;
-  const int hd = d / heads;
-  const int warps = max_len <= 32 ? 2 : 4;
-  const size_t smem = sizeof(float) * ((size_t)max_len * (hd + 1) + (size_t)max_len * hd +
-                                       (size_t)warps * hd + (size_t)warps * max_len);
+template <int HD>
+cudaError_t launch_attn_encoder_hd(const float* qkv, const int32_t* cu_seqlens,
+                                   const int32_t* seq_ids, int n_seqs, int max_len, int d,
+                                   int heads, int8_t* out_q, float alpha, uint32_t* status,
+                                   cudaStream_t s) {
+  const size_t smem = sizeof(float) * ((size_t)max_len * (2 * HD + 1) + kEncWarps * (size_t)HD +
+                                       kEncWarps * (size_t)max_len);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(attn_encoder_kernel,
+    cudaError_t e = cudaFuncSetAttribute(attn_encoder_kernel<HD>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  const int chunks = (max_len + kEncQueryChunk - 1) / kEncQueryChunk;
-  attn_encoder_kernel<<<dim3(n_seqs, heads, chunks), warps * 32, smem, s>>>(qkv, cu_seqlens, seq_ids, d, heads,
-                                                                    max_len, out_q, alpha, status);
+  const int chunks = (max_len + 31) / 32;
+  attn_encoder_kernel<HD><<<dim3(n_seqs, heads, chunks), kEncWarps * 32, smem, s>>>(qkv, cu_seqlens, seq_ids, d,
+                                                                        max_len, out_q, alpha, status);
   return cudaGetLastError();
+}
+
+cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens,
+                                const int32_t* seq_ids, int n_seqs, int max_len, int d, int heads,
+                                int8_t* out_q, float alpha, uint32_t* status, cudaStream_t s) {
+  if (n_seqs <= 0) return cudaSuccess;
+  switch (d / heads) {
+    case 32: return launch_attn_encoder_hd<32>(qkv, cu_seqlens, seq_ids, n_seqs, max_len, d, heads, out_q, alpha, status, s);
+    case 48: return launch_attn_encoder_hd<48>(qkv, cu_seqlens, seq_ids, n_seqs, max_len, d, heads, out_q, alpha, status, s);
+    case 64: return launch_attn_encoder_hd<64>(qkv, cu_seqlens, seq_ids, n_seqs, max_len, d, heads, out_q, alpha, status, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t* row_slot,

@@ -208,7 +208,7 @@ std::string validate_schema(HostModel* m) {
   }
   const int d = m->dim, f = m->ffn;
   if (m->heads <= 0 || d % m->heads != 0 || d % 16 != 0 || f % 16 != 0 || d > 1024 ||
-      (d / m->heads) % 4 != 0 || d / m->heads > 128 || m->heads > 16)
+      (d / m->heads != 32 && d / m->heads != 48 && d / m->heads != 64) || m->heads > 16)
     return "unsupported dimensions";
   if (m->vocab_src <= 2 || m->vocab_tgt <= 2)
     return "unsupported vocabulary size";
