@@ -174,6 +174,19 @@ mc_status mc_q8_gemm(const int8_t *a, const int8_t *w, int32_t m, int32_t n, int
                      const float *residual, int32_t relu, int32_t mode, void *out,
                      void *stream);
 
+/* Device-level Q8 linear, Q8Linear::run_into (q8_gemm.rs:380-448): quantizes
+ * the device f32 activations x [m, k] with activation_mult (ties-to-even,
+ * clamped to +-127, q8_gemm.rs:569-590) into a stream-ordered scratch buffer
+ * (cudaMallocAsync on stream, released after use), runs the int8 GEMM with
+ * the device int8 weights w [n, k] (canonical [out, in]) and writes device
+ * f32 y [m, n] = acc * (1 / (activation_mult * weight_mult)) + bias[n]
+ * (bias nullable).  k must be a multiple of 16.  A non-finite activation
+ * sets the non-finite bit read by mc_op_status (the reference returns an
+ * error for it). */
+mc_status mc_q8_linear(const float *x, int32_t m, int32_t k, const int8_t *w, int32_t n,
+                       float activation_mult, float weight_mult, const float *bias, float *y,
+                       void *stream);
+
 /* Reads and clears the status word the operator API's kernels write on the
  * current device (non-finite quantizer input, wait timeout); synchronizes. */
 mc_status mc_op_status(uint32_t *status_bits);

@@ -389,6 +389,19 @@ __global__ void attn_decode_kernel(const float* __restrict__ q, int ldq,
   if (has1) out_q[(size_t)r * d + h * hd + lane + 32] = quantize_one(acc1, alpha, status);
 }
 
+// ---- activation quantization (q8_gemm.rs:569-590) ------------------------------
+__global__ void quantize_kernel(const float* __restrict__ x, long long n4, float alpha,
+                                int8_t* __restrict__ out, uint32_t* status) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  const float4 v = reinterpret_cast<const float4*>(x)[i];
+  const uint32_t w = (uint32_t)(uint8_t)quantize_one(v.x, alpha, status) |
+                     ((uint32_t)(uint8_t)quantize_one(v.y, alpha, status) << 8) |
+                     ((uint32_t)(uint8_t)quantize_one(v.z, alpha, status) << 16) |
+                     ((uint32_t)(uint8_t)quantize_one(v.w, alpha, status) << 24);
+  reinterpret_cast<uint32_t*>(out)[i] = w;
+}
+
 // ---- token selection ----------------------------------------------------------
 __global__ void finalize_kernel(int rows, const int32_t* __restrict__ row_slot,
                                 unsigned long long* __restrict__ best, int32_t* slot_prev,
@@ -527,6 +540,13 @@ cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t*
                                                     pages_per_slot, page_tokens, k_pool, v_pool, d,
                                                     heads, out_q, alpha, status);
   return cudaGetLastError();
+}
+
+void launch_quantize(const float* x, long long n, float alpha, int8_t* out, uint32_t* status,
+                     cudaStream_t s) {
+  if (n <= 0) return;
+  const long long n4 = n / 4;
+  quantize_kernel<<<blocks_for(n4, 256), 256, 0, s>>>(x, n4, alpha, out, status);
 }
 
 void launch_finalize(int rows, const int32_t* row_slot, unsigned long long* best,

@@ -78,6 +78,11 @@ void launch_finalize(int rows, const int32_t* row_slot, unsigned long long* best
                      int32_t* slot_prev, int32_t* slot_step, const int32_t* slot_limit,
                      int32_t* step_tokens, uint8_t* done, uint32_t* status, cudaStream_t s);
 
+// q8_gemm.rs:569-590: out[i] = clamp(rte(x[i] * alpha), -127, 127) for n
+// values (n a multiple of 4), stored centred (the reference's u8 minus 127).
+void launch_quantize(const float* x, long long n, float alpha, int8_t* out, uint32_t* status,
+                     cudaStream_t s);
+
 // Initializes newly admitted slots: prev = -1, step = 0, limit, force_len,
 // source length, SSRU states zeroed (state pools [layers][slots][d]).
 void launch_init_slots(int n, const int32_t* slots, const int32_t* limits, const int32_t* force,

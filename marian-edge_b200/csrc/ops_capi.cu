@@ -3,6 +3,9 @@
 #include <cstring>
 #include <mutex>
 
+#include <cmath>
+
+#include "kernels.cuh"
 #include "marian_cuda.h"
 #include "q8_gemm.cuh"
 
@@ -62,6 +65,52 @@ extern "C" mc_status mc_q8_gemm(const int8_t* a, const int8_t* w, int32_t m, int
   p.status = status;
   cudaError_t e = mc::launch_q8_gemm(p, bn, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MC_OK : MC_CUDA;
+}
+
+extern "C" mc_status mc_q8_linear(const float* x, int32_t m, int32_t k, const int8_t* w, int32_t n,
+                                  float activation_mult, float weight_mult, const float* bias,
+                                  float* y, void* stream) {
+  if (m < 0 || n <= 0 || k <= 0 || (k % 16) != 0 || !x || !w || !y ||
+      (reinterpret_cast<uintptr_t>(x) & 15) != 0)
+    return MC_INVALID_INPUT;
+  if (!std::isfinite(activation_mult) || activation_mult <= 0.0f || !std::isfinite(weight_mult) ||
+      weight_mult <= 0.0f)
+    return MC_INVALID_INPUT;
+  const float inverse_scale = 1.0f / (activation_mult * weight_mult);  // q8_gemm.rs:438
+  if (!std::isfinite(inverse_scale) || inverse_scale <= 0.0f) return MC_INVALID_INPUT;
+  if (m == 0) return MC_OK;
+  uint32_t* status = op_status_word();
+  if (!status) return MC_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Q8LinearScratch::quantized (q8_gemm.rs:44-49): a stream-ordered buffer
+  // for the quantized activations, released when the GEMM is done with it.
+  int8_t* q = nullptr;
+  if (cudaMallocAsync(reinterpret_cast<void**>(&q), (size_t)m * k, s) != cudaSuccess) return MC_CUDA;
+  mc::launch_quantize(x, (long long)m * k, activation_mult, q, status, s);
+  mc::GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  const int bn = mc::pick_bn(m, n);
+  mc::GemmGroup& g = p.g[0];
+  mc_status st = MC_OK;
+  if (!mc::encode_tmap_i8(&g.tmap_a, q, (uint64_t)m, (uint64_t)k, 128) ||
+      !mc::encode_tmap_i8(&g.tmap_b, w, (uint64_t)n, (uint64_t)k, (uint32_t)bn)) {
+    st = MC_INVALID_INPUT;
+  } else {
+    g.uniform_scale = inverse_scale;
+    g.bias = bias;
+    g.out = y;
+    g.n = n;
+    g.ldo = n;
+    g.mode = mc::kEpiF32;
+    p.m = m;
+    p.k = k;
+    p.num_groups = 1;
+    p.max_n = n;
+    p.status = status;
+    if (mc::launch_q8_gemm(p, bn, s) != cudaSuccess) st = MC_CUDA;
+  }
+  if (cudaFreeAsync(q, s) != cudaSuccess && st == MC_OK) st = MC_CUDA;
+  return st;
 }
 
 extern "C" mc_status mc_op_status(uint32_t* status_bits) {
