@@ -187,6 +187,29 @@ mc_status mc_q8_linear(const float *x, int32_t m, int32_t k, const int8_t *w, in
                        float activation_mult, float weight_mult, const float *bias, float *y,
                        void *stream);
 
+/* Largest m * k accepted by mc_q8_linear_noalloc (bytes of quantized
+ * activations in its fixed device scratch). */
+#define MC_Q8_LINEAR_NOALLOC_MAX_ACTIVATIONS (8u * 1024u * 1024u)
+
+/* mc_q8_linear without any device allocation.  No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc -- a host
+ * application whose memory manager has reserved the GPU's memory for its own
+ * pool, or a latency-critical path that cannot take an allocation's driver
+ * call.  Same arguments and results as mc_q8_linear; the quantized
+ * activations go to a fixed device array of
+ * MC_Q8_LINEAR_NOALLOC_MAX_ACTIVATIONS bytes (plus a status word) that every
+ * GPU using the library holds until the process exits.  m * k beyond that
+ * size returns MC_INVALID_INPUT without launching anything.  The first call
+ * on a device looks up the array's device address (make it before any
+ * stream capture).  All calls share the array: calls whose kernels overlap
+ * on the GPU race.  status_bits (host pointer, nullable): when given, the
+ * call synchronizes the stream and returns the status bits recorded since
+ * the last report (bit 0: non-finite activation), clearing them; when null
+ * the call stays asynchronous and the bits accumulate. */
+mc_status mc_q8_linear_noalloc(const float *x, int32_t m, int32_t k, const int8_t *w, int32_t n,
+                               float activation_mult, float weight_mult, const float *bias,
+                               float *y, void *stream, uint32_t *status_bits);
+
 /* Reads and clears the status word the operator API's kernels write on the
  * current device (non-finite quantizer input, wait timeout); synchronizes. */
 mc_status mc_op_status(uint32_t *status_bits);
