@@ -184,6 +184,14 @@ __device__ __forceinline__ int8_t quantize_one(float v, float alpha, uint32_t* s
   return static_cast<int8_t>(static_cast<int>(s));
 }
 
+// quantize_one without the finiteness check (the caller checks a block of
+// values at once): rint(v * alpha) clamped to [-127, 127].  A NaN converts
+// to 0 and is reported by the caller.
+__device__ __forceinline__ int quantize_rte_clamped(float v, float alpha) {
+  const int q = __float2int_rn(__fmul_rn(v, alpha));  // saturating conversion
+  return q < -127 ? -127 : (q > 127 ? 127 : q);
+}
+
 // acc as f32 * scale + bias, two roundings (no fused multiply-add).
 __device__ __forceinline__ float dequant(int32_t acc, float scale, float bias) {
   return __fadd_rn(__fmul_rn(__int2float_rn(acc), scale), bias);

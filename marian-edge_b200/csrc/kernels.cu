@@ -231,8 +231,10 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
   const int q0 = blockIdx.z * 32;
   if (q0 >= len) return;
   const int ld = 3 * d;
-  constexpr int KLD = HD + 1;
-  float* ks = sm;                                 // [max_len][HD + 1]
+  // K row stride HD + 4 floats: 16-byte aligned rows whose 4-word index is
+  // odd, so the 8 lanes of each 128-bit shared load phase hit distinct banks.
+  constexpr int KLD = HD + 4;
+  float* ks = sm;                                 // [max_len][HD + 4]
   float* vs = ks + (size_t)max_len * KLD;          // [max_len][HD]
   float* qs = vs + (size_t)max_len * HD;          // [warps][HD]
   float* ps = qs + kEncWarps * HD;                // [warps][max_len]
@@ -240,12 +242,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
   for (int idx = threadIdx.x; idx < len * kVec; idx += blockDim.x) {
     const int j = idx / kVec, i = (idx % kVec) * 4;
     const float* row = qkv + (size_t)(start + j) * ld + h * HD + i;
-    const float4 k4 = *reinterpret_cast<const float4*>(row + d);
-    float* kd = ks + j * KLD + i;
-    kd[0] = k4.x;
-    kd[1] = k4.y;
-    kd[2] = k4.z;
-    kd[3] = k4.w;
+    *reinterpret_cast<float4*>(ks + j * KLD + i) = *reinterpret_cast<const float4*>(row + d);
     *reinterpret_cast<float4*>(vs + j * HD + i) = *reinterpret_cast<const float4*>(row + 2 * d);
   }
   __syncthreads();
@@ -258,12 +255,27 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
     const float* qrow = qkv + (size_t)(start + qi) * ld + h * HD;
     for (int i = lane; i < HD; i += 32) qw[i] = qrow[i];
     __syncwarp();
+    float q[HD];
+#pragma unroll
+    for (int i = 0; i < HD; i += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(qw + i);
+      q[i] = v.x;
+      q[i + 1] = v.y;
+      q[i + 2] = v.z;
+      q[i + 3] = v.w;
+    }
     float mx = -INFINITY;
     for (int j = lane; j < len; j += 32) {
       const float* kr = ks + j * KLD;
       float dot = 0.0f;
 #pragma unroll
-      for (int i = 0; i < HD; ++i) dot = dot + qw[i] * kr[i];
+      for (int i = 0; i < HD; i += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
+        dot = dot + q[i] * k4.x;
+        dot = dot + q[i + 1] * k4.y;
+        dot = dot + q[i + 2] * k4.z;
+        dot = dot + q[i + 3] * k4.w;
+      }
       const float sc = dot * scale;
       pw[j] = sc;
       mx = fmaxf(mx, sc);
@@ -281,18 +293,23 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
     inv = __shfl_sync(0xffffffffu, inv, 0);
     for (int j = lane; j < len; j += 32) pw[j] = pw[j] * inv;
     __syncwarp();
-    const bool has1 = lane + 32 < HD;
+    // lane owns output dims 2*lane and 2*lane + 1
+    const bool active = 2 * lane < HD;
     float acc0 = 0.0f, acc1 = 0.0f;
 #pragma unroll 8
     for (int j = 0; j < len; ++j) {
       const float p = pw[j];
-      const float* vr = vs + j * HD + lane;
-      acc0 = acc0 + vr[0] * p;
-      if (has1) acc1 = acc1 + vr[32] * p;
+      const float2 v2 = active ? *reinterpret_cast<const float2*>(vs + j * HD + 2 * lane)
+                               : make_float2(0.f, 0.f);
+      acc0 = acc0 + v2.x * p;
+      acc1 = acc1 + v2.y * p;
     }
-    int8_t* o = out_q + (size_t)(start + qi) * d + h * HD + lane;
-    o[0] = quantize_one(acc0, alpha, status);
-    if (has1) o[32] = quantize_one(acc1, alpha, status);
+    if (active) {
+      int8_t* o = out_q + (size_t)(start + qi) * d + h * HD + 2 * lane;
+      const uint16_t w2 = (uint16_t)(uint8_t)quantize_one(acc0, alpha, status) |
+                          ((uint16_t)(uint8_t)quantize_one(acc1, alpha, status) << 8);
+      *reinterpret_cast<uint16_t*>(o) = w2;
+    }
     __syncwarp();
   }
 }
@@ -502,7 +519,7 @@ cudaError_t launch_attn_encoder_hd(const float* qkv, const int32_t* cu_seqlens,
                                    const int32_t* seq_ids, int n_seqs, int max_len, int d,
                                    int heads, int8_t* out_q, float alpha, uint32_t* status,
                                    cudaStream_t s) {
-  const size_t smem = sizeof(float) * ((size_t)max_len * (2 * HD + 1) + kEncWarps * (size_t)HD +
+  const size_t smem = sizeof(float) * ((size_t)max_len * (2 * HD + 4) + kEncWarps * (size_t)HD +
                                        kEncWarps * (size_t)max_len);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(attn_encoder_kernel<HD>,

@@ -37,113 +37,243 @@ __device__ __forceinline__ unsigned long long pack_argmax(float v, int32_t n) {
   return (static_cast<unsigned long long>(ord) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(n));
 }
 
+// Per-warp staging tile for coalesced stores: 32 rows x 33 words (the odd
+// stride keeps both the row-wise writes and the column-wise reads of the 32
+// lanes on distinct banks).
+constexpr int kStageLd = 33;
+constexpr int kStagingBytes = kEpiWarps * 32 * kStageLd * 4;
+
+// One 32-column chunk of one tile row per lane.  `ok` is this lane's row
+// validity; the call itself is warp-uniform (tcgen05.ld precedes it).
 template <int BN>
 __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_t (&r)[32],
-                                               int row, int dest_row, int nb, float row_scale,
-                                               uint32_t* status, float& best, int& best_n) {
+                                               bool ok, int row, int dest_row, int nb,
+                                               float row_scale, uint32_t* status, float& best,
+                                               int& best_n, uint32_t* stage) {
   const int n_end = g.n;
+  const int lane = threadIdx.x & 31;
+  if (g.mode == kEpiArgmax) {
+    if (!ok) return;
+    const bool mask_eos = g.eos_mask != nullptr && g.eos_mask[row] != 0;
+    uint32_t cand = g.cand_bits[nb >> 5];  // nb is a multiple of 32
+    if (nb == 0 && mask_eos) cand &= ~1u;
+    if (nb + 32 > n_end) cand &= (n_end - nb >= 32) ? 0xFFFFFFFFu : ((1u << (n_end - nb)) - 1u);
+    const float uscale = g.row_scale ? __fmul_rn(row_scale, g.uniform_scale) : g.uniform_scale;
+    const float4* b4 = reinterpret_cast<const float4*>(g.bias + nb);
+    const bool full = nb + 32 <= n_end;
+#pragma unroll
+    for (int j4 = 0; j4 < 8; ++j4) {
+      float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (g.bias) {
+        if (full) {
+          b = b4[j4];
+        } else {
+          const int n = nb + 4 * j4;
+          b.x = n < n_end ? g.bias[n] : 0.f;
+          b.y = n + 1 < n_end ? g.bias[n + 1] : 0.f;
+          b.z = n + 2 < n_end ? g.bias[n + 2] : 0.f;
+          b.w = n + 3 < n_end ? g.bias[n + 3] : 0.f;
+        }
+      }
+      const float bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = 4 * j4 + u;
+        float scale = uscale;
+        if (g.col_scale && nb + j < n_end)
+          scale = g.row_scale ? __fmul_rn(row_scale, g.col_scale[nb + j]) : g.col_scale[nb + j];
+        const float logit = dequant(static_cast<int32_t>(r[j]), scale, bb[u]);
+        if (((cand >> j) & 1u) && logit > best) {  // strict: the lowest index wins ties
+          best = logit;
+          best_n = nb + j;
+        }
+      }
+    }
+    return;
+  }
   if (g.mode == kEpiI32) {
+    if (!ok) return;
     int32_t* out = static_cast<int32_t*>(g.out) + (size_t)dest_row * g.ldo + g.col_off;
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (nb + j < n_end) out[nb + j] = static_cast<int32_t>(r[j]);
     return;
   }
-  if (g.mode == kEpiArgmax) {
-    const bool mask_eos = g.eos_mask != nullptr && g.eos_mask[row] != 0;
-    uint32_t cand = g.cand_bits[nb >> 5];  // nb is a multiple of 32
-    if (nb == 0 && mask_eos) cand &= ~1u;
-    const float uscale = g.row_scale ? __fmul_rn(row_scale, g.uniform_scale) : g.uniform_scale;
+  float v[32];
+  const bool full = nb + 32 <= n_end;
+  if (full && !g.residual) {
+    // Fast path: per-column scale and bias fetched four at a time, no
+    // per-element bounds checks.
+    const float us = g.uniform_scale;
+#pragma unroll
+    for (int j4 = 0; j4 < 8; ++j4) {
+      float4 s4 = g.col_scale ? reinterpret_cast<const float4*>(g.col_scale + nb)[j4]
+                              : make_float4(us, us, us, us);
+      if (g.row_scale) {
+        s4.x = __fmul_rn(row_scale, s4.x);
+        s4.y = __fmul_rn(row_scale, s4.y);
+        s4.z = __fmul_rn(row_scale, s4.z);
+        s4.w = __fmul_rn(row_scale, s4.w);
+      }
+      const float4 b4 = g.bias ? reinterpret_cast<const float4*>(g.bias + nb)[j4]
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[4 * j4 + 0] = dequant(static_cast<int32_t>(r[4 * j4 + 0]), s4.x, b4.x);
+      v[4 * j4 + 1] = dequant(static_cast<int32_t>(r[4 * j4 + 1]), s4.y, b4.y);
+      v[4 * j4 + 2] = dequant(static_cast<int32_t>(r[4 * j4 + 2]), s4.z, b4.z);
+      v[4 * j4 + 3] = dequant(static_cast<int32_t>(r[4 * j4 + 3]), s4.w, b4.w);
+    }
+    if (g.relu) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+    }
+  } else {
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int n = nb + j;
-      if (n >= n_end) break;
-      if (!((cand >> j) & 1u)) continue;
-      float scale = uscale;
-      if (g.col_scale) scale = g.row_scale ? __fmul_rn(row_scale, g.col_scale[n]) : g.col_scale[n];
-      const float logit = dequant(static_cast<int32_t>(r[j]), scale, g.bias ? g.bias[n] : 0.0f);
-      if (logit > best) {  // strict: the lowest index wins ties
-        best = logit;
-        best_n = n;
+      float x = 0.0f;
+      if (ok && n < n_end) {
+        float scale = g.col_scale ? g.col_scale[n] : g.uniform_scale;
+        if (g.row_scale) scale = __fmul_rn(row_scale, scale);
+        x = dequant(static_cast<int32_t>(r[j]), scale, g.bias ? g.bias[n] : 0.0f);
+        if (g.relu) x = fmaxf(x, 0.0f);
+        if (g.residual) x = __fadd_rn(x, g.residual[(size_t)row * g.ldr + n]);
       }
-    }
-    return;
-  }
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const int n = nb + j;
-    if (n < n_end) {
-      float scale = g.col_scale ? g.col_scale[n] : g.uniform_scale;
-      if (g.row_scale) scale = __fmul_rn(row_scale, scale);
-      float x = dequant(static_cast<int32_t>(r[j]), scale, g.bias ? g.bias[n] : 0.0f);
-      if (g.relu) x = fmaxf(x, 0.0f);
-      if (g.residual) x = __fadd_rn(x, g.residual[(size_t)row * g.ldr + n]);
       v[j] = x;
-    } else {
-      v[j] = 0.0f;
     }
   }
-  const bool full = nb + 32 <= n_end;
   if (g.mode == kEpiF32) {
-    float* out = static_cast<float*>(g.out) + (size_t)dest_row * g.ldo + g.col_off + nb;
-    if (full && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
-      float4* o4 = reinterpret_cast<float4*>(out);
+    const bool aligned = ((reinterpret_cast<uintptr_t>(g.out) | (uintptr_t)g.ldo * 4 |
+                           (uintptr_t)(g.col_off + nb) * 4) & 15) == 0;
+    if (full && aligned) {
+      // stage the 32x32 block, then each instruction stores 4 rows x 128 B
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    } else {
+      for (int j = 0; j < 32; ++j) stage[lane * kStageLd + j] = __float_as_uint(v[j]);
+      __syncwarp();
+      const int sub = lane >> 3, c4 = (lane & 7) * 4;
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int rr = it * 4 + sub;
+        const int drow = __shfl_sync(0xffffffffu, dest_row, rr);
+        const bool rok = __shfl_sync(0xffffffffu, ok ? 1 : 0, rr) != 0;
+        const uint32_t* srow = stage + rr * kStageLd + c4;
+        if (rok) {
+          float* o = static_cast<float*>(g.out) + (size_t)drow * g.ldo + g.col_off + nb + c4;
+          *reinterpret_cast<float4*>(o) = make_float4(__uint_as_float(srow[0]), __uint_as_float(srow[1]),
+                                                      __uint_as_float(srow[2]), __uint_as_float(srow[3]));
+        }
+      }
+      __syncwarp();
+    } else if (ok) {
+      float* out = static_cast<float*>(g.out) + (size_t)dest_row * g.ldo + g.col_off + nb;
       for (int j = 0; j < 32; ++j)
         if (nb + j < n_end) out[j] = v[j];
     }
   } else {  // kEpiQ8
-    int8_t* out = static_cast<int8_t*>(g.out) + (size_t)dest_row * g.ldo + g.col_off + nb;
-    int8_t q[32];
+    uint32_t q4[8];
+    bool finite = true;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) q[j] = (nb + j < n_end) ? quantize_one(v[j], g.alpha, status) : 0;
-    if (full && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
-      uint4* o = reinterpret_cast<uint4*>(out);
-      const uint4* s = reinterpret_cast<const uint4*>(q);
-      o[0] = s[0];
-      o[1] = s[1];
-    } else {
+    for (int w = 0; w < 8; ++w) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = 4 * w + u;
+        finite &= fabsf(v[j]) <= 3.402823466e38f;  // false for NaN and +-inf
+        const int qi = (ok && nb + j < n_end) ? quantize_rte_clamped(v[j], g.alpha) : 0;
+        word |= (uint32_t)(uint8_t)(int8_t)qi << (8 * u);
+      }
+      q4[w] = word;
+    }
+    if (!finite && ok) flag_status(status, kStatusNonFinite);
+    const bool aligned = ((reinterpret_cast<uintptr_t>(g.out) | (uintptr_t)g.ldo |
+                           (uintptr_t)(g.col_off + nb)) & 3) == 0;
+    if (full && aligned) {
+      // stage 32 rows x 32 bytes, then each instruction stores 4 rows x 32 B
+#pragma unroll
+      for (int w = 0; w < 8; ++w) stage[lane * 9 + w] = q4[w];
+      __syncwarp();
+      const int sub = lane >> 3, w = lane & 7;
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int rr = it * 4 + sub;
+        const int drow = __shfl_sync(0xffffffffu, dest_row, rr);
+        const bool rok = __shfl_sync(0xffffffffu, ok ? 1 : 0, rr) != 0;
+        if (rok) {
+          int8_t* o = static_cast<int8_t*>(g.out) + (size_t)drow * g.ldo + g.col_off + nb + 4 * w;
+          *reinterpret_cast<uint32_t*>(o) = stage[rr * 9 + w];
+        }
+      }
+      __syncwarp();
+    } else if (ok) {
+      int8_t* out = static_cast<int8_t*>(g.out) + (size_t)dest_row * g.ldo + g.col_off + nb;
       for (int j = 0; j < 32; ++j)
-        if (nb + j < n_end) out[j] = q[j];
+        if (nb + j < n_end) out[j] = (int8_t)((q4[j >> 2] >> (8 * (j & 3))) & 0xFF);
     }
   }
 }
 
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_constant__ GemmParams p) {
-  const GemmGroup& g = p.g[blockIdx.z];
-  const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * kBM;
-  if (n0 >= g.n) return;  // whole CTA leaves before any barrier
+// Tile order shared by the three roles: tile t -> (group, m tile, n tile),
+// n fastest.  Tiles past a group's own N are skipped by every role alike.
+struct TileCoord {
+  int z, m0, n0;
+};
 
+template <int BN>
+__device__ __forceinline__ bool tile_coord(const GemmParams& p, int t, int n_tiles, int m_tiles,
+                                           TileCoord* c) {
+  const int per_group = n_tiles * m_tiles;
+  c->z = t / per_group;
+  const int rem = t - c->z * per_group;
+  c->m0 = (rem / n_tiles) * kBM;
+  c->n0 = (rem % n_tiles) * BN;
+  return c->n0 < p.g[c->z].n;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Persistent: each CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...
+// The shared-memory ring continues across tiles, and the accumulator is
+// double-buffered in TMEM (2 x BN columns) so the epilogue of one tile
+// overlaps the MMAs of the next.
+template <int BN, int MAX_STAGES>
+__global__ void __launch_bounds__(kThreads, 2) q8_gemm_kernel(const __grid_constant__ GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* smem_a = smem;                           // STAGES x 16 KB
-  uint8_t* smem_b = smem + STAGES * kBM * kBK;      // STAGES x BN*128
-  __shared__ __align__(8) uint64_t full_bar[STAGES];
-  __shared__ __align__(8) uint64_t empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t accum_bar;
+  const int stages = p.stages;
+  uint8_t* smem_a = smem;                           // stages x 16 KB
+  uint8_t* smem_b = smem + stages * kBM * kBK;      // stages x BN*128
+  uint32_t* staging = reinterpret_cast<uint32_t*>(smem_b + stages * BN * kBK);  // kStagingBytes
+  __shared__ __align__(8) uint64_t full_bar[MAX_STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[MAX_STAGES];
+  __shared__ __align__(8) uint64_t tfull_bar[2];
+  __shared__ __align__(8) uint64_t tempty_bar[2];
   __shared__ uint32_t tmem_base_s;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_kb = (p.k + kBK - 1) / kBK;
+  const int n_tiles = (p.max_n + BN - 1) / BN;
+  const int m_tiles = (p.m + kBM - 1) / kBM;
+  const int total = n_tiles * m_tiles * p.num_groups;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&accum_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], kEpiWarps);
+    }
     fence_barrier_init();
-    tma_prefetch_desc(&g.tmap_a);
-    tma_prefetch_desc(&g.tmap_b);
+    for (int z = 0; z < p.num_groups; ++z) {
+      tma_prefetch_desc(&p.g[z].tmap_a);
+      tma_prefetch_desc(&p.g[z].tmap_b);
+    }
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_base_s, BN);
+    tmem_alloc(&tmem_base_s, 2 * BN);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -154,93 +284,142 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
   if (warp == 0) {
     if (lane == 0) {
       constexpr uint32_t kStageBytes = kBM * kBK + BN * kBK;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t phase = (kb / STAGES) & 1;
-        if (!mbar_wait(&empty_bar[s], phase ^ 1, p.status)) break;
-        mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
-        tma_load_2d(smem_a + s * kBM * kBK, &g.tmap_a, kb * kBK, m0, &full_bar[s]);
-        tma_load_2d(smem_b + s * BN * kBK, &g.tmap_b, kb * kBK, n0, &full_bar[s]);
+      int kbg = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        TileCoord c;
+        if (!tile_coord<BN>(p, t, n_tiles, m_tiles, &c)) continue;
+        const GemmGroup& g = p.g[c.z];
+        for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
+          const int s = kbg % stages;
+          const uint32_t phase = (kbg / stages) & 1;
+          if (!(ok = mbar_wait(&empty_bar[s], phase ^ 1, p.status))) break;
+          mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+          tma_load_2d(smem_a + s * kBM * kBK, &g.tmap_a, kb * kBK, c.m0, &full_bar[s]);
+          tma_load_2d(smem_b + s * BN * kBK, &g.tmap_b, kb * kBK, c.n0, &full_bar[s]);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_i8(kBM, BN);
+      int kbg = 0, it = 0;
       bool ok = true;
-      for (int kb = 0; kb < num_kb && ok; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t phase = (kb / STAGES) & 1;
-        ok = mbar_wait(&full_bar[s], phase, p.status);
-        if (!ok) break;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        TileCoord c;
+        if (!tile_coord<BN>(p, t, n_tiles, m_tiles, &c)) continue;
+        const int buf = it & 1;
+        if (!(ok = mbar_wait(&tempty_bar[buf], ((it >> 1) & 1) ^ 1, p.status))) break;
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem_a + s * kBM * kBK);
-        const uint32_t b_addr = smem_u32(smem_b + s * BN * kBK);
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
+          const int s = kbg % stages;
+          const uint32_t phase = (kbg / stages) & 1;
+          if (!(ok = mbar_wait(&full_bar[s], phase, p.status))) break;
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem_a + s * kBM * kBK);
+          const uint32_t b_addr = smem_u32(smem_b + s * BN * kBK);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 32; ++kk) {
-          mma_i8(tmem_base, sdesc_k_sw128(a_addr + kk * 32), sdesc_k_sw128(b_addr + kk * 32), idesc,
-                 (kb > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBK / 32; ++kk)
+            mma_i8(d_tmem, sdesc_k_sw128(a_addr + kk * 32), sdesc_k_sw128(b_addr + kk * 32), idesc,
+                   (kb > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&empty_bar[s]);
         }
-        mma_commit(&empty_bar[s]);
+        mma_commit(&tfull_bar[buf]);
+        ++it;
       }
-      mma_commit(&accum_bar);
     }
   } else {
     // Epilogue warps 2..9: warp % 4 selects the TMEM lane quarter (rows),
     // (warp - 2) / 4 the half of the tile's columns.
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
-    const int row_in_tile = quarter * 32 + lane;
-    const int row = m0 + row_in_tile;
-    const bool row_ok = row < p.m;
-    // Warp-uniform: tcgen05.ld below is .sync.aligned.
-    const bool ready = __all_sync(0xffffffffu, mbar_wait(&accum_bar, 0, p.status));
-    tc_fence_after();
-    if (ready) {
+    uint32_t* stage = staging + (warp - 2) * 32 * kStageLd;
+    int it = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      TileCoord c;
+      if (!tile_coord<BN>(p, t, n_tiles, m_tiles, &c)) continue;
+      const GemmGroup& g = p.g[c.z];
+      const int buf = it & 1;
+      // Warp-uniform: tcgen05.ld below is .sync.aligned.
+      const bool ready = __all_sync(0xffffffffu, mbar_wait(&tfull_bar[buf], (it >> 1) & 1, p.status));
+      if (!ready) break;
+      tc_fence_after();
+      const int row = c.m0 + quarter * 32 + lane;
+      const bool row_ok = row < p.m;
       const int dest_row = row_ok ? (g.row_map ? g.row_map[row] : row) : 0;
       const float row_scale = (row_ok && g.row_scale) ? g.row_scale[row] : 1.0f;
       float best = -INFINITY;
       int best_n = -1;
-      const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+      const uint32_t lane_base = tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
       constexpr int kHalf = BN / 2 >= 32 ? BN / 2 : 32;
 #pragma unroll 1
       for (int c0 = half * kHalf; c0 < BN && c0 < (half + 1) * kHalf; c0 += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(lane_base + c0, r);
         tmem_ld_wait();
-        if (row_ok && dest_row >= 0 && n0 + c0 < g.n)
-          epilogue_chunk<BN>(g, r, row, dest_row, n0 + c0, row_scale, p.status, best, best_n);
+        if (c.n0 + c0 < g.n)
+          epilogue_chunk<BN>(g, r, row_ok && dest_row >= 0, row, dest_row, c.n0 + c0, row_scale,
+                             p.status, best, best_n, stage);
       }
       if (g.mode == kEpiArgmax && row_ok && dest_row >= 0 && best_n >= 0)
         atomicMax(&g.argmax[dest_row], pack_argmax(best, best_n));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[buf]);
+      ++it;
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, BN);
+    tmem_dealloc(tmem_base, 2 * BN);
   }
 }
 
-template <int BN, int STAGES>
-constexpr int smem_bytes() {
-  return STAGES * (kBM * kBK + BN * kBK) + 1024;
+template <int BN>
+constexpr int stage_bytes() {
+  return kBM * kBK + BN * kBK;
 }
 
-template <int BN, int STAGES>
-cudaError_t launch_impl(const GemmParams& p, cudaStream_t stream) {
-  constexpr int smem = smem_bytes<BN, STAGES>();
-  auto kern = q8_gemm_kernel<BN, STAGES>;
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 63;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+template <int BN, int MAX_STAGES>
+cudaError_t launch_impl(GemmParams p, cudaStream_t stream) {
+  auto kern = q8_gemm_kernel<BN, MAX_STAGES>;
   static unsigned long long configured = 0;  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured & (1ull << (dev & 63)))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         MAX_STAGES * stage_bytes<BN>() + kStagingBytes + 1024);
     if (e != cudaSuccess) return e;
     configured |= 1ull << (dev & 63);
   }
-  dim3 grid((p.max_n + BN - 1) / BN, (p.m + kBM - 1) / kBM, p.num_groups);
-  kern<<<grid, kThreads, smem, stream>>>(p);
+  const int num_kb = (p.k + kBK - 1) / kBK;
+  const int tiles = ((p.max_n + BN - 1) / BN) * ((p.m + kBM - 1) / kBM) * p.num_groups;
+  // Two CTAs per SM for the narrow tile when a 3-stage ring covers short K.
+  int ctas_per_sm = 1;
+  int stages = MAX_STAGES;
+  if (BN == 64 && num_kb <= 4) {
+    stages = 3;
+    ctas_per_sm = 2;
+  }
+  const int grid = tiles < num_sms() * ctas_per_sm ? tiles : num_sms() * ctas_per_sm;
+  p.stages = stages;
+  kern<<<grid, kThreads, stages * stage_bytes<BN>() + kStagingBytes + 1024, stream>>>(p);
   return cudaGetLastError();
 }
 
@@ -285,9 +464,9 @@ int pick_bn(int m, int max_n) {
 cudaError_t launch_q8_gemm(const GemmParams& p, int bn, cudaStream_t stream) {
   if (p.m <= 0 || p.num_groups <= 0) return cudaSuccess;
   switch (bn) {
-    case 256: return launch_impl<256, 4>(p, stream);
-    case 128: return launch_impl<128, 6>(p, stream);
-    default: return launch_impl<64, 8>(p, stream);
+    case 256: return launch_impl<256, 3>(p, stream);
+    case 128: return launch_impl<128, 5>(p, stream);
+    default: return launch_impl<64, 7>(p, stream);
   }
 }
 

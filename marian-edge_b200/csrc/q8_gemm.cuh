@@ -52,6 +52,7 @@ struct GemmParams {
   int32_t k;           // inner dimension (multiple of 16)
   int32_t num_groups;
   int32_t max_n;       // max over groups of n
+  int32_t stages;      // shared-memory ring depth (set by the launcher)
   uint32_t* status;    // device status word (error bits)
 };
 
