@@ -121,6 +121,7 @@ struct mc_engine {
   QBuf dec_q[kMaxQuantOut];
   QBuf dec_o, dec_h;
   int32_t *row_slot = nullptr, *self_row_map = nullptr, *step_tokens = nullptr;
+  int32_t *order_self = nullptr, *order_cross = nullptr;  // rows, longest keys first
   uint8_t *eos_mask = nullptr, *done = nullptr;
   unsigned long long* best = nullptr;
 
@@ -520,7 +521,7 @@ mc_status run_decode_step(mc_engine* e, int R) {
           {&e->dec_q[2], &a.wv, kEpiF32, e->self_v[l], d, 0, e->self_row_map, false, 0.f}};
       if ((st = gemm(e, MC_K_GEMM_QKV, R, qkv, 3))) return st;
       PROFILED(MC_K_ATTN_SELF, 4.0 * self_keys * d, 8.0 * self_keys * d + rows_d * 5,
-               CK(launch_attn_decode(e->dec_qkv, d, R, e->row_slot, e->slot_step, 1,
+               CK(launch_attn_decode(e->dec_qkv, d, R, e->row_slot, e->order_self, e->slot_step, 1,
                                      e->self_pages_d, e->pages_per_slot, e->page_tokens,
                                      e->self_k[l], e->self_v[l], d, e->heads, e->dec_o.p,
                                      a.wo.alpha, e->d_status, e->stream)));
@@ -546,7 +547,7 @@ mc_status run_decode_step(mc_engine* e, int R) {
     GroupSpec wq = {&e->dec_q[0], &c.wq, kEpiF32, e->dec_qkv, d, 0, nullptr, false, 0.f};
     if ((st = gemm(e, MC_K_GEMM_QKV, R, &wq, 1))) return st;
     PROFILED(MC_K_ATTN_CROSS, 4.0 * cross_keys * d, 8.0 * cross_keys * d + rows_d * 5,
-             CK(launch_attn_decode(e->dec_qkv, d, R, e->row_slot, e->slot_src, 0,
+             CK(launch_attn_decode(e->dec_qkv, d, R, e->row_slot, e->order_cross, e->slot_src, 0,
                                    e->cross_pages_d, e->pages_per_slot, e->page_tokens,
                                    e->cross_k[l], e->cross_v[l], d, e->heads, e->dec_o.p,
                                    c.wo.alpha, e->d_status, e->stream)));
@@ -649,6 +650,8 @@ mc_status allocate_buffers(mc_engine* e) {
   if ((st = make_qbuf(e, &e->dec_o, R, d))) return st;
   if ((st = make_qbuf(e, &e->dec_h, R, F))) return st;
   CK(dalloc(e, &e->row_slot, R));
+  CK(dalloc(e, &e->order_self, R));
+  CK(dalloc(e, &e->order_cross, R));
   CK(dalloc(e, &e->self_row_map, R));
   CK(dalloc(e, &e->step_tokens, R));
   CK(dalloc(e, &e->eos_mask, R));
@@ -873,12 +876,38 @@ mc_status admit(mc_engine* e, std::vector<Request*>* admitted) {
   return MC_OK;
 }
 
+// Row orders for the decode attention launches: rows with the most keys
+// first (counting sort; self keys = step + 1, cross keys = source length).
+void build_row_orders(mc_engine* e, int32_t* order_self, int32_t* order_cross) {
+  const int R = (int)e->active.size();
+  int count_s[kMaxSeq + 2] = {0}, count_c[kMaxSeq + 2] = {0};
+  std::vector<int> ks(R), kc(R);
+  for (int r = 0; r < R; ++r) {
+    const Request* q = e->slot_req[e->active[r]];
+    ks[r] = std::min<int>(kMaxSeq + 1, (int)q->output.size() + 1);
+    kc[r] = std::min<int>(kMaxSeq + 1, (int)q->tokens.size());
+    ++count_s[kMaxSeq + 1 - ks[r]];
+    ++count_c[kMaxSeq + 1 - kc[r]];
+  }
+  for (int i = 1; i < kMaxSeq + 2; ++i) {
+    count_s[i] += count_s[i - 1];
+    count_c[i] += count_c[i - 1];
+  }
+  for (int r = R - 1; r >= 0; --r) {
+    order_self[--count_s[kMaxSeq + 1 - ks[r]]] = r;
+    order_cross[--count_c[kMaxSeq + 1 - kc[r]]] = r;
+  }
+}
+
 mc_status decode_once(mc_engine* e) {
   const int R = (int)e->active.size();
   if (R == 0) return MC_OK;
   cudaStream_t s = e->stream;
   std::memcpy(e->h_i32, e->active.data(), R * 4);
+  build_row_orders(e, e->h_i32 + R, e->h_i32 + 2 * R);
   CK(cudaMemcpyAsync(e->row_slot, e->h_i32, R * 4, cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(e->order_self, e->h_i32 + R, R * 4, cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(e->order_cross, e->h_i32 + 2 * R, R * 4, cudaMemcpyHostToDevice, s));
   mc_status st = run_decode_step(e, R);
   if (st) return st;
   CK(cudaMemcpyAsync(e->h_step_tokens, e->step_tokens, R * 4, cudaMemcpyDeviceToHost, s));
@@ -1269,8 +1298,12 @@ extern "C" mc_status mc_trace_first_step(mc_engine* e, const int32_t* tokens, si
           CK(cudaMemcpy(cross_value + dst, e->cross_v[l] + row * d, row_bytes, cudaMemcpyDeviceToHost));
       }
     }
-  std::memcpy(e->h_i32, e->active.data(), e->active.size() * 4);
-  CK(cudaMemcpyAsync(e->row_slot, e->h_i32, e->active.size() * 4, cudaMemcpyHostToDevice, e->stream));
+  const int R = (int)e->active.size();
+  std::memcpy(e->h_i32, e->active.data(), R * 4);
+  build_row_orders(e, e->h_i32 + R, e->h_i32 + 2 * R);
+  CK(cudaMemcpyAsync(e->row_slot, e->h_i32, R * 4, cudaMemcpyHostToDevice, e->stream));
+  CK(cudaMemcpyAsync(e->order_self, e->h_i32 + R, R * 4, cudaMemcpyHostToDevice, e->stream));
+  CK(cudaMemcpyAsync(e->order_cross, e->h_i32 + 2 * R, R * 4, cudaMemcpyHostToDevice, e->stream));
   if ((st = run_decode_step(e, (int)e->active.size()))) {
     abort_all(e);
     return st;

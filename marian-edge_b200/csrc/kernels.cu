@@ -103,7 +103,8 @@ __global__ void embed_decoder_kernel(int rows, const int32_t* __restrict__ row_s
 
 // ---- LayerNorm (normalize_row, tensor.rs:372-385) ------------------------------
 // kLnRows rows per CTA are staged in shared memory with coalesced loads (row
-// stride d + 1 so the per-row threads below hit distinct banks).  One thread
+// stride d + 4: 16-byte aligned, and an odd number of 16-byte chunks so the
+// per-row threads' 128-bit reads hit distinct banks).  One thread
 // per row then sums the row left to right and sums the centred squares left
 // to right, exactly as the reference's Iterator::sum; the normalized rows and
 // their quantized copies are written back coalesced.
@@ -116,19 +117,29 @@ __device__ __forceinline__ void ln_stats_and_store(float* tile, int nrows, int d
                                                    float* __restrict__ out, const QuantOut& q,
                                                    uint32_t* status) {
   __shared__ float s_mean[kLnRows], s_inv[kLnRows];
-  const int ld = d + 1;
+  const int ld = d + 4;
   if (threadIdx.x < nrows) {
     const float* row = tile + threadIdx.x * ld;
     float sum = 0.0f;
-#pragma unroll 16
-    for (int i = 0; i < d; ++i) sum = sum + row[i];
+#pragma unroll 8
+    for (int i = 0; i < d; i += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(row + i);
+      sum = sum + v.x;
+      sum = sum + v.y;
+      sum = sum + v.z;
+      sum = sum + v.w;
+    }
     const float fd = (float)d;
     const float mean = sum / fd;
     float var = 0.0f;
-#pragma unroll 16
-    for (int i = 0; i < d; ++i) {
-      const float c = row[i] - mean;
-      var = var + c * c;
+#pragma unroll 8
+    for (int i = 0; i < d; i += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(row + i);
+      const float c0 = v.x - mean, c1 = v.y - mean, c2 = v.z - mean, c3 = v.w - mean;
+      var = var + c0 * c0;
+      var = var + c1 * c1;
+      var = var + c2 * c2;
+      var = var + c3 * c3;
     }
     var = var / fd;
     s_mean[threadIdx.x] = mean;
@@ -139,15 +150,15 @@ __device__ __forceinline__ void ln_stats_and_store(float* tile, int nrows, int d
 #pragma unroll 4
   for (int idx = threadIdx.x; idx < nrows * vec; idx += blockDim.x) {
     const int rr = idx / vec, c = (idx % vec) * 4;
-    const float* t = tile + rr * ld + c;
+    const float4 t = *reinterpret_cast<const float4*>(tile + rr * ld + c);
     const float mean = s_mean[rr], inv = s_inv[rr];
     const float4 g = *reinterpret_cast<const float4*>(gamma + c);
     const float4 b = *reinterpret_cast<const float4*>(beta + c);
     float4 v;
-    v.x = (t[0] - mean) * inv * g.x + b.x;
-    v.y = (t[1] - mean) * inv * g.y + b.y;
-    v.z = (t[2] - mean) * inv * g.z + b.z;
-    v.w = (t[3] - mean) * inv * g.w + b.w;
+    v.x = (t.x - mean) * inv * g.x + b.x;
+    v.y = (t.y - mean) * inv * g.y + b.y;
+    v.z = (t.z - mean) * inv * g.z + b.z;
+    v.w = (t.w - mean) * inv * g.w + b.w;
     const long long elem = (long long)(row0 + rr) * d + c;
     *reinterpret_cast<float4*>(out + elem) = v;
     store_quant4(q, elem, v.x, v.y, v.z, v.w, status);
@@ -161,17 +172,14 @@ __global__ void __launch_bounds__(kLnThreads) residual_ln_kernel(
   extern __shared__ float tile[];  // [kLnRows][d + 1]
   const int row0 = blockIdx.x * kLnRows;
   const int nrows = min(kLnRows, rows - row0);
-  const int vec = d >> 2, ld = d + 1;
+  const int vec = d >> 2, ld = d + 4;
 #pragma unroll 4
   for (int idx = threadIdx.x; idx < nrows * vec; idx += blockDim.x) {
     const int rr = idx / vec, c = (idx % vec) * 4;
     const float4 x = *reinterpret_cast<const float4*>(a + (size_t)(row0 + rr) * lda + c);
     const float4 y = *reinterpret_cast<const float4*>(r + (size_t)(row0 + rr) * ldr + c);
-    float* t = tile + rr * ld + c;
-    t[0] = x.x + y.x;
-    t[1] = x.y + y.y;
-    t[2] = x.z + y.z;
-    t[3] = x.w + y.w;
+    *reinterpret_cast<float4*>(tile + rr * ld + c) =
+        make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
   }
   __syncthreads();
   ln_stats_and_store(tile, nrows, d, row0, gamma, beta, out, q, status);
@@ -187,7 +195,7 @@ __global__ void __launch_bounds__(kLnThreads) ssru_kernel(
   extern __shared__ float tile[];
   const int row0 = blockIdx.x * kLnRows;
   const int nrows = min(kLnRows, rows - row0);
-  const int ld = d + 1;
+  const int ld = d + 4;
 #pragma unroll 4
   for (int idx = threadIdx.x; idx < nrows * d; idx += blockDim.x) {
     const int rr = idx / d, c = idx % d;
@@ -314,52 +322,53 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
   }
 }
 
-// Decode: one CTA per active row, one warp per head.  Each lane scores its
-// own keys with a sequential dot product; one lane sums the exponentials in
-// key order; each lane then accumulates up to four output dimensions over the
-// keys in order.  Cache rows are found through the slot's page table.
-__global__ void attn_decode_kernel(const float* __restrict__ q, int ldq,
-                                   const int32_t* __restrict__ row_slot,
-                                   const int32_t* __restrict__ slot_len, int len_add,
-                                   const int32_t* __restrict__ page_table, int pages_per_slot,
-                                   int page_tokens, const float* __restrict__ k_pool,
-                                   const float* __restrict__ v_pool, int d, int heads,
-                                   int8_t* __restrict__ out_q, float alpha, uint32_t* status) {
+// Decode: one CTA per active row (taken in row_order, longest rows first,
+// so long rows start in the first wave), one warp per head.  Each lane
+// scores its own keys with an in-order dot product; lane 0 sums the
+// exponentials in key order; each lane accumulates output dims 2*lane and
+// 2*lane + 1 over the keys in order, with 16 keys' values fetched ahead.
+// Cache rows come from the slot's page table.
+template <int HD>
+__global__ void __launch_bounds__(256) attn_decode_kernel(
+    const float* __restrict__ q, int ldq, const int32_t* __restrict__ row_slot,
+    const int32_t* __restrict__ row_order, const int32_t* __restrict__ slot_len, int len_add,
+    const int32_t* __restrict__ page_table, int pages_per_slot, int page_tokens,
+    const float* __restrict__ k_pool, const float* __restrict__ v_pool, int d, int heads,
+    int8_t* __restrict__ out_q, float alpha, uint32_t* status) {
   extern __shared__ float sm[];
-  const int r = blockIdx.x;
+  const int r = row_order ? row_order[blockIdx.x] : blockIdx.x;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hd = d / heads;
   const int slot = row_slot[r];
   const int len = slot_len[slot] + len_add;
   if (len <= 0 || len > kMaxSeq || len > pages_per_slot * page_tokens) {
     if (threadIdx.x == 0) flag_status(status, kStatusBadIndex);
     return;
   }
-  float* qw = sm + h * hd;                        // [heads][hd]
-  float* pw = sm + heads * hd + h * kMaxSeq;      // [heads][kMaxSeq]
-  int* rows_s = reinterpret_cast<int*>(sm + heads * hd + heads * kMaxSeq);  // [kMaxSeq]
+  float* qw = sm + h * HD;                        // [heads][HD]
+  float* pw = sm + heads * HD + h * kMaxSeq;      // [heads][kMaxSeq]
+  int* rows_s = reinterpret_cast<int*>(sm + heads * HD + heads * kMaxSeq);  // [kMaxSeq]
   const int32_t* pages = page_table + (size_t)slot * pages_per_slot;
   for (int j = threadIdx.x; j < len; j += blockDim.x)
     rows_s[j] = pages[j / page_tokens] * page_tokens + j % page_tokens;
-  for (int i = lane; i < hd; i += 32) qw[i] = q[(size_t)r * ldq + h * hd + i];
+  for (int i = lane; i < HD; i += 32) qw[i] = q[(size_t)r * ldq + h * HD + i];
   __syncthreads();
-  const float scale = 1.0f / sqrtf((float)hd);
+  const float scale = 1.0f / sqrtf((float)HD);
   float mx = -INFINITY;
-#pragma unroll 2
   for (int j = lane; j < len; j += 32) {
-    const float* kr = k_pool + (size_t)rows_s[j] * d + h * hd;
+    const float* kr = k_pool + (size_t)rows_s[j] * d + h * HD;
     float dot = 0.0f;
-#pragma unroll 16
-    for (int i = 0; i < hd; i += 4) {
+#pragma unroll
+    for (int i = 0; i < HD; i += 4) {
       const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
-      dot = dot + qw[i] * k4.x;
-      dot = dot + qw[i + 1] * k4.y;
-      dot = dot + qw[i + 2] * k4.z;
-      dot = dot + qw[i + 3] * k4.w;
+      const float4 q4 = *reinterpret_cast<const float4*>(qw + i);
+      dot = dot + q4.x * k4.x;
+      dot = dot + q4.y * k4.y;
+      dot = dot + q4.z * k4.z;
+      dot = dot + q4.w * k4.w;
     }
-    const float s = dot * scale;
-    pw[j] = s;
-    mx = fmaxf(mx, s);
+    const float sc = dot * scale;
+    pw[j] = sc;
+    mx = fmaxf(mx, sc);
   }
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   for (int j = lane; j < len; j += 32) pw[j] = exp_f32(pw[j] - mx);
@@ -367,43 +376,42 @@ __global__ void attn_decode_kernel(const float* __restrict__ q, int ldq,
   float inv = 0.0f;
   if (lane == 0) {
     float sum = 0.0f;
-    #pragma unroll 8
+#pragma unroll 8
     for (int j = 0; j < len; ++j) sum = sum + pw[j];
     inv = 1.0f / sum;
   }
   inv = __shfl_sync(0xffffffffu, inv, 0);
   for (int j = lane; j < len; j += 32) pw[j] = pw[j] * inv;
   __syncwarp();
-  // Each lane owns output dims lane and lane + 32 (head width <= 64).  V
-  // values of 16 keys are fetched into registers before the 16 in-order
-  // accumulations, so 32 loads per lane are in flight instead of one.
-  const bool has1 = lane + 32 < hd;
-  const float* vbase = v_pool + h * hd + lane;
+  const bool active = 2 * lane < HD;
+  const float* vbase = v_pool + h * HD + 2 * lane;
   float acc0 = 0.0f, acc1 = 0.0f;
   int j = 0;
   for (; j + 16 <= len; j += 16) {
-    float v0[16], v1[16];
+    float2 v2[16];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const float* vr = vbase + (size_t)rows_s[j + u] * d;
-      v0[u] = vr[0];
-      v1[u] = has1 ? vr[32] : 0.0f;
-    }
+    for (int u = 0; u < 16; ++u)
+      v2[u] = active ? *reinterpret_cast<const float2*>(vbase + (size_t)rows_s[j + u] * d)
+                     : make_float2(0.f, 0.f);
 #pragma unroll
     for (int u = 0; u < 16; ++u) {
       const float p = pw[j + u];
-      acc0 = acc0 + v0[u] * p;
-      acc1 = acc1 + v1[u] * p;
+      acc0 = acc0 + v2[u].x * p;
+      acc1 = acc1 + v2[u].y * p;
     }
   }
   for (; j < len; ++j) {
-    const float* vr = vbase + (size_t)rows_s[j] * d;
+    const float2 v = active ? *reinterpret_cast<const float2*>(vbase + (size_t)rows_s[j] * d)
+                            : make_float2(0.f, 0.f);
     const float p = pw[j];
-    acc0 = acc0 + vr[0] * p;
-    if (has1) acc1 = acc1 + vr[32] * p;
+    acc0 = acc0 + v.x * p;
+    acc1 = acc1 + v.y * p;
   }
-  out_q[(size_t)r * d + h * hd + lane] = quantize_one(acc0, alpha, status);
-  if (has1) out_q[(size_t)r * d + h * hd + lane + 32] = quantize_one(acc1, alpha, status);
+  if (active) {
+    const uint16_t w2 = (uint16_t)(uint8_t)quantize_one(acc0, alpha, status) |
+                        ((uint16_t)(uint8_t)quantize_one(acc1, alpha, status) << 8);
+    *reinterpret_cast<uint16_t*>(out_q + (size_t)r * d + h * HD + 2 * lane) = w2;
+  }
 }
 
 // ---- activation quantization (q8_gemm.rs:569-590) ------------------------------
@@ -496,7 +504,7 @@ void launch_residual_ln(const float* a, int lda, const float* r, int ldr, const 
                         const float* beta, int rows, int d, float* out, const QuantOut& q,
                         uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return;
-  const size_t smem = sizeof(float) * kLnRows * (d + 1);
+  const size_t smem = sizeof(float) * kLnRows * (d + 4);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(residual_ln_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   residual_ln_kernel<<<blocks_for(rows, kLnRows), kLnThreads, smem, s>>>(a, lda, r, ldr, gamma, beta,
@@ -507,7 +515,7 @@ void launch_ssru(const float* cf, int ld, int fcol, float* state, const int32_t*
                  const float* residual, const float* gamma, const float* beta, int rows, int d,
                  float* out, const QuantOut& q, uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return;
-  const size_t smem = sizeof(float) * kLnRows * (d + 1);
+  const size_t smem = sizeof(float) * kLnRows * (d + 4);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(ssru_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   ssru_kernel<<<blocks_for(rows, kLnRows), kLnThreads, smem, s>>>(cf, ld, fcol, state, row_slot, residual,
@@ -546,16 +554,32 @@ cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens,
 }
 
 cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t* row_slot,
-                               const int32_t* slot_len, int len_add, const int32_t* page_table,
-                               int pages_per_slot, int page_tokens, const float* k_pool,
-                               const float* v_pool, int d, int heads, int8_t* out_q, float alpha,
-                               uint32_t* status, cudaStream_t s) {
+                               const int32_t* row_order, const int32_t* slot_len, int len_add,
+                               const int32_t* page_table, int pages_per_slot, int page_tokens,
+                               const float* k_pool, const float* v_pool, int d, int heads,
+                               int8_t* out_q, float alpha, uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
   const int hd = d / heads;
   const size_t smem = sizeof(float) * ((size_t)heads * hd + (size_t)heads * kMaxSeq + kMaxSeq);
-  attn_decode_kernel<<<rows, heads * 32, smem, s>>>(q, ldq, row_slot, slot_len, len_add, page_table,
-                                                    pages_per_slot, page_tokens, k_pool, v_pool, d,
-                                                    heads, out_q, alpha, status);
+  switch (hd) {
+    case 32:
+      attn_decode_kernel<32><<<rows, heads * 32, smem, s>>>(q, ldq, row_slot, row_order, slot_len, len_add,
+                                                           page_table, pages_per_slot, page_tokens, k_pool,
+                                                           v_pool, d, heads, out_q, alpha, status);
+      break;
+    case 48:
+      attn_decode_kernel<48><<<rows, heads * 32, smem, s>>>(q, ldq, row_slot, row_order, slot_len, len_add,
+                                                           page_table, pages_per_slot, page_tokens, k_pool,
+                                                           v_pool, d, heads, out_q, alpha, status);
+      break;
+    case 64:
+      attn_decode_kernel<64><<<rows, heads * 32, smem, s>>>(q, ldq, row_slot, row_order, slot_len, len_add,
+                                                           page_table, pages_per_slot, page_tokens, k_pool,
+                                                           v_pool, d, heads, out_q, alpha, status);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 

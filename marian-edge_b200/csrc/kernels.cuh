@@ -65,11 +65,12 @@ cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens,
 // tensor.rs:251-318 with one query per row over a paged cache: keys of row r
 // are cache rows page_table[slot][j / page_tokens] * page_tokens +
 // j % page_tokens for j < slot_len[slot] + len_add.
+// row_order (nullable) lists the rows in the order CTAs take them.
 cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t* row_slot,
-                               const int32_t* slot_len, int len_add, const int32_t* page_table,
-                               int pages_per_slot, int page_tokens, const float* k_pool,
-                               const float* v_pool, int d, int heads, int8_t* out_q, float alpha,
-                               uint32_t* status, cudaStream_t s);
+                               const int32_t* row_order, const int32_t* slot_len, int len_add,
+                               const int32_t* page_table, int pages_per_slot, int page_tokens,
+                               const float* k_pool, const float* v_pool, int d, int heads,
+                               int8_t* out_q, float alpha, uint32_t* status, cudaStream_t s);
 
 // Turns the packed per-row maxima into tokens (q8_engine.rs:437-449):
 // advances each slot's step/previous token, reports the token and whether
