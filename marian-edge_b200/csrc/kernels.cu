@@ -212,15 +212,18 @@ __global__ void __launch_bounds__(kLnThreads) ssru_kernel(
 }
 
 // ---- attention (attention_into, tensor.rs:251-318) ------------------------------
-// Encoder: one CTA of 8 warps per (sequence, head, 32-query chunk).  K and V
-// of the head are staged in shared memory (K rows padded to HD + 1 floats so
-// the 32 lanes, each scoring a different key, hit different banks).  A warp
-// takes one query at a time: lanes score keys with in-order dot products,
-// lane 0 sums the exponentials in key order, and each lane accumulates two
-// output dimensions over the keys in order -- the reference's operation
-// order throughout.  The host launches one grid per length bucket so shared
-// memory follows the bucket's longest sequence.
+// Encoder: one CTA of 8 warps per (sequence, head, 32-query chunk); each
+// warp owns 4 queries and advances them together, so every dependent chain
+// below has 4 (scores) or 8 (outputs) independent neighbours to overlap with.
+// K and V of the head are staged in shared memory (K rows padded to HD + 4
+// floats: 16-byte aligned with an odd number of 16-byte chunks, so the lanes'
+// 128-bit reads of different keys hit distinct banks).  Per query the
+// operation order is the reference's: in-order dot products, max, exp, a
+// left-to-right sum (lane qq sums query qq), scaling, and a left-to-right
+// weighted sum of V per output dimension.  The host launches one grid per
+// length bucket so shared memory follows the bucket's longest sequence.
 constexpr int kEncWarps = 8;
+constexpr int kEncQpw = 4;  // queries per warp
 
 template <int HD>
 __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
@@ -239,13 +242,11 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
   const int q0 = blockIdx.z * 32;
   if (q0 >= len) return;
   const int ld = 3 * d;
-  // K row stride HD + 4 floats: 16-byte aligned rows whose 4-word index is
-  // odd, so the 8 lanes of each 128-bit shared load phase hit distinct banks.
   constexpr int KLD = HD + 4;
-  float* ks = sm;                                 // [max_len][HD + 4]
-  float* vs = ks + (size_t)max_len * KLD;          // [max_len][HD]
-  float* qs = vs + (size_t)max_len * HD;          // [warps][HD]
-  float* ps = qs + kEncWarps * HD;                // [warps][max_len]
+  float* ks = sm;                                          // [max_len][HD + 4]
+  float* vs = ks + (size_t)max_len * KLD;                   // [max_len][HD]
+  float* qs = vs + (size_t)max_len * HD;                   // [warps][4][HD]
+  float* ps = qs + kEncWarps * kEncQpw * HD;               // [warps][4][max_len]
   constexpr int kVec = HD / 4;
   for (int idx = threadIdx.x; idx < len * kVec; idx += blockDim.x) {
     const int j = idx / kVec, i = (idx % kVec) * 4;
@@ -253,72 +254,97 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
     *reinterpret_cast<float4*>(ks + j * KLD + i) = *reinterpret_cast<const float4*>(row + d);
     *reinterpret_cast<float4*>(vs + j * HD + i) = *reinterpret_cast<const float4*>(row + 2 * d);
   }
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = q0 + warp * kEncQpw;                      // this warp's first query
+  const int nq = max(0, min(kEncQpw, len - qb));
+  float* qw = qs + warp * kEncQpw * HD;
+  float* pw = ps + warp * kEncQpw * max_len;
+  for (int idx = lane; idx < kEncQpw * HD; idx += 32) {
+    const int qq = idx / HD, i = idx % HD;
+    qw[idx] = qq < nq ? qkv[(size_t)(start + qb + qq) * ld + h * HD + i] : 0.0f;
+  }
+  __syncthreads();
+  if (nq == 0) return;
   const float scale = 1.0f / sqrtf((float)HD);
-  float* qw = qs + warp * HD;
-  float* pw = ps + warp * max_len;
-  const int q_end = min(len, q0 + 32);
-  for (int qi = q0 + warp; qi < q_end; qi += kEncWarps) {
-    const float* qrow = qkv + (size_t)(start + qi) * ld + h * HD;
-    for (int i = lane; i < HD; i += 32) qw[i] = qrow[i];
-    __syncwarp();
-    float q[HD];
+  float mx[kEncQpw];
+#pragma unroll
+  for (int qq = 0; qq < kEncQpw; ++qq) mx[qq] = -INFINITY;
+  for (int j = lane; j < len; j += 32) {
+    const float* kr = ks + j * KLD;
+    float dot[kEncQpw];
+#pragma unroll
+    for (int qq = 0; qq < kEncQpw; ++qq) dot[qq] = 0.0f;
 #pragma unroll
     for (int i = 0; i < HD; i += 4) {
-      const float4 v = *reinterpret_cast<const float4*>(qw + i);
-      q[i] = v.x;
-      q[i + 1] = v.y;
-      q[i + 2] = v.z;
-      q[i + 3] = v.w;
-    }
-    float mx = -INFINITY;
-    for (int j = lane; j < len; j += 32) {
-      const float* kr = ks + j * KLD;
-      float dot = 0.0f;
+      const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
 #pragma unroll
-      for (int i = 0; i < HD; i += 4) {
-        const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
-        dot = dot + q[i] * k4.x;
-        dot = dot + q[i + 1] * k4.y;
-        dot = dot + q[i + 2] * k4.z;
-        dot = dot + q[i + 3] * k4.w;
+      for (int qq = 0; qq < kEncQpw; ++qq) {
+        const float4 q4 = *reinterpret_cast<const float4*>(qw + qq * HD + i);
+        float t = dot[qq];
+        t = t + q4.x * k4.x;
+        t = t + q4.y * k4.y;
+        t = t + q4.z * k4.z;
+        t = t + q4.w * k4.w;
+        dot[qq] = t;
       }
-      const float sc = dot * scale;
-      pw[j] = sc;
-      mx = fmaxf(mx, sc);
     }
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    for (int j = lane; j < len; j += 32) pw[j] = exp_f32(pw[j] - mx);
-    __syncwarp();
-    float inv = 0.0f;
-    if (lane == 0) {
-      float sum = 0.0f;
+#pragma unroll
+    for (int qq = 0; qq < kEncQpw; ++qq) {
+      const float sc = dot[qq] * scale;
+      pw[qq * max_len + j] = sc;
+      mx[qq] = fmaxf(mx[qq], sc);
+    }
+  }
+#pragma unroll
+  for (int qq = 0; qq < kEncQpw; ++qq)
+    for (int o = 16; o > 0; o >>= 1) mx[qq] = fmaxf(mx[qq], __shfl_xor_sync(0xffffffffu, mx[qq], o));
+  for (int j = lane; j < len; j += 32) {
+#pragma unroll
+    for (int qq = 0; qq < kEncQpw; ++qq) pw[qq * max_len + j] = exp_f32(pw[qq * max_len + j] - mx[qq]);
+  }
+  __syncwarp();
+  float inv_mine = 0.0f;
+  if (lane < kEncQpw) {  // lane qq sums query qq's exponentials in key order
+    const float* pr = pw + lane * max_len;
+    float sum = 0.0f;
 #pragma unroll 8
-      for (int j = 0; j < len; ++j) sum = sum + pw[j];
-      inv = 1.0f / sum;
+    for (int j = 0; j < len; ++j) sum = sum + pr[j];
+    inv_mine = 1.0f / sum;
+  }
+  float inv[kEncQpw];
+#pragma unroll
+  for (int qq = 0; qq < kEncQpw; ++qq) inv[qq] = __shfl_sync(0xffffffffu, inv_mine, qq);
+  for (int j = lane; j < len; j += 32) {
+#pragma unroll
+    for (int qq = 0; qq < kEncQpw; ++qq) pw[qq * max_len + j] = pw[qq * max_len + j] * inv[qq];
+  }
+  __syncwarp();
+  // lane owns output dims 2*lane and 2*lane + 1 of each of the 4 queries
+  const bool active = 2 * lane < HD;
+  float acc[kEncQpw][2];
+#pragma unroll
+  for (int qq = 0; qq < kEncQpw; ++qq) acc[qq][0] = acc[qq][1] = 0.0f;
+#pragma unroll 4
+  for (int j = 0; j < len; ++j) {
+    const float2 v2 = active ? *reinterpret_cast<const float2*>(vs + j * HD + 2 * lane)
+                             : make_float2(0.f, 0.f);
+#pragma unroll
+    for (int qq = 0; qq < kEncQpw; ++qq) {
+      const float p = pw[qq * max_len + j];
+      acc[qq][0] = acc[qq][0] + v2.x * p;
+      acc[qq][1] = acc[qq][1] + v2.y * p;
     }
-    inv = __shfl_sync(0xffffffffu, inv, 0);
-    for (int j = lane; j < len; j += 32) pw[j] = pw[j] * inv;
-    __syncwarp();
-    // lane owns output dims 2*lane and 2*lane + 1
-    const bool active = 2 * lane < HD;
-    float acc0 = 0.0f, acc1 = 0.0f;
-#pragma unroll 8
-    for (int j = 0; j < len; ++j) {
-      const float p = pw[j];
-      const float2 v2 = active ? *reinterpret_cast<const float2*>(vs + j * HD + 2 * lane)
-                               : make_float2(0.f, 0.f);
-      acc0 = acc0 + v2.x * p;
-      acc1 = acc1 + v2.y * p;
+  }
+  if (active) {
+#pragma unroll
+    for (int qq = 0; qq < kEncQpw; ++qq) {
+      if (qq < nq) {
+        int8_t* o = out_q + (size_t)(start + qb + qq) * d + h * HD + 2 * lane;
+        const uint16_t w2 = (uint16_t)(uint8_t)quantize_one(acc[qq][0], alpha, status) |
+                            ((uint16_t)(uint8_t)quantize_one(acc[qq][1], alpha, status) << 8);
+        *reinterpret_cast<uint16_t*>(o) = w2;
+      }
     }
-    if (active) {
-      int8_t* o = out_q + (size_t)(start + qi) * d + h * HD + 2 * lane;
-      const uint16_t w2 = (uint16_t)(uint8_t)quantize_one(acc0, alpha, status) |
-                          ((uint16_t)(uint8_t)quantize_one(acc1, alpha, status) << 8);
-      *reinterpret_cast<uint16_t*>(o) = w2;
-    }
-    __syncwarp();
   }
 }
 
@@ -527,8 +553,9 @@ cudaError_t launch_attn_encoder_hd(const float* qkv, const int32_t* cu_seqlens,
                                    const int32_t* seq_ids, int n_seqs, int max_len, int d,
                                    int heads, int8_t* out_q, float alpha, uint32_t* status,
                                    cudaStream_t s) {
-  const size_t smem = sizeof(float) * ((size_t)max_len * (2 * HD + 4) + kEncWarps * (size_t)HD +
-                                       kEncWarps * (size_t)max_len);
+  const size_t smem = sizeof(float) * ((size_t)max_len * (2 * HD + 4) +
+                                       (size_t)kEncWarps * kEncQpw * HD +
+                                       (size_t)kEncWarps * kEncQpw * max_len);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(attn_encoder_kernel<HD>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
