@@ -30,6 +30,22 @@ __device__ __forceinline__ void flag_status(uint32_t* status, uint32_t bits) {
   if (status) atomicOr(status, bits);
 }
 
+// ---- programmatic dependent launch ------------------------------------------
+// Every engine kernel is launched with programmatic stream serialization: it
+// may start while its predecessor on the stream is still running, waits in
+// pdl_wait() until that grid has completed and its writes are visible, and
+// then lets its own successor begin launching.  Nothing touches global memory
+// written or read by other kernels before pdl_wait().
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void pdl_enter() {
+  pdl_wait();
+  pdl_trigger();
+}
+
 // ---- mbarrier ---------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
@@ -196,5 +212,23 @@ __device__ __forceinline__ int quantize_rte_clamped(float v, float alpha) {
 __device__ __forceinline__ float dequant(int32_t acc, float scale, float bias) {
   return __fadd_rn(__fmul_rn(__int2float_rn(acc), scale), bias);
 }
+
+#ifdef __CUDACC__
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+#endif
 
 }  // namespace mc

@@ -39,6 +39,7 @@ __global__ void embed_encoder_kernel(const int32_t* __restrict__ tokens,
                                      const int8_t* __restrict__ emb, float emb_mult,
                                      float emb_scale, const float* __restrict__ positions, int d,
                                      float* __restrict__ x, QuantOut q, uint32_t* status) {
+  pdl_enter();
   const int vec_per_row = d >> 2;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)n_tokens * vec_per_row) return;
@@ -67,6 +68,7 @@ __global__ void embed_decoder_kernel(int rows, const int32_t* __restrict__ row_s
                                      float* __restrict__ x, QuantOut q, uint8_t* eos_mask,
                                      const int32_t* __restrict__ self_pages, int pages_per_slot,
                                      int page_tokens, int32_t* self_row_map, uint32_t* status) {
+  pdl_enter();
   const int vec_per_row = d >> 2;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)rows * vec_per_row) return;
@@ -169,6 +171,7 @@ __global__ void __launch_bounds__(kLnThreads) residual_ln_kernel(
     const float* __restrict__ a, int lda, const float* __restrict__ r, int ldr,
     const float* __restrict__ gamma, const float* __restrict__ beta, int rows, int d,
     float* __restrict__ out, QuantOut q, uint32_t* status) {
+  pdl_enter();
   extern __shared__ float tile[];  // [kLnRows][d + 1]
   const int row0 = blockIdx.x * kLnRows;
   const int nrows = min(kLnRows, rows - row0);
@@ -192,6 +195,7 @@ __global__ void __launch_bounds__(kLnThreads) ssru_kernel(
     const int32_t* __restrict__ row_slot, const float* __restrict__ residual,
     const float* __restrict__ gamma, const float* __restrict__ beta, int rows, int d,
     float* __restrict__ out, QuantOut q, uint32_t* status) {
+  pdl_enter();
   extern __shared__ float tile[];
   const int row0 = blockIdx.x * kLnRows;
   const int nrows = min(kLnRows, rows - row0);
@@ -230,6 +234,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
     const float* __restrict__ qkv, const int32_t* __restrict__ cu,
     const int32_t* __restrict__ seq_ids, int d, int max_len, int8_t* __restrict__ out_q,
     float alpha, uint32_t* status) {
+  pdl_enter();
   extern __shared__ float sm[];
   const int b = seq_ids[blockIdx.x];
   const int h = blockIdx.y;
@@ -361,6 +366,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(
     const int32_t* __restrict__ page_table, int pages_per_slot, int page_tokens,
     const float* __restrict__ k_pool, const float* __restrict__ v_pool, int d, int heads,
     int8_t* __restrict__ out_q, float alpha, uint32_t* status) {
+  pdl_enter();
   extern __shared__ float sm[];
   const int r = row_order ? row_order[blockIdx.x] : blockIdx.x;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -443,6 +449,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(
 // ---- activation quantization (q8_gemm.rs:569-590) ------------------------------
 __global__ void quantize_kernel(const float* __restrict__ x, long long n4, float alpha,
                                 int8_t* __restrict__ out, uint32_t* status) {
+  pdl_enter();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n4) return;
   const float4 v = reinterpret_cast<const float4*>(x)[i];
@@ -458,6 +465,7 @@ __global__ void finalize_kernel(int rows, const int32_t* __restrict__ row_slot,
                                 unsigned long long* __restrict__ best, int32_t* slot_prev,
                                 int32_t* slot_step, const int32_t* __restrict__ slot_limit,
                                 int32_t* step_tokens, uint8_t* done, uint32_t* status) {
+  pdl_enter();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rows) return;
   const int slot = row_slot[r];
@@ -481,6 +489,7 @@ __global__ void init_slots_kernel(int n, const int32_t* slots, const int32_t* li
                                   int32_t* slot_step, int32_t* slot_limit, int32_t* slot_force,
                                   int32_t* slot_src, float* ssru_state, int layers, int max_slots,
                                   int d) {
+  pdl_enter();
   const int i = blockIdx.x;
   if (i >= n) return;
   const int s = slots[i];
@@ -509,8 +518,8 @@ void launch_embed_encoder(const int32_t* tokens, const int32_t* pos_idx, int n_t
                           uint32_t* status, cudaStream_t s) {
   if (n_tokens <= 0) return;
   const long long n = (long long)n_tokens * (d / 4);
-  embed_encoder_kernel<<<blocks_for(n, 256), 256, 0, s>>>(tokens, pos_idx, n_tokens, emb, emb_mult,
-                                                          emb_scale, positions, d, x, q, status);
+  launch_pdl(embed_encoder_kernel, blocks_for(n, 256), 256, 0, s, tokens, pos_idx, n_tokens, emb,
+             emb_mult, emb_scale, positions, d, x, q, status);
 }
 
 void launch_embed_decoder(int rows, const int32_t* row_slot, const int32_t* slot_prev,
@@ -521,7 +530,7 @@ void launch_embed_decoder(int rows, const int32_t* row_slot, const int32_t* slot
                           uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return;
   const long long n = (long long)rows * (d / 4);
-  embed_decoder_kernel<<<blocks_for(n, 256), 256, 0, s>>>(
+  launch_pdl(embed_decoder_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, s, 
       rows, row_slot, slot_prev, slot_step, slot_force, emb, emb_mult, emb_scale, positions, d, x,
       q, eos_mask, self_pages, pages_per_slot, page_tokens, self_row_map, status);
 }
@@ -533,7 +542,7 @@ void launch_residual_ln(const float* a, int lda, const float* r, int ldr, const 
   const size_t smem = sizeof(float) * kLnRows * (d + 4);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(residual_ln_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  residual_ln_kernel<<<blocks_for(rows, kLnRows), kLnThreads, smem, s>>>(a, lda, r, ldr, gamma, beta,
+  launch_pdl(residual_ln_kernel, dim3(blocks_for(rows, kLnRows)), dim3(kLnThreads), smem, s, a, lda, r, ldr, gamma, beta,
                                                                          rows, d, out, q, status);
 }
 
@@ -544,7 +553,7 @@ void launch_ssru(const float* cf, int ld, int fcol, float* state, const int32_t*
   const size_t smem = sizeof(float) * kLnRows * (d + 4);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(ssru_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  ssru_kernel<<<blocks_for(rows, kLnRows), kLnThreads, smem, s>>>(cf, ld, fcol, state, row_slot, residual,
+  launch_pdl(ssru_kernel, dim3(blocks_for(rows, kLnRows)), dim3(kLnThreads), smem, s, cf, ld, fcol, state, row_slot, residual,
                                                                   gamma, beta, rows, d, out, q, status);
 }
 
@@ -563,7 +572,7 @@ cudaError_t launch_attn_encoder_hd(const float* qkv, const int32_t* cu_seqlens,
     if (e != cudaSuccess) return e;
   }
   const int chunks = (max_len + 31) / 32;
-  attn_encoder_kernel<HD><<<dim3(n_seqs, heads, chunks), kEncWarps * 32, smem, s>>>(qkv, cu_seqlens, seq_ids, d,
+  launch_pdl(attn_encoder_kernel<HD>, dim3(dim3(n_seqs, heads, chunks)), dim3(kEncWarps * 32), smem, s, qkv, cu_seqlens, seq_ids, d,
                                                                         max_len, out_q, alpha, status);
   return cudaGetLastError();
 }
@@ -590,17 +599,17 @@ cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t*
   const size_t smem = sizeof(float) * ((size_t)heads * hd + (size_t)heads * kMaxSeq + kMaxSeq);
   switch (hd) {
     case 32:
-      attn_decode_kernel<32><<<rows, heads * 32, smem, s>>>(q, ldq, row_slot, row_order, slot_len, len_add,
+      launch_pdl(attn_decode_kernel<32>, dim3(rows), dim3(heads * 32), smem, s, q, ldq, row_slot, row_order, slot_len, len_add,
                                                            page_table, pages_per_slot, page_tokens, k_pool,
                                                            v_pool, d, heads, out_q, alpha, status);
       break;
     case 48:
-      attn_decode_kernel<48><<<rows, heads * 32, smem, s>>>(q, ldq, row_slot, row_order, slot_len, len_add,
+      launch_pdl(attn_decode_kernel<48>, dim3(rows), dim3(heads * 32), smem, s, q, ldq, row_slot, row_order, slot_len, len_add,
                                                            page_table, pages_per_slot, page_tokens, k_pool,
                                                            v_pool, d, heads, out_q, alpha, status);
       break;
     case 64:
-      attn_decode_kernel<64><<<rows, heads * 32, smem, s>>>(q, ldq, row_slot, row_order, slot_len, len_add,
+      launch_pdl(attn_decode_kernel<64>, dim3(rows), dim3(heads * 32), smem, s, q, ldq, row_slot, row_order, slot_len, len_add,
                                                            page_table, pages_per_slot, page_tokens, k_pool,
                                                            v_pool, d, heads, out_q, alpha, status);
       break;
@@ -614,14 +623,14 @@ void launch_quantize(const float* x, long long n, float alpha, int8_t* out, uint
                      cudaStream_t s) {
   if (n <= 0) return;
   const long long n4 = n / 4;
-  quantize_kernel<<<blocks_for(n4, 256), 256, 0, s>>>(x, n4, alpha, out, status);
+  launch_pdl(quantize_kernel, dim3(blocks_for(n4, 256)), dim3(256), 0, s, x, n4, alpha, out, status);
 }
 
 void launch_finalize(int rows, const int32_t* row_slot, unsigned long long* best,
                      int32_t* slot_prev, int32_t* slot_step, const int32_t* slot_limit,
                      int32_t* step_tokens, uint8_t* done, uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return;
-  finalize_kernel<<<blocks_for(rows, 128), 128, 0, s>>>(rows, row_slot, best, slot_prev, slot_step,
+  launch_pdl(finalize_kernel, dim3(blocks_for(rows, 128)), dim3(128), 0, s, rows, row_slot, best, slot_prev, slot_step,
                                                         slot_limit, step_tokens, done, status);
 }
 
@@ -630,7 +639,7 @@ void launch_init_slots(int n, const int32_t* slots, const int32_t* limits, const
                        int32_t* slot_limit, int32_t* slot_force, int32_t* slot_src,
                        float* ssru_state, int layers, int max_slots, int d, cudaStream_t s) {
   if (n <= 0) return;
-  init_slots_kernel<<<n, 128, 0, s>>>(n, slots, limits, force, src_len, slot_prev, slot_step,
+  launch_pdl(init_slots_kernel, dim3(n), dim3(128), 0, s, n, slots, limits, force, src_len, slot_prev, slot_step,
                                       slot_limit, slot_force, slot_src, ssru_state, layers,
                                       max_slots, d);
 }

@@ -280,6 +280,7 @@ __global__ void __launch_bounds__(kThreads, 2) q8_gemm_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_s;
+  pdl_enter();  // set-up above overlaps the previous kernel's tail
 
   if (warp == 0) {
     if (lane == 0) {
@@ -419,7 +420,7 @@ cudaError_t launch_impl(GemmParams p, cudaStream_t stream) {
   }
   const int grid = tiles < num_sms() * ctas_per_sm ? tiles : num_sms() * ctas_per_sm;
   p.stages = stages;
-  kern<<<grid, kThreads, stages * stage_bytes<BN>() + kStagingBytes + 1024, stream>>>(p);
+  launch_pdl(kern, dim3(grid), dim3(kThreads), stages * stage_bytes<BN>() + kStagingBytes + 1024, stream, p);
   return cudaGetLastError();
 }
 
