@@ -194,6 +194,21 @@ def run_reference(args):
 
 
 # ---- CUDA arm --------------------------------------------------------------------
+def reduce_job(tokens, dev_ms, wall_s, world, device):
+    """Whole-job totals over the ranks: tokens summed, device time and wall
+    time as the max over ranks (the job ends when its slowest rank does)."""
+    if world == 1:
+        return float(tokens), float(dev_ms), float(wall_s)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(tokens)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    m = torch.tensor([float(dev_ms), float(wall_s)], dtype=torch.float64, device=device)
+    dist.all_reduce(m, op=dist.ReduceOp.MAX)
+    return float(t.item()), float(m[0].item()), float(m[1].item())
+
+
+
 # DRAM traffic per algorithmic byte, from one ncu --set full capture of each
 # kernel class on the benchmark stream (2,048-request run, steady-state
 # launch; dram__bytes_read.sum + dram__bytes_write.sum divided by the
@@ -234,19 +249,6 @@ def run_cuda(args):
         if world > 1:
             dist.barrier()
 
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def sum_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
 
     model_bytes = W.synthetic_model(W.SHAPES[args.model], seed=0)
     eng = CudaEngine(model_bytes, device=local, max_inflight=args.max_inflight, max_encode_tokens=65536)
@@ -295,9 +297,7 @@ def run_cuda(args):
     barrier()
     launches = lib.mc_launch_count(eng.handle) - launches0
     dev_ms = start.elapsed_time(end)
-    max_ms = max_over_ranks(dev_ms)
-    max_wall = max_over_ranks(wall)
-    all_tokens = sum_over_ranks(float(tokens))
+    all_tokens, max_ms, max_wall = reduce_job(tokens, dev_ms, wall, world, "cuda")
 
     latency = None
     if not args.no_latency and rank == 0:
