@@ -145,3 +145,63 @@ def test_zero_output_budget_returns_empty_rows():
         out, off = eng.translate_token_ids(np.array([4, 5, 0, 6, 0], np.int32), np.array([0, 3, 5], np.uint32),
                                            np.array([0, 3], np.uint32))
         assert off[1] == 0 and off[2] >= 1
+
+
+@pytest.mark.parametrize("name", ["tiny_ssru", "tiny_self"])
+def test_batch_and_single_translations_are_identical(name):
+    # The reference's batch-vs-single invariance golden (crates/marian-cpu/
+    # tests/q8_golden.rs): a sentence translates the same alone or in a batch.
+    batch = W.short_batch(n=6, vocab=512, seed=21, lo=3, hi=40)
+    with CudaEngine(model(name), max_inflight=16, max_encode_tokens=1024) as eng:
+        got, off = eng.translate_token_ids(batch.tokens, batch.offsets, batch.max_out, batch.force_len)
+        for b in range(batch.size):
+            s, e = batch.offsets[b], batch.offsets[b + 1]
+            one, one_off = eng.translate_token_ids(batch.tokens[s:e], np.array([0, e - s], np.uint32),
+                                                   batch.max_out[b:b + 1], batch.force_len[b:b + 1])
+            np.testing.assert_array_equal(one, got[off[b]:off[b + 1]])
+
+
+def test_ssru_state_is_reset_when_slots_are_reused():
+    # 2 slots for 7 requests: every slot is reused; SSRU states must start
+    # from zero for each new request (q8_engine.rs:360-362).
+    name = "tiny_ssru"
+    batch = W.short_batch(n=7, vocab=512, seed=33, lo=4, hi=20)
+    om = O.OracleModel(model(name))
+    ref, ref_off = om.translate(batch.tokens, batch.offsets, batch.max_out, batch.force_len)
+    with CudaEngine(model(name), max_inflight=2, max_encode_tokens=256) as eng:
+        got, got_off = eng.translate_token_ids(batch.tokens, batch.offsets, batch.max_out, batch.force_len)
+    np.testing.assert_array_equal(got_off, ref_off)
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_longest_sources_and_repeated_calls():
+    # 256-token sources (the maximum) next to 1-token ones, translated twice
+    # on the same engine: identical results, matching the oracle.
+    name = "tiny_self"
+    rng = np.random.default_rng(5)
+    srcs = [W.zipf_ids(rng, 255, 512), np.zeros(0, np.int32), W.zipf_ids(rng, 100, 512)]
+    batch = W.pack(srcs)
+    om = O.OracleModel(model(name))
+    # the oracle keeps the reference's CPU cap (batch * Lmax^2 <= 65,536), so
+    # it translates the rows one by one (batch invariance makes that equal)
+    parts = [om.translate(*[x for x in (sb.tokens, sb.offsets, sb.max_out, sb.force_len)])
+             for sb in (W.subset(batch, [b]) for b in range(batch.size))]
+    ref = np.concatenate([p[0] for p in parts])
+    ref_off = np.concatenate([[0], np.cumsum([p[1][-1] for p in parts])]).astype(np.uint32)
+    with CudaEngine(model(name), max_inflight=8, max_encode_tokens=1024) as eng:
+        for _ in range(2):
+            got, got_off = eng.translate_token_ids(batch.tokens, batch.offsets, batch.max_out, batch.force_len)
+            np.testing.assert_array_equal(got_off, ref_off)
+            np.testing.assert_array_equal(got, ref)
+
+
+def test_ssru_reference_limits_without_forced_length():
+    name = "tiny_ssru"
+    batch = W.short_batch(n=6, vocab=512, seed=8, lo=2, hi=12)
+    mo = np.array([3, 600, 1, 9, 256, 40], np.uint32)
+    om = O.OracleModel(model(name))
+    ref, ref_off = om.translate(batch.tokens, batch.offsets, mo, None)
+    with CudaEngine(model(name), max_inflight=16, max_encode_tokens=1024) as eng:
+        got, got_off = eng.translate_token_ids(batch.tokens, batch.offsets, mo)
+    np.testing.assert_array_equal(got_off, ref_off)
+    np.testing.assert_array_equal(got, ref)
