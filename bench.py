@@ -47,6 +47,7 @@ def parse():
     p.add_argument("--model", default="graph_b", choices=list(W.SHAPES))
     p.add_argument("--requests", type=int, default=20000, help="requests per step per GPU")
     p.add_argument("--max-inflight", type=int, default=1024)
+    p.add_argument("--lanes", type=int, default=0, help="decode lanes (0: library default)")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-latency", action="store_true")
@@ -251,7 +252,8 @@ def run_cuda(args):
 
 
     model_bytes = W.synthetic_model(W.SHAPES[args.model], seed=0)
-    eng = CudaEngine(model_bytes, device=local, max_inflight=args.max_inflight, max_encode_tokens=65536)
+    eng = CudaEngine(model_bytes, device=local, max_inflight=args.max_inflight, max_encode_tokens=65536,
+                     lanes=args.lanes)
     lib = L.load()
     stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
     warm = step_batches(args, rank, max(1, args.warmup), 100)

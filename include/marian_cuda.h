@@ -60,6 +60,9 @@ typedef struct {
     uint32_t page_tokens;        /* tokens per KV-cache page (default 16) */
     uint32_t kv_pages;           /* pages per cache pool; 0 = enough for every slot at full length */
     uint32_t max_length_factor;  /* Architecture::max_length_factor, 1..8 (default 3) */
+    uint32_t lanes;              /* concurrent decode lanes, 1..8 (default 1; 0 = default):
+                                    the active rows are split over this many CUDA streams
+                                    whose decode steps overlap on the GPU */
 } mc_config;
 
 typedef struct {
@@ -106,11 +109,17 @@ mc_status mc_translate_token_ids(mc_engine *e, const int32_t *tokens, size_t n_t
                                  int32_t *out_tokens, size_t out_capacity,
                                  uint32_t *out_offsets);
 
-/* Continuous batching.  mc_submit queues one request (tokens end in EOS);
- * mc_step admits queued requests into free decode slots (one packed encoder
- * pass) and runs one decode step over every active slot; mc_poll returns
- * finished requests: ids[i], lengths[i] and their tokens packed in order
- * into tokens (capacity token_capacity). */
+/* Continuous batching.  mc_submit queues one request (tokens end in EOS).
+ * mc_step advances every decode lane by one step: it waits for the lane's
+ * step in flight (if any) and applies its tokens, admits queued requests
+ * into the lane's free slots (one packed encoder pass), and launches the
+ * lane's next decode step over its active slots without waiting for it; so
+ * a lane's tokens become visible one mc_step call after its step was
+ * launched.  active_after counts the active slots of every lane, including
+ * those of steps still in flight.  mc_poll returns finished requests:
+ * ids[i], lengths[i] and their tokens packed in order into tokens (capacity
+ * token_capacity).  Call mc_step until active_after and queued_after are
+ * both 0 to drain every request. */
 mc_status mc_submit(mc_engine *e, uint64_t request_id, const int32_t *tokens, uint32_t n_tokens,
                     uint32_t max_output_tokens, uint32_t force_len);
 mc_status mc_step(mc_engine *e, uint32_t *active_after, uint32_t *queued_after);

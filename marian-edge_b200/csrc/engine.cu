@@ -2,14 +2,21 @@
 // paged cross/self caches, and a continuous-batching greedy decoder.
 //
 // Control flow restated from Q8CpuEngine::translate_token_ids
-// (crates/marian-cpu/src/q8_engine.rs:353-466) with three B200 changes:
+// (crates/marian-cpu/src/q8_engine.rs:353-466) with four B200 changes:
 //   * sources are packed without padding (cu_seqlens) instead of [B, Lmax];
 //   * cross keys/values and (for the self-attention decoder) self
 //     keys/values live in pools of fixed-size pages addressed through
 //     per-slot page tables;
 //   * decode rows are the active slots only: finished rows retire at once and
 //     queued requests are admitted into free slots between steps
-//     (the reference keeps computing finished rows, q8_engine.rs:438-441).
+//     (the reference keeps computing finished rows, q8_engine.rs:438-441);
+//   * the active rows are split over lanes: each lane has its own CUDA
+//     stream, activation buffers and decode step (replayed from a CUDA graph
+//     captured once per lane), and the host completes one lane's step and
+//     relaunches it while the other lanes' steps run, so the latency-bound
+//     kernels of several steps overlap on the GPU.  Weights, slots, page
+//     pools and page tables are shared; lanes use disjoint slots and pages.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -29,6 +36,7 @@ namespace {
 using namespace mc;
 
 constexpr int kBNs[3] = {64, 128, 256};
+constexpr int kMaxLanes = 8;
 
 int bn_index(int bn) { return bn == 64 ? 0 : (bn == 128 ? 1 : 2); }
 
@@ -76,6 +84,65 @@ struct Finished {
   std::vector<int32_t> tokens;
 };
 
+// Per-kernel-class timing (mc_profile): CUDA event pairs on a lane's stream
+// around each launch, harvested after the lane's step is complete.
+struct ProfRec {
+  int kind;
+  double flops, bytes;
+  cudaEvent_t a, b;
+};
+
+// One lane: a stream, the activation buffers of an encoder pass and of a
+// decode step, and the rows (slots) whose step runs on it.
+struct Lane {
+  int id = 0;
+  int cap = 0;                       // scheduling limit on active rows
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  uint32_t* d_status = nullptr;      // error bits of this lane's kernels
+  uint32_t* h_status = nullptr;      // pinned
+
+  // encoder pass (capacity tmax packed tokens)
+  float *enc_x = nullptr, *enc_x1 = nullptr, *enc_qkv = nullptr, *enc_proj = nullptr;
+  QBuf enc_q[kMaxQuantOut];
+  QBuf enc_o, enc_h;
+  // admission block, pinned on the host and mirrored on the device:
+  // tokens[T] pos[T] cross_rows[T] cu[B+1] slots[B] limits[B] force[B]
+  // src[B] seq_ids[B] page_rows[2][B][pages_per_slot]
+  int32_t* adm_h = nullptr;
+  int32_t* adm_d = nullptr;
+  size_t adm_cap = 0;  // int32 entries
+  struct Bucket {
+    int offset, count, max_len;
+  };
+  std::vector<Bucket> buckets;
+
+  // decode step (capacity rmax rows)
+  float *dec_a = nullptr, *dec_b = nullptr, *dec_qkv = nullptr, *dec_proj = nullptr;
+  QBuf dec_q[kMaxQuantOut];
+  QBuf dec_o, dec_h;
+  // rows block [4 + 3 * rmax]: row count, pad, then row slots, self-attention
+  // row order and cross-attention row order (longest first), rmax each
+  int32_t* rows_h = nullptr;  // pinned
+  int32_t* rows_d = nullptr;
+  int32_t *self_row_map = nullptr, *step_tokens = nullptr;
+  uint8_t *eos_mask = nullptr, *done = nullptr;
+  unsigned long long* best = nullptr;
+  int32_t* h_step_tokens = nullptr;  // pinned
+  uint8_t* h_done = nullptr;         // pinned
+
+  std::vector<int32_t> active;  // slots in row order
+  int launched = 0;             // rows of the step in flight (0: none)
+  float* last_state = nullptr;  // final decoder state of the last step
+  int eager_steps = 0;
+  cudaGraphExec_t graph = nullptr;  // decode step for up to `cap` rows
+  bool graph_tried = false;
+  uint64_t graph_kernels = 0;
+  std::vector<ProfRec> prof_pending;
+
+  int32_t* row_slot() const { return rows_d + 4; }
+};
+
 }  // namespace
 
 struct mc_engine {
@@ -83,8 +150,7 @@ struct mc_engine {
   std::string error;
   bool ready = true;
   bool loaded = false;
-  cudaStream_t stream = nullptr;
-  uint32_t* d_status = nullptr;
+  cudaStream_t stream = nullptr;  // load stream; lane 0 runs on it
   HostModel host;  // dims; tensor payloads are released after upload
   int d = 0, heads = 0, ffn = 0, enc_layers = 0, dec_layers = 0, kind = 0, vsrc = 0, vtgt = 0;
   float emb_scale = 1.0f;
@@ -103,67 +169,29 @@ struct mc_engine {
   std::vector<DevFfn> enc_ffn, dec_ffn;
   std::vector<DevSsru> dec_ssru;
 
-  // encoder buffers (capacity tmax packed tokens)
-  int tmax = 0;
-  float *enc_x = nullptr, *enc_x1 = nullptr, *enc_qkv = nullptr, *enc_proj = nullptr;
-  QBuf enc_q[kMaxQuantOut];
-  QBuf enc_o, enc_h;
-  int32_t *enc_tokens = nullptr, *enc_pos = nullptr, *enc_cu = nullptr, *enc_cross_rows = nullptr;
-  int32_t* enc_seq_ids = nullptr;  // admitted sequences grouped by length bucket
-  struct Bucket {
-    int offset, count, max_len;
-  };
-  std::vector<Bucket> buckets;
+  int tmax = 0;  // packed tokens per encoder pass
+  int rmax = 0;  // slots
 
-  // decoder buffers (capacity rmax rows = slots)
-  int rmax = 0;
-  float *dec_a = nullptr, *dec_b = nullptr, *dec_qkv = nullptr, *dec_proj = nullptr;
-  QBuf dec_q[kMaxQuantOut];
-  QBuf dec_o, dec_h;
-  int32_t *row_slot = nullptr, *self_row_map = nullptr, *step_tokens = nullptr;
-  int32_t *order_self = nullptr, *order_cross = nullptr;  // rows, longest keys first
-  uint8_t *eos_mask = nullptr, *done = nullptr;
-  unsigned long long* best = nullptr;
-
-  // slots and caches
+  // slots and caches (shared by the lanes)
   int32_t *slot_prev = nullptr, *slot_step = nullptr, *slot_limit = nullptr, *slot_force = nullptr,
           *slot_src = nullptr;
   float* ssru_state = nullptr;
   int pages_per_slot = 0, page_tokens = 16;
   int cross_pool_pages = 0, self_pool_pages = 0;
   int32_t *cross_pages_d = nullptr, *self_pages_d = nullptr;
-  std::vector<int32_t> cross_pages_h, self_pages_h;
   std::vector<float*> cross_k, cross_v, self_k, self_v;
   std::vector<int32_t> free_cross, free_self, free_slots;
-  bool pages_dirty = true;
 
-  // pinned staging
-  int32_t* h_i32 = nullptr;  // staging for uploads
-  size_t h_i32_cap = 0;
-  int32_t* h_step_tokens = nullptr;
-  uint8_t* h_done = nullptr;
-  uint32_t* h_status = nullptr;
+  std::vector<Lane> lanes;
+  bool use_graphs = true;
 
   // scheduler
   std::deque<Request*> queue;
-  std::vector<Request*> slot_req;    // [rmax]
-  std::vector<int32_t> active;       // slots in row order
+  std::vector<Request*> slot_req;  // [rmax]
   std::vector<Finished> finished;
   uint64_t steps = 0, launches = 0;
-  float* last_state = nullptr;  // final decoder state buffer of the last step
 
-  // admission staging on the device
-  int32_t *adm_slots = nullptr, *adm_limits = nullptr, *adm_force = nullptr, *adm_src = nullptr;
-
-  // optional per-kernel-class timing (mc_profile): CUDA event pairs on the
-  // engine stream around each launch, harvested after each synchronization
-  struct ProfRec {
-    int kind;
-    double flops, bytes;
-    cudaEvent_t a, b;
-  };
   bool profiling = false;
-  std::vector<ProfRec> prof_pending;
   std::vector<cudaEvent_t> event_pool;
   double prof_ms[MC_KERNEL_KINDS] = {}, prof_flops[MC_KERNEL_KINDS] = {}, prof_bytes[MC_KERNEL_KINDS] = {};
   uint64_t prof_n[MC_KERNEL_KINDS] = {};
@@ -190,7 +218,7 @@ mc_status fail_cuda(mc_engine* e, const char* what, cudaError_t err) {
   return MC_CUDA;
 }
 
-int prof_begin(mc_engine* e, int kind, double flops, double bytes) {
+int prof_begin(mc_engine* e, Lane& L, int kind, double flops, double bytes) {
   if (!e->profiling) return -1;
   auto ev = [&]() {
     cudaEvent_t x;
@@ -202,19 +230,19 @@ int prof_begin(mc_engine* e, int kind, double flops, double bytes) {
     }
     return x;
   };
-  mc_engine::ProfRec r{kind, flops, bytes, ev(), ev()};
-  cudaEventRecord(r.a, e->stream);
-  e->prof_pending.push_back(r);
-  return (int)e->prof_pending.size() - 1;
+  ProfRec r{kind, flops, bytes, ev(), ev()};
+  cudaEventRecord(r.a, L.stream);
+  L.prof_pending.push_back(r);
+  return (int)L.prof_pending.size() - 1;
 }
 
-void prof_end(mc_engine* e, int idx) {
-  if (idx >= 0) cudaEventRecord(e->prof_pending[idx].b, e->stream);
+void prof_end(Lane& L, int idx) {
+  if (idx >= 0) cudaEventRecord(L.prof_pending[idx].b, L.stream);
 }
 
-// Call after the engine stream is synchronized.
-void prof_harvest(mc_engine* e) {
-  for (auto& r : e->prof_pending) {
+// Call after the lane's stream is synchronized.
+void prof_harvest(mc_engine* e, Lane& L) {
+  for (auto& r : L.prof_pending) {
     float ms = 0.0f;
     if (cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) {
       e->prof_ms[r.kind] += ms;
@@ -225,14 +253,14 @@ void prof_harvest(mc_engine* e) {
     e->event_pool.push_back(r.a);
     e->event_pool.push_back(r.b);
   }
-  e->prof_pending.clear();
+  L.prof_pending.clear();
 }
 
-#define PROFILED(kind, flops, bytes, stmt)                     \
-  do {                                                         \
-    const int pi_ = prof_begin(e, (kind), (flops), (bytes));   \
-    stmt;                                                      \
-    prof_end(e, pi_);                                          \
+#define PROFILED(kind, flops, bytes, stmt)                        \
+  do {                                                            \
+    const int pi_ = prof_begin(e, L, (kind), (flops), (bytes));   \
+    stmt;                                                         \
+    prof_end(L, pi_);                                             \
   } while (0)
 
 template <class T>
@@ -247,7 +275,7 @@ cudaError_t dalloc(mc_engine* e, T** p, size_t count) {
   return r;
 }
 
-// Host-to-device copy on the engine stream (ordered after dalloc's memset),
+// Host-to-device copy on the load stream (ordered after dalloc's memset),
 // synchronous because the source is usually a temporary.
 cudaError_t h2d(mc_engine* e, void* dst, const void* src, size_t bytes) {
   cudaError_t r = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, e->stream);
@@ -344,8 +372,12 @@ struct GroupSpec {
   float alpha;  // next linear's alpha (kEpiQ8)
 };
 
-mc_status gemm(mc_engine* e, int kind, int m, const GroupSpec* specs, int n_groups,
-               unsigned long long* argmax = nullptr, const uint8_t* eos = nullptr) {
+// One grouped GEMM launch on the lane's stream.  m is the row capacity the
+// grid is sized for; m_dev (nullable) is the device row count the kernel
+// reads.  flops/bytes for the profile use m_prof rows.
+mc_status gemm(mc_engine* e, Lane& L, int kind, int m, const int32_t* m_dev, double m_prof,
+               const GroupSpec* specs, int n_groups, unsigned long long* argmax = nullptr,
+               const uint8_t* eos = nullptr) {
   if (m <= 0) return MC_OK;
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
@@ -373,20 +405,21 @@ mc_status gemm(mc_engine* e, int kind, int m, const GroupSpec* specs, int n_grou
     g.eos_mask = eos;
   }
   p.m = m;
+  p.m_dev = m_dev;
   p.k = specs[0].w->in;
   p.num_groups = n_groups;
   p.max_n = max_n;
-  p.status = e->d_status;
+  p.status = L.d_status;
   double flops = 0, bytes = 0;
   for (int i = 0; i < n_groups; ++i) {
     const double n = specs[i].w->out, k = specs[i].w->in;
-    flops += 2.0 * m * n * k;
-    const double out_bytes = specs[i].mode == kEpiArgmax ? 8.0 * m
-                             : specs[i].mode == kEpiQ8   ? 1.0 * m * n
-                                                         : 4.0 * m * n;
-    bytes += (double)m * k + n * k + 4.0 * n * (specs[i].w->bias ? 2 : 1) + out_bytes;
+    flops += 2.0 * m_prof * n * k;
+    const double out_bytes = specs[i].mode == kEpiArgmax ? 8.0 * m_prof
+                             : specs[i].mode == kEpiQ8   ? 1.0 * m_prof * n
+                                                         : 4.0 * m_prof * n;
+    bytes += m_prof * k + n * k + 4.0 * n * (specs[i].w->bias ? 2 : 1) + out_bytes;
   }
-  PROFILED(kind, flops, bytes, CK(launch_q8_gemm(p, bn, e->stream)));
+  PROFILED(kind, flops, bytes, CK(launch_q8_gemm(p, bn, L.stream)));
   ++e->launches;
   return MC_OK;
 }
@@ -432,82 +465,120 @@ std::vector<float> dec_input_alphas(mc_engine* e, int layer) {
   return {a.wq.alpha, a.wk.alpha, a.wv.alpha};
 }
 
+// Device pointers of one admission block (see Lane::adm_h).
+struct AdmLayout {
+  int T = 0, B = 0;
+  size_t tok = 0, pos = 0, crow = 0, cu = 0, slots = 0, lims = 0, force = 0, src = 0, seq_ids = 0,
+         pages = 0, end = 0;
+};
+
+AdmLayout adm_layout(int T, int B, int pps) {
+  AdmLayout a;
+  a.T = T;
+  a.B = B;
+  a.tok = 0;
+  a.pos = a.tok + T;
+  a.crow = a.pos + T;
+  a.cu = a.crow + T;
+  a.slots = a.cu + B + 1;
+  a.lims = a.slots + B;
+  a.force = a.lims + B;
+  a.src = a.force + B;
+  a.seq_ids = a.src + B;
+  a.pages = a.seq_ids + B;
+  a.end = a.pages + (size_t)2 * B * pps;
+  return a;
+}
+
 // ---- encoder pass over packed admitted sources ------------------------------
-mc_status run_encoder(mc_engine* e, int T, int batch, int max_len, double sum_len_sq) {
+mc_status run_encoder(mc_engine* e, Lane& L, const AdmLayout& A, double sum_len_sq) {
   const int d = e->d;
+  const int T = A.T;
+  const int32_t* adm = L.adm_d;
   const double rows_d = (double)T * d;
   PROFILED(MC_K_EMBED, 0.0, rows_d * (1 + 4 + 4 + 3),
-           launch_embed_encoder(e->enc_tokens, e->enc_pos, T, e->enc_emb, e->enc_emb_mult,
-                                e->emb_scale, e->positions, d, e->enc_x,
-                                quant_out_vec(e->enc_q, enc_input_alphas(e, 0)), e->d_status,
-                                e->stream));
+           launch_embed_encoder(adm + A.tok, adm + A.pos, T, e->enc_emb, e->enc_emb_mult,
+                                e->emb_scale, e->positions, d, L.enc_x,
+                                quant_out_vec(L.enc_q, enc_input_alphas(e, 0)), L.d_status,
+                                L.stream));
   ++e->launches;
   mc_status st;
   for (int l = 0; l < e->enc_layers; ++l) {
     const DevAttention& a = e->enc_attn[l];
     const DevFfn& f = e->enc_ffn[l];
     GroupSpec qkv[3] = {
-        {&e->enc_q[0], &a.wq, kEpiF32, e->enc_qkv, 3 * d, 0, nullptr, false, 0.f},
-        {&e->enc_q[1], &a.wk, kEpiF32, e->enc_qkv, 3 * d, d, nullptr, false, 0.f},
-        {&e->enc_q[2], &a.wv, kEpiF32, e->enc_qkv, 3 * d, 2 * d, nullptr, false, 0.f}};
-    if ((st = gemm(e, MC_K_GEMM_QKV, T, qkv, 3))) return st;
+        {&L.enc_q[0], &a.wq, kEpiF32, L.enc_qkv, 3 * d, 0, nullptr, false, 0.f},
+        {&L.enc_q[1], &a.wk, kEpiF32, L.enc_qkv, 3 * d, d, nullptr, false, 0.f},
+        {&L.enc_q[2], &a.wv, kEpiF32, L.enc_qkv, 3 * d, 2 * d, nullptr, false, 0.f}};
+    if ((st = gemm(e, L, MC_K_GEMM_QKV, T, nullptr, T, qkv, 3))) return st;
     PROFILED(MC_K_ATTN_ENC, 4.0 * sum_len_sq * d, rows_d * (12 + 1), {
-      for (const auto& bk : e->buckets)
-        CK(launch_attn_encoder(e->enc_qkv, e->enc_cu, e->enc_seq_ids + bk.offset, bk.count,
-                               bk.max_len, d, e->heads, e->enc_o.p, a.wo.alpha, e->d_status,
-                               e->stream));
+      for (const auto& bk : L.buckets)
+        CK(launch_attn_encoder(L.enc_qkv, adm + A.cu, adm + A.seq_ids + bk.offset, bk.count,
+                               bk.max_len, d, e->heads, L.enc_o.p, a.wo.alpha, L.d_status,
+                               L.stream));
     });
-    ++e->launches;
-    GroupSpec wo = {&e->enc_o, &a.wo, kEpiF32, e->enc_proj, d, 0, nullptr, false, 0.f};
-    if ((st = gemm(e, MC_K_GEMM_OUT, T, &wo, 1))) return st;
+    e->launches += L.buckets.size();
+    GroupSpec wo = {&L.enc_o, &a.wo, kEpiF32, L.enc_proj, d, 0, nullptr, false, 0.f};
+    if ((st = gemm(e, L, MC_K_GEMM_OUT, T, nullptr, T, &wo, 1))) return st;
     PROFILED(MC_K_LAYERNORM, 0.0, rows_d * 13,
-             launch_residual_ln(e->enc_proj, d, e->enc_x, d, a.ln_g, a.ln_b, T, d, e->enc_x1,
-                                quant_out(e->enc_q, {f.w1.alpha}), e->d_status, e->stream));
-    GroupSpec w1 = {&e->enc_q[0], &f.w1, kEpiQ8, e->enc_h.p, e->ffn, 0, nullptr, true, f.w2.alpha};
-    if ((st = gemm(e, MC_K_GEMM_FFN1, T, &w1, 1))) return st;
-    GroupSpec w2 = {&e->enc_h, &f.w2, kEpiF32, e->enc_proj, d, 0, nullptr, false, 0.f};
-    if ((st = gemm(e, MC_K_GEMM_FFN2, T, &w2, 1))) return st;
+             launch_residual_ln(L.enc_proj, d, L.enc_x, d, a.ln_g, a.ln_b, T, nullptr, d, L.enc_x1,
+                                quant_out(L.enc_q, {f.w1.alpha}), L.d_status, L.stream));
+    GroupSpec w1 = {&L.enc_q[0], &f.w1, kEpiQ8, L.enc_h.p, e->ffn, 0, nullptr, true, f.w2.alpha};
+    if ((st = gemm(e, L, MC_K_GEMM_FFN1, T, nullptr, T, &w1, 1))) return st;
+    GroupSpec w2 = {&L.enc_h, &f.w2, kEpiF32, L.enc_proj, d, 0, nullptr, false, 0.f};
+    if ((st = gemm(e, L, MC_K_GEMM_FFN2, T, nullptr, T, &w2, 1))) return st;
     PROFILED(MC_K_LAYERNORM, 0.0, rows_d * (12 + enc_input_alphas(e, l + 1).size()),
-             launch_residual_ln(e->enc_proj, d, e->enc_x1, d, f.ln_g, f.ln_b, T, d, e->enc_x,
-                                quant_out_vec(e->enc_q, enc_input_alphas(e, l + 1)), e->d_status,
-                                e->stream));
+             launch_residual_ln(L.enc_proj, d, L.enc_x1, d, f.ln_g, f.ln_b, T, nullptr, d, L.enc_x,
+                                quant_out_vec(L.enc_q, enc_input_alphas(e, l + 1)), L.d_status,
+                                L.stream));
     e->launches += 2;
   }
   // cross keys/values of every decoder layer into the paged pools
   // (q8_engine.rs:560-567)
   std::vector<GroupSpec> cross;
   for (int l = 0; l < e->dec_layers; ++l) {
-    cross.push_back({&e->enc_q[2 * l], &e->dec_ctx[l].wk, kEpiF32, e->cross_k[l], d, 0,
-                     e->enc_cross_rows, false, 0.f});
-    cross.push_back({&e->enc_q[2 * l + 1], &e->dec_ctx[l].wv, kEpiF32, e->cross_v[l], d, 0,
-                     e->enc_cross_rows, false, 0.f});
+    cross.push_back({&L.enc_q[2 * l], &e->dec_ctx[l].wk, kEpiF32, e->cross_k[l], d, 0,
+                     adm + A.crow, false, 0.f});
+    cross.push_back({&L.enc_q[2 * l + 1], &e->dec_ctx[l].wv, kEpiF32, e->cross_v[l], d, 0,
+                     adm + A.crow, false, 0.f});
   }
   for (size_t i = 0; i < cross.size(); i += kMaxGemmGroups)
-    if ((st = gemm(e, MC_K_GEMM_CROSSKV, T, cross.data() + i, (int)std::min<size_t>(kMaxGemmGroups, cross.size() - i))))
+    if ((st = gemm(e, L, MC_K_GEMM_CROSSKV, T, nullptr, T, cross.data() + i,
+                   (int)std::min<size_t>(kMaxGemmGroups, cross.size() - i))))
       return st;
   return MC_OK;
 }
 
-// ---- one decode step over the active rows --------------------------------------
-mc_status run_decode_step(mc_engine* e, int R) {
+// ---- one decode step over a lane's active rows -------------------------------
+// Grids cover `cap` rows; the kernels read the step's row count from the
+// lane's rows block (rows_d[0]), so the same launches serve any row count up
+// to cap and can be replayed from a CUDA graph.
+mc_status run_decode_step(mc_engine* e, Lane& L, int cap) {
   const int d = e->d;
-  float* x = e->dec_a;   // layer input
-  float* y = e->dec_b;   // next
+  float* x = L.dec_a;   // layer input
+  float* y = L.dec_b;   // next
+  const int32_t* nrows = L.rows_d;
+  const int32_t* row_slot = L.row_slot();
+  const int32_t* order_self = row_slot + e->rmax;
+  const int32_t* order_cross = order_self + e->rmax;
   // key counts for the attention roofline: self = step + 1, cross = source
   double self_keys = 0, cross_keys = 0;
-  for (int s : e->active) {
-    const Request* q = e->slot_req[s];
-    if (!q) continue;
-    self_keys += (double)q->output.size() + 1;
-    cross_keys += (double)q->tokens.size();
+  if (e->profiling) {
+    for (int s : L.active) {
+      const Request* q = e->slot_req[s];
+      if (!q) continue;
+      self_keys += (double)q->output.size() + 1;
+      cross_keys += (double)q->tokens.size();
+    }
   }
-  const double rows_d = (double)R * d;
+  const double R = (double)L.active.size();
+  const double rows_d = R * d;
   PROFILED(MC_K_EMBED, 0.0, rows_d * (1 + 4 + 4 + 3),
-           launch_embed_decoder(R, e->row_slot, e->slot_prev, e->slot_step, e->slot_force,
+           launch_embed_decoder(cap, nrows, row_slot, e->slot_prev, e->slot_step, e->slot_force,
                                 e->dec_emb, e->dec_emb_mult, e->emb_scale, e->positions, d, x,
-                                quant_out_vec(e->dec_q, dec_input_alphas(e, 0)), e->eos_mask,
+                                quant_out_vec(L.dec_q, dec_input_alphas(e, 0)), L.eos_mask,
                                 e->kind == 1 ? e->self_pages_d : nullptr, e->pages_per_slot,
-                                e->page_tokens, e->self_row_map, e->d_status, e->stream));
+                                e->page_tokens, L.self_row_map, L.d_status, L.stream));
   ++e->launches;
   mc_status st;
   for (int l = 0; l < e->dec_layers; ++l) {
@@ -516,66 +587,66 @@ mc_status run_decode_step(mc_engine* e, int R) {
     if (e->kind == 1) {
       const DevAttention& a = e->dec_self[l];
       GroupSpec qkv[3] = {
-          {&e->dec_q[0], &a.wq, kEpiF32, e->dec_qkv, d, 0, nullptr, false, 0.f},
-          {&e->dec_q[1], &a.wk, kEpiF32, e->self_k[l], d, 0, e->self_row_map, false, 0.f},
-          {&e->dec_q[2], &a.wv, kEpiF32, e->self_v[l], d, 0, e->self_row_map, false, 0.f}};
-      if ((st = gemm(e, MC_K_GEMM_QKV, R, qkv, 3))) return st;
+          {&L.dec_q[0], &a.wq, kEpiF32, L.dec_qkv, d, 0, nullptr, false, 0.f},
+          {&L.dec_q[1], &a.wk, kEpiF32, e->self_k[l], d, 0, L.self_row_map, false, 0.f},
+          {&L.dec_q[2], &a.wv, kEpiF32, e->self_v[l], d, 0, L.self_row_map, false, 0.f}};
+      if ((st = gemm(e, L, MC_K_GEMM_QKV, cap, nrows, R, qkv, 3))) return st;
       PROFILED(MC_K_ATTN_SELF, 4.0 * self_keys * d, 8.0 * self_keys * d + rows_d * 5,
-               CK(launch_attn_decode(e->dec_qkv, d, R, e->row_slot, e->order_self, e->slot_step, 1,
+               CK(launch_attn_decode(L.dec_qkv, d, cap, nrows, row_slot, order_self, e->slot_step, 1,
                                      e->self_pages_d, e->pages_per_slot, e->page_tokens,
-                                     e->self_k[l], e->self_v[l], d, e->heads, e->dec_o.p,
-                                     a.wo.alpha, e->d_status, e->stream)));
-      GroupSpec wo = {&e->dec_o, &a.wo, kEpiF32, e->dec_proj, d, 0, nullptr, false, 0.f};
-      if ((st = gemm(e, MC_K_GEMM_OUT, R, &wo, 1))) return st;
+                                     e->self_k[l], e->self_v[l], d, e->heads, L.dec_o.p,
+                                     a.wo.alpha, L.d_status, L.stream)));
+      GroupSpec wo = {&L.dec_o, &a.wo, kEpiF32, L.dec_proj, d, 0, nullptr, false, 0.f};
+      if ((st = gemm(e, L, MC_K_GEMM_OUT, cap, nrows, R, &wo, 1))) return st;
       PROFILED(MC_K_LAYERNORM, 0.0, rows_d * 13,
-               launch_residual_ln(e->dec_proj, d, x, d, a.ln_g, a.ln_b, R, d, y,
-                                  quant_out(e->dec_q, {c.wq.alpha}), e->d_status, e->stream));
+               launch_residual_ln(L.dec_proj, d, x, d, a.ln_g, a.ln_b, cap, nrows, d, y,
+                                  quant_out(L.dec_q, {c.wq.alpha}), L.d_status, L.stream));
       e->launches += 2;
     } else {
       const DevSsru& s = e->dec_ssru[l];
       GroupSpec wf[2] = {
-          {&e->dec_q[0], &s.w, kEpiF32, e->dec_qkv, 2 * d, 0, nullptr, false, 0.f},
-          {&e->dec_q[1], &s.wf, kEpiF32, e->dec_qkv, 2 * d, d, nullptr, false, 0.f}};
-      if ((st = gemm(e, MC_K_GEMM_QKV, R, wf, 2))) return st;
+          {&L.dec_q[0], &s.w, kEpiF32, L.dec_qkv, 2 * d, 0, nullptr, false, 0.f},
+          {&L.dec_q[1], &s.wf, kEpiF32, L.dec_qkv, 2 * d, d, nullptr, false, 0.f}};
+      if ((st = gemm(e, L, MC_K_GEMM_QKV, cap, nrows, R, wf, 2))) return st;
       PROFILED(MC_K_SSRU, 0.0, rows_d * 25,
-               launch_ssru(e->dec_qkv, 2 * d, d, e->ssru_state + (size_t)l * e->rmax * d,
-                           e->row_slot, x, s.ln_g, s.ln_b, R, d, y,
-                           quant_out(e->dec_q, {c.wq.alpha}), e->d_status, e->stream));
+               launch_ssru(L.dec_qkv, 2 * d, d, e->ssru_state + (size_t)l * e->rmax * d,
+                           row_slot, x, s.ln_g, s.ln_b, cap, nrows, d, y,
+                           quant_out(L.dec_q, {c.wq.alpha}), L.d_status, L.stream));
       ++e->launches;
     }
     std::swap(x, y);
-    GroupSpec wq = {&e->dec_q[0], &c.wq, kEpiF32, e->dec_qkv, d, 0, nullptr, false, 0.f};
-    if ((st = gemm(e, MC_K_GEMM_QKV, R, &wq, 1))) return st;
+    GroupSpec wq = {&L.dec_q[0], &c.wq, kEpiF32, L.dec_qkv, d, 0, nullptr, false, 0.f};
+    if ((st = gemm(e, L, MC_K_GEMM_QKV, cap, nrows, R, &wq, 1))) return st;
     PROFILED(MC_K_ATTN_CROSS, 4.0 * cross_keys * d, 8.0 * cross_keys * d + rows_d * 5,
-             CK(launch_attn_decode(e->dec_qkv, d, R, e->row_slot, e->order_cross, e->slot_src, 0,
+             CK(launch_attn_decode(L.dec_qkv, d, cap, nrows, row_slot, order_cross, e->slot_src, 0,
                                    e->cross_pages_d, e->pages_per_slot, e->page_tokens,
-                                   e->cross_k[l], e->cross_v[l], d, e->heads, e->dec_o.p,
-                                   c.wo.alpha, e->d_status, e->stream)));
-    GroupSpec wo = {&e->dec_o, &c.wo, kEpiF32, e->dec_proj, d, 0, nullptr, false, 0.f};
-    if ((st = gemm(e, MC_K_GEMM_OUT, R, &wo, 1))) return st;
+                                   e->cross_k[l], e->cross_v[l], d, e->heads, L.dec_o.p,
+                                   c.wo.alpha, L.d_status, L.stream)));
+    GroupSpec wo = {&L.dec_o, &c.wo, kEpiF32, L.dec_proj, d, 0, nullptr, false, 0.f};
+    if ((st = gemm(e, L, MC_K_GEMM_OUT, cap, nrows, R, &wo, 1))) return st;
     PROFILED(MC_K_LAYERNORM, 0.0, rows_d * 13,
-             launch_residual_ln(e->dec_proj, d, x, d, c.ln_g, c.ln_b, R, d, y,
-                                quant_out(e->dec_q, {f.w1.alpha}), e->d_status, e->stream));
+             launch_residual_ln(L.dec_proj, d, x, d, c.ln_g, c.ln_b, cap, nrows, d, y,
+                                quant_out(L.dec_q, {f.w1.alpha}), L.d_status, L.stream));
     std::swap(x, y);
-    GroupSpec w1 = {&e->dec_q[0], &f.w1, kEpiQ8, e->dec_h.p, e->ffn, 0, nullptr, true, f.w2.alpha};
-    if ((st = gemm(e, MC_K_GEMM_FFN1, R, &w1, 1))) return st;
-    GroupSpec w2 = {&e->dec_h, &f.w2, kEpiF32, e->dec_proj, d, 0, nullptr, false, 0.f};
-    if ((st = gemm(e, MC_K_GEMM_FFN2, R, &w2, 1))) return st;
+    GroupSpec w1 = {&L.dec_q[0], &f.w1, kEpiQ8, L.dec_h.p, e->ffn, 0, nullptr, true, f.w2.alpha};
+    if ((st = gemm(e, L, MC_K_GEMM_FFN1, cap, nrows, R, &w1, 1))) return st;
+    GroupSpec w2 = {&L.dec_h, &f.w2, kEpiF32, L.dec_proj, d, 0, nullptr, false, 0.f};
+    if ((st = gemm(e, L, MC_K_GEMM_FFN2, cap, nrows, R, &w2, 1))) return st;
     PROFILED(MC_K_LAYERNORM, 0.0, rows_d * (12 + dec_input_alphas(e, l + 1).size()),
-             launch_residual_ln(e->dec_proj, d, x, d, f.ln_g, f.ln_b, R, d, y,
-                                quant_out_vec(e->dec_q, dec_input_alphas(e, l + 1)), e->d_status,
-                                e->stream));
+             launch_residual_ln(L.dec_proj, d, x, d, f.ln_g, f.ln_b, cap, nrows, d, y,
+                                quant_out_vec(L.dec_q, dec_input_alphas(e, l + 1)), L.d_status,
+                                L.stream));
     std::swap(x, y);
     e->launches += 3;
   }
   // tied vocabulary projection + masked argmax (q8_engine.rs:749-790)
-  GroupSpec voc = {&e->dec_q[0], &e->vocab, kEpiArgmax, nullptr, 0, 0, nullptr, false, 0.f};
-  if ((st = gemm(e, MC_K_GEMM_VOCAB, R, &voc, 1, e->best, e->eos_mask))) return st;
-  PROFILED(MC_K_FINALIZE, 0.0, (double)R * 29,
-           launch_finalize(R, e->row_slot, e->best, e->slot_prev, e->slot_step, e->slot_limit,
-                           e->step_tokens, e->done, e->d_status, e->stream));
+  GroupSpec voc = {&L.dec_q[0], &e->vocab, kEpiArgmax, nullptr, 0, 0, nullptr, false, 0.f};
+  if ((st = gemm(e, L, MC_K_GEMM_VOCAB, cap, nrows, R, &voc, 1, L.best, L.eos_mask))) return st;
+  PROFILED(MC_K_FINALIZE, 0.0, R * 29,
+           launch_finalize(cap, nrows, row_slot, L.best, e->slot_prev, e->slot_step, e->slot_limit,
+                           L.step_tokens, L.done, L.d_status, L.stream));
   ++e->launches;
-  e->last_state = x;
+  L.last_state = x;
   return MC_OK;
 }
 
@@ -586,18 +657,24 @@ mc_status run_decode_step(mc_engine* e, int R) {
 // ============================================================================
 
 mc_engine::~mc_engine() {
+  for (Lane& L : lanes)
+    if (L.stream) cudaStreamSynchronize(L.stream);
   if (stream) cudaStreamSynchronize(stream);
-  for (auto& r : prof_pending) {
-    cudaEventDestroy(r.a);
-    cudaEventDestroy(r.b);
+  for (Lane& L : lanes) {
+    for (auto& r : L.prof_pending) {
+      cudaEventDestroy(r.a);
+      cudaEventDestroy(r.b);
+    }
+    if (L.graph) cudaGraphExecDestroy(L.graph);
+    if (L.h_status) cudaFreeHost(L.h_status);
+    if (L.adm_h) cudaFreeHost(L.adm_h);
+    if (L.rows_h) cudaFreeHost(L.rows_h);
+    if (L.h_step_tokens) cudaFreeHost(L.h_step_tokens);
+    if (L.h_done) cudaFreeHost(L.h_done);
+    if (L.own_stream && L.stream) cudaStreamDestroy(L.stream);
   }
   for (cudaEvent_t ev : event_pool) cudaEventDestroy(ev);
   for (void* p : allocations) cudaFree(p);
-  if (d_status) cudaFree(d_status);
-  if (h_i32) cudaFreeHost(h_i32);
-  if (h_step_tokens) cudaFreeHost(h_step_tokens);
-  if (h_done) cudaFreeHost(h_done);
-  if (h_status) cudaFreeHost(h_status);
   if (stream) cudaStreamDestroy(stream);
   for (Request* r : queue) delete r;
   for (Request* r : slot_req) delete r;
@@ -610,62 +687,67 @@ mc_status set_device(mc_engine* e) {
   return MC_OK;
 }
 
-mc_status allocate_buffers(mc_engine* e) {
+mc_status allocate_lane(mc_engine* e, Lane& L) {
   const int d = e->d, F = e->ffn;
   const int T = e->tmax, R = e->rmax;
-  CK(dalloc(e, &e->enc_x, (size_t)T * d));
-  CK(dalloc(e, &e->enc_x1, (size_t)T * d));
-  CK(dalloc(e, &e->enc_qkv, (size_t)T * 3 * d));
-  CK(dalloc(e, &e->enc_proj, (size_t)T * d));
+  CK(dalloc(e, &L.d_status, 1));
+  CK(cudaHostAlloc(&L.h_status, sizeof(uint32_t), cudaHostAllocDefault));
+  *L.h_status = 0;
+  CK(dalloc(e, &L.enc_x, (size_t)T * d));
+  CK(dalloc(e, &L.enc_x1, (size_t)T * d));
+  CK(dalloc(e, &L.enc_qkv, (size_t)T * 3 * d));
+  CK(dalloc(e, &L.enc_proj, (size_t)T * d));
   // quantized copies: one contiguous block so copy i = base + i * stride
   int8_t* eq = nullptr;
   CK(dalloc(e, &eq, (size_t)kMaxQuantOut * T * d));
   for (int i = 0; i < kMaxQuantOut; ++i) {
-    e->enc_q[i].p = eq + (size_t)i * T * d;
-    e->enc_q[i].rows = T;
-    e->enc_q[i].cols = d;
-    if (!encode_tmap_i8(&e->enc_q[i].tmap, e->enc_q[i].p, T, d, 128)) return fail(e, MC_MODEL, "tensor map");
+    L.enc_q[i].p = eq + (size_t)i * T * d;
+    L.enc_q[i].rows = T;
+    L.enc_q[i].cols = d;
+    if (!encode_tmap_i8(&L.enc_q[i].tmap, L.enc_q[i].p, T, d, 128)) return fail(e, MC_MODEL, "tensor map");
   }
   mc_status st;
-  if ((st = make_qbuf(e, &e->enc_o, T, d))) return st;
-  if ((st = make_qbuf(e, &e->enc_h, T, F))) return st;
-  CK(dalloc(e, &e->enc_tokens, T));
-  CK(dalloc(e, &e->enc_pos, T));
-  CK(dalloc(e, &e->enc_cu, T + 1));
-  CK(dalloc(e, &e->enc_cross_rows, T));
-  CK(dalloc(e, &e->enc_seq_ids, R));
+  if ((st = make_qbuf(e, &L.enc_o, T, d))) return st;
+  if ((st = make_qbuf(e, &L.enc_h, T, F))) return st;
+  L.adm_cap = adm_layout(T, R, e->pages_per_slot).end + 16;
+  CK(dalloc(e, &L.adm_d, L.adm_cap));
+  CK(cudaHostAlloc(&L.adm_h, L.adm_cap * sizeof(int32_t), cudaHostAllocDefault));
 
-  CK(dalloc(e, &e->dec_a, (size_t)R * d));
-  CK(dalloc(e, &e->dec_b, (size_t)R * d));
-  CK(dalloc(e, &e->dec_qkv, (size_t)R * 3 * d));
-  CK(dalloc(e, &e->dec_proj, (size_t)R * d));
+  CK(dalloc(e, &L.dec_a, (size_t)R * d));
+  CK(dalloc(e, &L.dec_b, (size_t)R * d));
+  CK(dalloc(e, &L.dec_qkv, (size_t)R * 3 * d));
+  CK(dalloc(e, &L.dec_proj, (size_t)R * d));
   int8_t* dq = nullptr;
   CK(dalloc(e, &dq, (size_t)kMaxQuantOut * R * d));
   for (int i = 0; i < kMaxQuantOut; ++i) {
-    e->dec_q[i].p = dq + (size_t)i * R * d;
-    e->dec_q[i].rows = R;
-    e->dec_q[i].cols = d;
-    if (!encode_tmap_i8(&e->dec_q[i].tmap, e->dec_q[i].p, R, d, 128)) return fail(e, MC_MODEL, "tensor map");
+    L.dec_q[i].p = dq + (size_t)i * R * d;
+    L.dec_q[i].rows = R;
+    L.dec_q[i].cols = d;
+    if (!encode_tmap_i8(&L.dec_q[i].tmap, L.dec_q[i].p, R, d, 128)) return fail(e, MC_MODEL, "tensor map");
   }
-  if ((st = make_qbuf(e, &e->dec_o, R, d))) return st;
-  if ((st = make_qbuf(e, &e->dec_h, R, F))) return st;
-  CK(dalloc(e, &e->row_slot, R));
-  CK(dalloc(e, &e->order_self, R));
-  CK(dalloc(e, &e->order_cross, R));
-  CK(dalloc(e, &e->self_row_map, R));
-  CK(dalloc(e, &e->step_tokens, R));
-  CK(dalloc(e, &e->eos_mask, R));
-  CK(dalloc(e, &e->done, R));
-  CK(dalloc(e, &e->best, R));
+  if ((st = make_qbuf(e, &L.dec_o, R, d))) return st;
+  if ((st = make_qbuf(e, &L.dec_h, R, F))) return st;
+  CK(dalloc(e, &L.rows_d, (size_t)4 + 3 * R));
+  CK(cudaHostAlloc(&L.rows_h, ((size_t)4 + 3 * R) * sizeof(int32_t), cudaHostAllocDefault));
+  std::memset(L.rows_h, 0, ((size_t)4 + 3 * R) * sizeof(int32_t));
+  CK(dalloc(e, &L.self_row_map, R));
+  CK(dalloc(e, &L.step_tokens, R));
+  CK(dalloc(e, &L.eos_mask, R));
+  CK(dalloc(e, &L.done, R));
+  CK(dalloc(e, &L.best, R));
+  CK(cudaHostAlloc(&L.h_step_tokens, (size_t)R * sizeof(int32_t), cudaHostAllocDefault));
+  CK(cudaHostAlloc(&L.h_done, (size_t)R, cudaHostAllocDefault));
+  return MC_OK;
+}
+
+mc_status allocate_buffers(mc_engine* e) {
+  const int d = e->d;
+  const int R = e->rmax;
   CK(dalloc(e, &e->slot_prev, R));
   CK(dalloc(e, &e->slot_step, R));
   CK(dalloc(e, &e->slot_limit, R));
   CK(dalloc(e, &e->slot_force, R));
   CK(dalloc(e, &e->slot_src, R));
-  CK(dalloc(e, &e->adm_slots, R));
-  CK(dalloc(e, &e->adm_limits, R));
-  CK(dalloc(e, &e->adm_force, R));
-  CK(dalloc(e, &e->adm_src, R));
   if (e->kind == 0) CK(dalloc(e, &e->ssru_state, (size_t)e->dec_layers * R * d));
 
   e->page_tokens = (int)e->cfg.page_tokens;
@@ -690,8 +772,6 @@ mc_status allocate_buffers(mc_engine* e) {
   }
   CK(dalloc(e, &e->cross_pages_d, (size_t)R * e->pages_per_slot));
   CK(dalloc(e, &e->self_pages_d, (size_t)R * e->pages_per_slot));
-  e->cross_pages_h.assign((size_t)R * e->pages_per_slot, 0);
-  e->self_pages_h.assign((size_t)R * e->pages_per_slot, 0);
   e->free_cross.clear();
   e->free_self.clear();
   for (int p = pool - 1; p >= 0; --p) e->free_cross.push_back(p);
@@ -700,10 +780,22 @@ mc_status allocate_buffers(mc_engine* e) {
   for (int s = R - 1; s >= 0; --s) e->free_slots.push_back(s);
   e->slot_req.assign(R, nullptr);
 
-  e->h_i32_cap = (size_t)4 * T + 6 * R + 16;
-  CK(cudaHostAlloc(&e->h_i32, e->h_i32_cap * sizeof(int32_t), cudaHostAllocDefault));
-  CK(cudaHostAlloc(&e->h_step_tokens, (size_t)R * sizeof(int32_t), cudaHostAllocDefault));
-  CK(cudaHostAlloc(&e->h_done, (size_t)R, cudaHostAllocDefault));
+  const int n_lanes = std::max(1, std::min<int>(e->cfg.lanes ? (int)e->cfg.lanes : 1, std::min(kMaxLanes, R)));
+  e->lanes.resize(n_lanes);
+  for (int i = 0; i < n_lanes; ++i) {
+    Lane& L = e->lanes[i];
+    L.id = i;
+    L.cap = (R + n_lanes - 1) / n_lanes;
+    if (i == 0) {
+      L.stream = e->stream;
+    } else {
+      CK(cudaStreamCreateWithFlags(&L.stream, cudaStreamNonBlocking));
+      L.own_stream = true;
+    }
+    mc_status st = allocate_lane(e, L);
+    if (st) return st;
+  }
+  CK(prepare_q8_gemm());
   CK(cudaStreamSynchronize(e->stream));
   return MC_OK;
 }
@@ -735,26 +827,39 @@ void finish_request(mc_engine* e, Request* r) {
   delete r;
 }
 
-// Drops every queued and in-flight request (after a failed step).
+// Drops every queued and in-flight request (after a failed step).  Waits for
+// every lane's work first: their kernels may still read the slots and pages
+// released here.
 void abort_all(mc_engine* e) {
+  for (Lane& L : e->lanes) {
+    cudaStreamSynchronize(L.stream);
+    for (auto& r : L.prof_pending) {
+      e->event_pool.push_back(r.a);
+      e->event_pool.push_back(r.b);
+    }
+    L.prof_pending.clear();
+    L.launched = 0;
+  }
   for (Request* r : e->queue) delete r;
   e->queue.clear();
-  for (int s : e->active) {
-    Request* r = e->slot_req[s];
-    if (r) {
-      release_slot(e, r);
-      delete r;
+  for (Lane& L : e->lanes) {
+    for (int s : L.active) {
+      Request* r = e->slot_req[s];
+      if (r) {
+        release_slot(e, r);
+        delete r;
+      }
     }
+    L.active.clear();
   }
-  e->active.clear();
 }
 
-mc_status check_status(mc_engine* e) {
-  const uint32_t bits = *e->h_status;
+mc_status check_status(mc_engine* e, Lane& L) {
+  const uint32_t bits = *L.h_status;
   if (!bits) return MC_OK;
-  *e->h_status = 0;
-  CK(cudaMemsetAsync(e->d_status, 0, sizeof(uint32_t), e->stream));
-  CK(cudaStreamSynchronize(e->stream));
+  *L.h_status = 0;
+  CK(cudaMemsetAsync(L.d_status, 0, sizeof(uint32_t), L.stream));
+  CK(cudaStreamSynchronize(L.stream));
   abort_all(e);
   if (bits & kStatusWaitTimeout) {
     e->ready = false;
@@ -767,29 +872,35 @@ mc_status check_status(mc_engine* e) {
   return fail(e, MC_INFERENCE, "activation contains a non-finite value");
 }
 
-// Admits queued requests into free slots and runs one packed encoder pass.
-mc_status admit(mc_engine* e, std::vector<Request*>* admitted) {
-  int T = 0, max_len = 0;
+// Admits queued requests into free slots of lane L and enqueues one packed
+// encoder pass on its stream (asynchronous: the staging block is pinned and
+// the lane's previous step has completed).  `cap` overrides the lane's row
+// limit (per-layer capture).
+mc_status admit(mc_engine* e, Lane& L, int cap) {
+  int T = 0;
   const int pt = e->page_tokens;
+  const int pps = e->pages_per_slot;
+  const size_t room = cap > (int)L.active.size() ? (size_t)(cap - (int)L.active.size()) : 0;
+  const size_t avail = std::min(room, e->free_slots.size());
   // Admission granularity: an encoder pass over a handful of sources costs
   // nearly as much launch latency as one over hundreds, so wait until an
-  // eighth of the slots are free -- unless nothing is running or the whole
+  // eighth of the lane is free -- unless the lane is idle or the whole
   // queue fits (which keeps latency low under light load).
-  const size_t free_slots = e->free_slots.size();
-  if (!e->active.empty() && free_slots < (size_t)std::max(1, e->rmax / 8) &&
-      e->queue.size() > free_slots)
+  if (avail == 0 || e->queue.empty()) return MC_OK;
+  if (!L.active.empty() && avail < (size_t)std::max(1, cap / 8) && e->queue.size() > avail)
     return MC_OK;
-  while (!e->queue.empty() && !e->free_slots.empty()) {
+  std::vector<Request*> admitted;
+  while (!e->queue.empty() && admitted.size() < avail) {
     Request* r = e->queue.front();
-    const int L = (int)r->tokens.size();
+    const int len = (int)r->tokens.size();
     const uint32_t lim = request_limit(e, r);
     if (lim == 0) {  // nothing to generate
       e->queue.pop_front();
       finish_request(e, r);
       continue;
     }
-    if (T + L > e->tmax) break;
-    const int need_c = (L + pt - 1) / pt;
+    if (T + len > e->tmax) break;
+    const int need_c = (len + pt - 1) / pt;
     const int need_s = e->kind == 1 ? (int)((lim + pt - 1) / pt) : 0;
     if ((int)e->free_cross.size() < need_c || (int)e->free_self.size() < need_s) break;
     e->queue.pop_front();
@@ -803,41 +914,43 @@ mc_status admit(mc_engine* e, std::vector<Request*>* admitted) {
       r->self_pages.push_back(e->free_self.back());
       e->free_self.pop_back();
     }
-    int32_t* cp = e->cross_pages_h.data() + (size_t)r->slot * e->pages_per_slot;
-    for (int i = 0; i < need_c; ++i) cp[i] = r->cross_pages[i];
-    int32_t* sp = e->self_pages_h.data() + (size_t)r->slot * e->pages_per_slot;
-    for (int i = 0; i < need_s; ++i) sp[i] = r->self_pages[i];
     e->slot_req[r->slot] = r;
-    T += L;
-    max_len = std::max(max_len, L);
-    admitted->push_back(r);
+    T += len;
+    admitted.push_back(r);
   }
-  const int B = (int)admitted->size();
+  const int B = (int)admitted.size();
   if (B == 0) return MC_OK;
-  // staging: tokens[T] pos[T] rows[T] cu[B+1] slots[B] limits[B] force[B] src[B]
-  int32_t* h = e->h_i32;
-  int32_t *tok = h, *pos = h + T, *rows = h + 2 * T, *cu = h + 3 * T, *slots = cu + B + 1,
-          *lims = slots + B, *force = lims + B, *src = force + B, *seq_ids = src + B;
+  const AdmLayout A = adm_layout(T, B, pps);
+  int32_t* h = L.adm_h;
+  int32_t *tok = h + A.tok, *pos = h + A.pos, *crow = h + A.crow, *cu = h + A.cu,
+          *slots = h + A.slots, *lims = h + A.lims, *force = h + A.force, *src = h + A.src,
+          *seq_ids = h + A.seq_ids, *pages = h + A.pages;
   int t = 0;
   double sum_len_sq = 0;
   cu[0] = 0;
   for (int b = 0; b < B; ++b) {
-    Request* r = (*admitted)[b];
-    const int L = (int)r->tokens.size();
-    for (int i = 0; i < L; ++i, ++t) {
+    Request* r = admitted[b];
+    const int len = (int)r->tokens.size();
+    for (int i = 0; i < len; ++i, ++t) {
       tok[t] = r->tokens[i];
       pos[t] = i;
-      rows[t] = r->cross_pages[i / pt] * pt + i % pt;
+      crow[t] = r->cross_pages[i / pt] * pt + i % pt;
     }
     cu[b + 1] = t;
-    sum_len_sq += (double)L * L;
+    sum_len_sq += (double)len * len;
     slots[b] = r->slot;
     lims[b] = (int32_t)request_limit(e, r);
     force[b] = (int32_t)r->force;
-    src[b] = L;
+    src[b] = len;
+    int32_t* cp = pages + (size_t)b * pps;
+    int32_t* sp = pages + ((size_t)B + b) * pps;
+    for (int i = 0; i < pps; ++i) {
+      cp[i] = i < (int)r->cross_pages.size() ? r->cross_pages[i] : 0;
+      sp[i] = i < (int)r->self_pages.size() ? r->self_pages[i] : 0;
+    }
   }
   // length buckets for the encoder attention (shared memory follows length)
-  e->buckets.clear();
+  L.buckets.clear();
   {
     const int bounds[4] = {32, 64, 128, kMaxSeq};
     int off = 0, lo = 0;
@@ -845,45 +958,32 @@ mc_status admit(mc_engine* e, std::vector<Request*>* admitted) {
       const int start = off;
       for (int b = 0; b < B; ++b)
         if (src[b] > lo && src[b] <= hi) seq_ids[off++] = b;
-      if (off > start) e->buckets.push_back({start, off - start, hi});
+      if (off > start) L.buckets.push_back({start, off - start, hi});
       lo = hi;
     }
   }
-  cudaStream_t s = e->stream;
-  CK(cudaMemcpyAsync(e->enc_seq_ids, seq_ids, B * 4, cudaMemcpyHostToDevice, s));
-  CK(cudaMemcpyAsync(e->enc_tokens, tok, T * 4, cudaMemcpyHostToDevice, s));
-  CK(cudaMemcpyAsync(e->enc_pos, pos, T * 4, cudaMemcpyHostToDevice, s));
-  CK(cudaMemcpyAsync(e->enc_cross_rows, rows, T * 4, cudaMemcpyHostToDevice, s));
-  CK(cudaMemcpyAsync(e->enc_cu, cu, (B + 1) * 4, cudaMemcpyHostToDevice, s));
-  CK(cudaMemcpyAsync(e->adm_slots, slots, B * 4, cudaMemcpyHostToDevice, s));
-  CK(cudaMemcpyAsync(e->adm_limits, lims, B * 4, cudaMemcpyHostToDevice, s));
-  CK(cudaMemcpyAsync(e->adm_force, force, B * 4, cudaMemcpyHostToDevice, s));
-  CK(cudaMemcpyAsync(e->adm_src, src, B * 4, cudaMemcpyHostToDevice, s));
-  const size_t pt_bytes = (size_t)e->rmax * e->pages_per_slot * 4;
-  CK(cudaMemcpyAsync(e->cross_pages_d, e->cross_pages_h.data(), pt_bytes, cudaMemcpyHostToDevice, s));
-  if (e->kind == 1)
-    CK(cudaMemcpyAsync(e->self_pages_d, e->self_pages_h.data(), pt_bytes, cudaMemcpyHostToDevice, s));
-  mc_status st = run_encoder(e, T, B, max_len, sum_len_sq);
+  cudaStream_t s = L.stream;
+  CK(cudaMemcpyAsync(L.adm_d, L.adm_h, A.end * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+  mc_status st = run_encoder(e, L, A, sum_len_sq);
   if (st) return st;
-  launch_init_slots(B, e->adm_slots, e->adm_limits, e->adm_force, e->adm_src, e->slot_prev,
+  const int32_t* ad = L.adm_d;
+  launch_init_slots(B, ad + A.slots, ad + A.lims, ad + A.force, ad + A.src, e->slot_prev,
                     e->slot_step, e->slot_limit, e->slot_force, e->slot_src, e->ssru_state,
-                    e->dec_layers, e->rmax, e->d, s);
+                    e->dec_layers, e->rmax, e->d, ad + A.pages, e->cross_pages_d,
+                    e->kind == 1 ? e->self_pages_d : nullptr, pps, s);
   ++e->launches;
-  // the page-table copies read pageable host memory: finish before edits
-  CK(cudaStreamSynchronize(s));
-  prof_harvest(e);
-  for (Request* r : *admitted) e->active.push_back(r->slot);
+  for (Request* r : admitted) L.active.push_back(r->slot);
   return MC_OK;
 }
 
 // Row orders for the decode attention launches: rows with the most keys
 // first (counting sort; self keys = step + 1, cross keys = source length).
-void build_row_orders(mc_engine* e, int32_t* order_self, int32_t* order_cross) {
-  const int R = (int)e->active.size();
+void build_row_orders(mc_engine* e, const Lane& L, int32_t* order_self, int32_t* order_cross) {
+  const int R = (int)L.active.size();
   int count_s[kMaxSeq + 2] = {0}, count_c[kMaxSeq + 2] = {0};
   std::vector<int> ks(R), kc(R);
   for (int r = 0; r < R; ++r) {
-    const Request* q = e->slot_req[e->active[r]];
+    const Request* q = e->slot_req[L.active[r]];
     ks[r] = std::min<int>(kMaxSeq + 1, (int)q->output.size() + 1);
     kc[r] = std::min<int>(kMaxSeq + 1, (int)q->tokens.size());
     ++count_s[kMaxSeq + 1 - ks[r]];
@@ -899,50 +999,128 @@ void build_row_orders(mc_engine* e, int32_t* order_self, int32_t* order_cross) {
   }
 }
 
-mc_status decode_once(mc_engine* e) {
-  const int R = (int)e->active.size();
-  if (R == 0) return MC_OK;
-  cudaStream_t s = e->stream;
-  std::memcpy(e->h_i32, e->active.data(), R * 4);
-  build_row_orders(e, e->h_i32 + R, e->h_i32 + 2 * R);
-  CK(cudaMemcpyAsync(e->row_slot, e->h_i32, R * 4, cudaMemcpyHostToDevice, s));
-  CK(cudaMemcpyAsync(e->order_self, e->h_i32 + R, R * 4, cudaMemcpyHostToDevice, s));
-  CK(cudaMemcpyAsync(e->order_cross, e->h_i32 + 2 * R, R * 4, cudaMemcpyHostToDevice, s));
-  mc_status st = run_decode_step(e, R);
+// The device work of one decode step of lane L, grids sized for `cap` rows:
+// the rows block upload, the step's kernels, and the read-back of `cap`
+// tokens, finished flags and the status word.
+mc_status enqueue_step(mc_engine* e, Lane& L, int cap) {
+  cudaStream_t s = L.stream;
+  CK(cudaMemcpyAsync(L.rows_d, L.rows_h, ((size_t)4 + 3 * e->rmax) * sizeof(int32_t),
+                     cudaMemcpyHostToDevice, s));
+  mc_status st = run_decode_step(e, L, cap);
   if (st) return st;
-  CK(cudaMemcpyAsync(e->h_step_tokens, e->step_tokens, R * 4, cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(e->h_done, e->done, R, cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(e->h_status, e->d_status, 4, cudaMemcpyDeviceToHost, s));
-  CK(cudaStreamSynchronize(s));
-  prof_harvest(e);
-  ++e->steps;
-  if ((st = check_status(e))) return st;
-  std::vector<int32_t> keep;
-  keep.reserve(R);
-  for (int r = 0; r < R; ++r) {
-    const int slot = e->active[r];
-    Request* q = e->slot_req[slot];
-    q->output.push_back(e->h_step_tokens[r]);
-    if (e->h_done[r]) finish_request(e, q);
-    else keep.push_back(slot);
-  }
-  e->active.swap(keep);
+  CK(cudaMemcpyAsync(L.h_step_tokens, L.step_tokens, (size_t)cap * 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(L.h_done, L.done, (size_t)cap, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(L.h_status, L.d_status, 4, cudaMemcpyDeviceToHost, s));
   return MC_OK;
 }
 
+// Captures lane L's decode step for L.cap rows as a CUDA graph.  A failed
+// capture is not an error: the lane keeps launching eagerly.
+void capture_step(mc_engine* e, Lane& L) {
+  L.graph_tried = true;
+  const std::string saved_error = e->error;
+  const bool saved_ready = e->ready;
+  const uint64_t launches0 = e->launches;
+  cudaGraph_t g = nullptr;
+  bool ok = cudaStreamBeginCapture(L.stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+  if (ok) {
+    const mc_status st = enqueue_step(e, L, L.cap);
+    ok = cudaStreamEndCapture(L.stream, &g) == cudaSuccess && st == MC_OK && g != nullptr;
+  }
+  if (ok) ok = cudaGraphInstantiate(&L.graph, g, 0) == cudaSuccess;
+  if (g) cudaGraphDestroy(g);
+  if (!ok) {
+    if (L.graph) cudaGraphExecDestroy(L.graph);
+    L.graph = nullptr;
+    cudaGetLastError();
+    e->error = saved_error;
+    e->ready = saved_ready;
+  }
+  L.graph_kernels = e->launches - launches0;
+  e->launches = launches0;
+}
+
+// Launches one decode step over lane L's active rows (asynchronous).
+mc_status launch_decode(mc_engine* e, Lane& L, bool allow_graph) {
+  const int R = (int)L.active.size();
+  if (R == 0) return MC_OK;
+  int32_t* rs = L.rows_h + 4;
+  L.rows_h[0] = R;
+  std::memcpy(rs, L.active.data(), R * 4);
+  build_row_orders(e, L, rs + e->rmax, rs + 2 * e->rmax);
+  const bool graph_ok = allow_graph && e->use_graphs && !e->profiling && R <= L.cap &&
+                        L.eager_steps > 0;
+  if (graph_ok && !L.graph_tried) capture_step(e, L);
+  if (graph_ok && L.graph) {
+    CK(cudaGraphLaunch(L.graph, L.stream));
+    e->launches += L.graph_kernels;
+  } else {
+    mc_status st = enqueue_step(e, L, R);
+    if (st) return st;
+    ++L.eager_steps;
+  }
+  L.launched = R;
+  return MC_OK;
+}
+
+// Waits for lane L's step in flight and applies its tokens: each row appends
+// its token; finished rows retire and release their slot and pages.
+mc_status complete_lane(mc_engine* e, Lane& L) {
+  if (!L.launched) return MC_OK;
+  const int R = L.launched;
+  L.launched = 0;
+  CK(cudaStreamSynchronize(L.stream));
+  prof_harvest(e, L);
+  ++e->steps;
+  mc_status st = check_status(e, L);
+  if (st) return st;
+  std::vector<int32_t> keep;
+  keep.reserve(R);
+  for (int r = 0; r < R; ++r) {
+    const int slot = L.active[r];
+    Request* q = e->slot_req[slot];
+    q->output.push_back(L.h_step_tokens[r]);
+    if (L.h_done[r]) finish_request(e, q);
+    else keep.push_back(slot);
+  }
+  L.active.swap(keep);
+  return MC_OK;
+}
+
+size_t total_active(const mc_engine* e) {
+  size_t n = 0;
+  for (const Lane& L : e->lanes) n += L.active.size();
+  return n;
+}
+
+// One scheduler step: each lane in turn completes its step in flight (if
+// any), admits queued requests, and launches its next step.  Lane i's new
+// step runs on the GPU while the host completes lane i+1, so the GPU stays
+// busy across the host's bookkeeping.  With profiling on, lanes run one at a
+// time so the per-kernel times are not shared with another lane.
 mc_status engine_step(mc_engine* e) {
   if (!e->loaded) return fail(e, MC_MODEL, "no model loaded");
   if (!e->ready) return fail(e, MC_INFERENCE, "engine is not ready after a device failure");
   mc_status st = set_device(e);
   if (st) return st;
-  std::vector<Request*> admitted;
-  if ((st = admit(e, &admitted))) return st;
-  if (!admitted.empty()) {
-    CK(cudaMemcpyAsync(e->h_status, e->d_status, 4, cudaMemcpyDeviceToHost, e->stream));
-    CK(cudaStreamSynchronize(e->stream));
-    if ((st = check_status(e))) return st;
+  for (Lane& L : e->lanes) {
+    if ((st = complete_lane(e, L))) return st;
+    if ((st = admit(e, L, L.cap)) || (st = launch_decode(e, L, true))) {
+      abort_all(e);
+      return st;
+    }
+    if (e->profiling && (st = complete_lane(e, L))) return st;
   }
-  return decode_once(e);
+  return MC_OK;
+}
+
+// Completes every lane's step in flight (used before returning results that
+// must be whole).
+mc_status drain_lanes(mc_engine* e) {
+  mc_status st;
+  for (Lane& L : e->lanes)
+    if ((st = complete_lane(e, L))) return st;
+  return MC_OK;
 }
 
 mc_status validate_source(const mc_engine* e, const int32_t* tokens, size_t n, std::string* why) {
@@ -975,6 +1153,7 @@ extern "C" void mc_config_default(mc_config* cfg) {
   cfg->page_tokens = 16;
   cfg->kv_pages = 0;
   cfg->max_length_factor = 3;
+  cfg->lanes = 1;
 }
 
 extern "C" mc_status mc_create(const mc_config* cfg, mc_engine** out) {
@@ -982,18 +1161,14 @@ extern "C" mc_status mc_create(const mc_config* cfg, mc_engine** out) {
   *out = nullptr;
   if (cfg->max_inflight == 0 || cfg->max_inflight > 65536 || cfg->max_encode_tokens < 256 ||
       cfg->page_tokens == 0 || cfg->page_tokens > 256 || cfg->max_length_factor < 1 ||
-      cfg->max_length_factor > 8)
+      cfg->max_length_factor > 8 || cfg->lanes > (uint32_t)kMaxLanes)
     return MC_INVALID_INPUT;
   mc_engine* e = new mc_engine();
   e->cfg = *cfg;
   mc_status st = set_device(e);
   if (st == MC_OK) {
     cudaError_t r = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
-    if (r == cudaSuccess) r = cudaMalloc(&e->d_status, sizeof(uint32_t));
-    if (r == cudaSuccess) r = cudaMemset(e->d_status, 0, sizeof(uint32_t));
-    if (r == cudaSuccess) r = cudaHostAlloc(&e->h_status, sizeof(uint32_t), cudaHostAllocDefault);
     if (r != cudaSuccess) st = MC_CUDA;
-    else *e->h_status = 0;
   }
   if (st != MC_OK) {
     delete e;
@@ -1152,7 +1327,7 @@ extern "C" mc_status mc_submit(mc_engine* e, uint64_t id, const int32_t* tokens,
 extern "C" mc_status mc_step(mc_engine* e, uint32_t* active_after, uint32_t* queued_after) {
   if (!e) return MC_INVALID_INPUT;
   mc_status st = engine_step(e);
-  if (active_after) *active_after = (uint32_t)e->active.size();
+  if (active_after) *active_after = (uint32_t)total_active(e);
   if (queued_after) *queued_after = (uint32_t)e->queue.size();
   return st;
 }
@@ -1192,7 +1367,7 @@ mc_status validate_batch(mc_engine* e, const int32_t* tokens, size_t n_tokens,
     mc_status st = validate_source(e, tokens + offsets[b], offsets[b + 1] - offsets[b], &why);
     if (st) return fail(e, st, why);
   }
-  if (!e->queue.empty() || !e->active.empty())
+  if (!e->queue.empty() || total_active(e) != 0)
     return fail(e, MC_INVALID_INPUT, "engine has streaming requests in flight");
   return MC_OK;
 }
@@ -1218,14 +1393,19 @@ extern "C" mc_status mc_translate_token_ids(mc_engine* e, const int32_t* tokens,
     e->queue.push_back(r);
   }
   const uint64_t step_bound = (uint64_t)batch * (kMaxSeq + 2) + 16;
-  for (uint64_t i = 0; i < step_bound && (!e->queue.empty() || !e->active.empty()); ++i) {
+  for (uint64_t i = 0; i < step_bound && (!e->queue.empty() || total_active(e) != 0); ++i) {
     if ((st = engine_step(e))) {
       abort_all(e);
       e->finished.clear();
       return st;
     }
   }
-  if (!e->queue.empty() || !e->active.empty()) {
+  if ((st = drain_lanes(e))) {
+    abort_all(e);
+    e->finished.clear();
+    return st;
+  }
+  if (!e->queue.empty() || total_active(e) != 0) {
     abort_all(e);
     e->finished.clear();
     return fail(e, MC_INFERENCE, "scheduler made no progress");
@@ -1259,6 +1439,7 @@ extern "C" mc_status mc_trace_first_step(mc_engine* e, const int32_t* tokens, si
   if (batch > (uint32_t)e->rmax || n_tokens > (size_t)e->tmax)
     return fail(e, MC_INVALID_INPUT, "trace batch exceeds one encoder pass");
   if ((st = set_device(e))) return st;
+  Lane& L = e->lanes[0];
   uint32_t lmax = 0;
   for (uint32_t b = 0; b < batch; ++b) lmax = std::max(lmax, offsets[b + 1] - offsets[b]);
   for (uint32_t b = 0; b < batch; ++b) {
@@ -1269,26 +1450,26 @@ extern "C" mc_status mc_trace_first_step(mc_engine* e, const int32_t* tokens, si
     r->force = 0;
     e->queue.push_back(r);
   }
-  std::vector<Request*> admitted;
-  if ((st = admit(e, &admitted))) {
+  if ((st = admit(e, L, e->rmax))) {
     abort_all(e);
     return st;
   }
-  if (admitted.size() != batch) {
+  if (L.active.size() != batch) {
     abort_all(e);
     return fail(e, MC_INVALID_INPUT, "trace batch does not fit the free slots or pages");
   }
+  CK(cudaStreamSynchronize(L.stream));
   const int d = e->d;
   const size_t row_bytes = (size_t)d * 4;
   if (encoder_output) {
     for (uint32_t b = 0; b < batch; ++b)
       for (uint32_t i = 0; i < offsets[b + 1] - offsets[b]; ++i)
-        CK(cudaMemcpy(encoder_output + ((size_t)b * lmax + i) * d, e->enc_x + (size_t)(offsets[b] + i) * d,
+        CK(cudaMemcpy(encoder_output + ((size_t)b * lmax + i) * d, L.enc_x + (size_t)(offsets[b] + i) * d,
                       row_bytes, cudaMemcpyDeviceToHost));
   }
   for (int l = 0; l < e->dec_layers && (cross_key || cross_value); ++l)
     for (uint32_t b = 0; b < batch; ++b) {
-      const Request* r = admitted[b];
+      const Request* r = e->slot_req[L.active[b]];
       for (uint32_t i = 0; i < offsets[b + 1] - offsets[b]; ++i) {
         const size_t row = (size_t)r->cross_pages[i / e->page_tokens] * e->page_tokens + i % e->page_tokens;
         const size_t dst = (((size_t)l * batch + b) * lmax + i) * d;
@@ -1298,30 +1479,26 @@ extern "C" mc_status mc_trace_first_step(mc_engine* e, const int32_t* tokens, si
           CK(cudaMemcpy(cross_value + dst, e->cross_v[l] + row * d, row_bytes, cudaMemcpyDeviceToHost));
       }
     }
-  const int R = (int)e->active.size();
-  std::memcpy(e->h_i32, e->active.data(), R * 4);
-  build_row_orders(e, e->h_i32 + R, e->h_i32 + 2 * R);
-  CK(cudaMemcpyAsync(e->row_slot, e->h_i32, R * 4, cudaMemcpyHostToDevice, e->stream));
-  CK(cudaMemcpyAsync(e->order_self, e->h_i32 + R, R * 4, cudaMemcpyHostToDevice, e->stream));
-  CK(cudaMemcpyAsync(e->order_cross, e->h_i32 + 2 * R, R * 4, cudaMemcpyHostToDevice, e->stream));
-  if ((st = run_decode_step(e, (int)e->active.size()))) {
+  if ((st = launch_decode(e, L, false))) {
     abort_all(e);
     return st;
   }
-  CK(cudaMemcpyAsync(e->h_status, e->d_status, 4, cudaMemcpyDeviceToHost, e->stream));
-  CK(cudaStreamSynchronize(e->stream));
-  prof_harvest(e);
-  if ((st = check_status(e))) return st;
+  L.launched = 0;
+  CK(cudaStreamSynchronize(L.stream));
+  prof_harvest(e, L);
+  if ((st = check_status(e, L))) return st;
   if (decoder_state)
-    CK(cudaMemcpy(decoder_state, e->last_state, (size_t)batch * row_bytes, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(decoder_state, L.last_state, (size_t)batch * row_bytes, cudaMemcpyDeviceToHost));
   abort_all(e);
   return MC_OK;
 }
 
 extern "C" mc_status mc_profile(mc_engine* e, int32_t enable) {
   if (!e) return MC_INVALID_INPUT;
-  if (e->stream) cudaStreamSynchronize(e->stream);
-  prof_harvest(e);
+  for (Lane& L : e->lanes) {
+    cudaStreamSynchronize(L.stream);
+    prof_harvest(e, L);
+  }
   e->profiling = enable != 0;
   for (int k = 0; k < MC_KERNEL_KINDS; ++k) {
     e->prof_ms[k] = e->prof_flops[k] = e->prof_bytes[k] = 0.0;

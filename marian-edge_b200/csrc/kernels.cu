@@ -17,6 +17,12 @@ namespace {
 
 constexpr float kLnEps = 1.0e-6f;  // tensor.rs:3
 
+// Rows of a launch: the device count when given (launches replayed from a
+// CUDA graph, whose grids cover `cap` rows), else cap.
+__device__ __forceinline__ int launch_rows(const int32_t* rows_dev, int cap) {
+  return rows_dev ? max(0, min(*rows_dev, cap)) : cap;
+}
+
 __device__ __forceinline__ float exp_f32(float x) {
   return static_cast<float>(exp(static_cast<double>(x)));
 }
@@ -59,7 +65,8 @@ __global__ void embed_encoder_kernel(const int32_t* __restrict__ tokens,
   store_quant4(q, elem, v.x, v.y, v.z, v.w, status);
 }
 
-__global__ void embed_decoder_kernel(int rows, const int32_t* __restrict__ row_slot,
+__global__ void embed_decoder_kernel(int cap, const int32_t* __restrict__ rows_dev,
+                                     const int32_t* __restrict__ row_slot,
                                      const int32_t* __restrict__ slot_prev,
                                      const int32_t* __restrict__ slot_step,
                                      const int32_t* __restrict__ slot_force,
@@ -69,6 +76,7 @@ __global__ void embed_decoder_kernel(int rows, const int32_t* __restrict__ row_s
                                      const int32_t* __restrict__ self_pages, int pages_per_slot,
                                      int page_tokens, int32_t* self_row_map, uint32_t* status) {
   pdl_enter();
+  const int rows = launch_rows(rows_dev, cap);
   const int vec_per_row = d >> 2;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)rows * vec_per_row) return;
@@ -169,12 +177,15 @@ __device__ __forceinline__ void ln_stats_and_store(float* tile, int nrows, int d
 
 __global__ void __launch_bounds__(kLnThreads) residual_ln_kernel(
     const float* __restrict__ a, int lda, const float* __restrict__ r, int ldr,
-    const float* __restrict__ gamma, const float* __restrict__ beta, int rows, int d,
-    float* __restrict__ out, QuantOut q, uint32_t* status) {
+    const float* __restrict__ gamma, const float* __restrict__ beta, int cap,
+    const int32_t* __restrict__ rows_dev, int d, float* __restrict__ out, QuantOut q,
+    uint32_t* status) {
   pdl_enter();
-  extern __shared__ float tile[];  // [kLnRows][d + 1]
+  extern __shared__ float tile[];  // [kLnRows][d + 4]
+  const int rows = launch_rows(rows_dev, cap);
   const int row0 = blockIdx.x * kLnRows;
   const int nrows = min(kLnRows, rows - row0);
+  if (nrows <= 0) return;
   const int vec = d >> 2, ld = d + 4;
 #pragma unroll 4
   for (int idx = threadIdx.x; idx < nrows * vec; idx += blockDim.x) {
@@ -193,12 +204,15 @@ __global__ void __launch_bounds__(kLnThreads) residual_ln_kernel(
 __global__ void __launch_bounds__(kLnThreads) ssru_kernel(
     const float* __restrict__ cf, int ld_cf, int fcol, float* __restrict__ state,
     const int32_t* __restrict__ row_slot, const float* __restrict__ residual,
-    const float* __restrict__ gamma, const float* __restrict__ beta, int rows, int d,
-    float* __restrict__ out, QuantOut q, uint32_t* status) {
+    const float* __restrict__ gamma, const float* __restrict__ beta, int cap,
+    const int32_t* __restrict__ rows_dev, int d, float* __restrict__ out, QuantOut q,
+    uint32_t* status) {
   pdl_enter();
   extern __shared__ float tile[];
+  const int rows = launch_rows(rows_dev, cap);
   const int row0 = blockIdx.x * kLnRows;
   const int nrows = min(kLnRows, rows - row0);
+  if (nrows <= 0) return;
   const int ld = d + 4;
 #pragma unroll 4
   for (int idx = threadIdx.x; idx < nrows * d; idx += blockDim.x) {
@@ -353,96 +367,142 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
   }
 }
 
-// Decode: one CTA per active row (taken in row_order, longest rows first,
-// so long rows start in the first wave), one warp per head.  Each lane
-// scores its own keys with an in-order dot product; lane 0 sums the
-// exponentials in key order; each lane accumulates output dims 2*lane and
-// 2*lane + 1 over the keys in order, with 16 keys' values fetched ahead.
-// Cache rows come from the slot's page table.
+// Decode: one CTA of 4 warps per (active row, group of 4 heads); warp h of
+// the CTA is head 4 * blockIdx.y + h.  Rows are taken in row_order (longest
+// first, so long rows start in the first wave).  The group's slices of the
+// cached keys, then values, are staged in shared memory 64 keys at a time
+// with 16-byte cp.async copies: each key's slice of the group is
+// 4 * HD * 4 contiguous bytes of a page row, so every copy instruction of a
+// warp reads whole 128-byte lines.  Rows in shared memory are padded by 16
+// bytes so the lanes' 128-bit reads of different keys fall on distinct
+// banks.  Per head the operation order is the reference's: lane t scores
+// key t with an in-order dot product, max, exp, a left-to-right sum by
+// lane 0, scaling, and a left-to-right weighted sum of V per output dim
+// (lane i owns dims 2i and 2i + 1).
+constexpr int kDecGroup = 4;   // heads per CTA
+constexpr int kDecChunk = 64;  // keys staged per round
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Copies the group's slice of cache rows rows_s[c0 .. c0 + n) into
+// stage[t][0 .. W) (row stride W + 4 floats).
+template <int W>
+__device__ __forceinline__ void stage_rows(float* stage, const float* __restrict__ pool,
+                                           const int* rows_s, int c0, int n, int d, int col0) {
+  constexpr int kVec = W / 4;
+  for (int idx = threadIdx.x; idx < n * kVec; idx += kDecGroup * 32) {
+    const int t = idx / kVec, c = (idx - t * kVec) * 4;
+    cp_async16(stage + t * (W + 4) + c, pool + (size_t)rows_s[c0 + t] * d + col0 + c);
+  }
+}
+
 template <int HD>
-__global__ void __launch_bounds__(256) attn_decode_kernel(
-    const float* __restrict__ q, int ldq, const int32_t* __restrict__ row_slot,
+__global__ void __launch_bounds__(kDecGroup * 32) attn_decode_kernel(
+    const float* __restrict__ q, int ldq, const int32_t* __restrict__ rows_dev, int cap,
+    const int32_t* __restrict__ row_slot,
     const int32_t* __restrict__ row_order, const int32_t* __restrict__ slot_len, int len_add,
     const int32_t* __restrict__ page_table, int pages_per_slot, int page_tokens,
     const float* __restrict__ k_pool, const float* __restrict__ v_pool, int d, int heads,
     int8_t* __restrict__ out_q, float alpha, uint32_t* status) {
+  constexpr int W = kDecGroup * HD;
+  constexpr int SLD = W + 4;
   pdl_enter();
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float dsm[];
+  if ((int)blockIdx.x >= launch_rows(rows_dev, cap)) return;
   const int r = row_order ? row_order[blockIdx.x] : blockIdx.x;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int col0 = blockIdx.y * W;  // first column of this head group
   const int slot = row_slot[r];
   const int len = slot_len[slot] + len_add;
   if (len <= 0 || len > kMaxSeq || len > pages_per_slot * page_tokens) {
     if (threadIdx.x == 0) flag_status(status, kStatusBadIndex);
     return;
   }
-  float* qw = sm + h * HD;                        // [heads][HD]
-  float* pw = sm + heads * HD + h * kMaxSeq;      // [heads][kMaxSeq]
-  int* rows_s = reinterpret_cast<int*>(sm + heads * HD + heads * kMaxSeq);  // [kMaxSeq]
+  float* stage = dsm;                                  // [kDecChunk][W + 4]
+  float* qs = stage + kDecChunk * SLD;                 // [4][HD]
+  float* ps = qs + W;                                  // [4][kMaxSeq]
+  int* rows_s = reinterpret_cast<int*>(ps + kDecGroup * kMaxSeq);  // [kMaxSeq]
   const int32_t* pages = page_table + (size_t)slot * pages_per_slot;
   for (int j = threadIdx.x; j < len; j += blockDim.x)
     rows_s[j] = pages[j / page_tokens] * page_tokens + j % page_tokens;
-  for (int i = lane; i < HD; i += 32) qw[i] = q[(size_t)r * ldq + h * HD + i];
+  for (int i = threadIdx.x; i < W; i += blockDim.x) qs[i] = q[(size_t)r * ldq + col0 + i];
   __syncthreads();
+  const float* qh = qs + h * HD;
+  float* ph = ps + h * kMaxSeq;
   const float scale = 1.0f / sqrtf((float)HD);
   float mx = -INFINITY;
-  for (int j = lane; j < len; j += 32) {
-    const float* kr = k_pool + (size_t)rows_s[j] * d + h * HD;
-    float dot = 0.0f;
+  for (int c0 = 0; c0 < len; c0 += kDecChunk) {
+    const int n = min(kDecChunk, len - c0);
+    stage_rows<W>(stage, k_pool, rows_s, c0, n, d, col0);
+    cp_async_wait_all();
+    __syncthreads();
 #pragma unroll
-    for (int i = 0; i < HD; i += 4) {
-      const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
-      const float4 q4 = *reinterpret_cast<const float4*>(qw + i);
-      dot = dot + q4.x * k4.x;
-      dot = dot + q4.y * k4.y;
-      dot = dot + q4.z * k4.z;
-      dot = dot + q4.w * k4.w;
+    for (int u = 0; u < kDecChunk / 32; ++u) {
+      const int t = lane + 32 * u;
+      if (t < n) {
+        const float* kr = stage + t * SLD + h * HD;
+        float dot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < HD; i += 4) {
+          const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
+          const float4 q4 = *reinterpret_cast<const float4*>(qh + i);
+          dot = dot + q4.x * k4.x;
+          dot = dot + q4.y * k4.y;
+          dot = dot + q4.z * k4.z;
+          dot = dot + q4.w * k4.w;
+        }
+        const float sc = dot * scale;
+        ph[c0 + t] = sc;
+        mx = fmaxf(mx, sc);
+      }
     }
-    const float sc = dot * scale;
-    pw[j] = sc;
-    mx = fmaxf(mx, sc);
+    __syncthreads();  // the stage is refilled next
   }
+  // the first value rows load while the softmax runs
+  stage_rows<W>(stage, v_pool, rows_s, 0, min(kDecChunk, len), d, col0);
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  for (int j = lane; j < len; j += 32) pw[j] = exp_f32(pw[j] - mx);
+  for (int j = lane; j < len; j += 32) ph[j] = exp_f32(ph[j] - mx);
   __syncwarp();
   float inv = 0.0f;
   if (lane == 0) {
     float sum = 0.0f;
 #pragma unroll 8
-    for (int j = 0; j < len; ++j) sum = sum + pw[j];
+    for (int j = 0; j < len; ++j) sum = sum + ph[j];
     inv = 1.0f / sum;
   }
   inv = __shfl_sync(0xffffffffu, inv, 0);
-  for (int j = lane; j < len; j += 32) pw[j] = pw[j] * inv;
+  for (int j = lane; j < len; j += 32) ph[j] = ph[j] * inv;
   __syncwarp();
   const bool active = 2 * lane < HD;
-  const float* vbase = v_pool + h * HD + 2 * lane;
   float acc0 = 0.0f, acc1 = 0.0f;
-  int j = 0;
-  for (; j + 16 <= len; j += 16) {
-    float2 v2[16];
-#pragma unroll
-    for (int u = 0; u < 16; ++u)
-      v2[u] = active ? *reinterpret_cast<const float2*>(vbase + (size_t)rows_s[j + u] * d)
-                     : make_float2(0.f, 0.f);
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const float p = pw[j + u];
-      acc0 = acc0 + v2[u].x * p;
-      acc1 = acc1 + v2[u].y * p;
+  for (int c0 = 0; c0 < len; c0 += kDecChunk) {
+    const int n = min(kDecChunk, len - c0);
+    if (c0 > 0) stage_rows<W>(stage, v_pool, rows_s, c0, n, d, col0);
+    cp_async_wait_all();
+    __syncthreads();
+    if (active) {
+      const float* vb = stage + h * HD + 2 * lane;
+#pragma unroll 8
+      for (int t = 0; t < n; ++t) {
+        const float2 v2 = *reinterpret_cast<const float2*>(vb + t * SLD);
+        const float p = ph[c0 + t];
+        acc0 = acc0 + v2.x * p;
+        acc1 = acc1 + v2.y * p;
+      }
     }
-  }
-  for (; j < len; ++j) {
-    const float2 v = active ? *reinterpret_cast<const float2*>(vbase + (size_t)rows_s[j] * d)
-                            : make_float2(0.f, 0.f);
-    const float p = pw[j];
-    acc0 = acc0 + v.x * p;
-    acc1 = acc1 + v.y * p;
+    __syncthreads();
   }
   if (active) {
     const uint16_t w2 = (uint16_t)(uint8_t)quantize_one(acc0, alpha, status) |
                         ((uint16_t)(uint8_t)quantize_one(acc1, alpha, status) << 8);
-    *reinterpret_cast<uint16_t*>(out_q + (size_t)r * d + h * HD + 2 * lane) = w2;
+    *reinterpret_cast<uint16_t*>(out_q + (size_t)r * d + col0 + h * HD + 2 * lane) = w2;
   }
 }
 
@@ -461,13 +521,14 @@ __global__ void quantize_kernel(const float* __restrict__ x, long long n4, float
 }
 
 // ---- token selection ----------------------------------------------------------
-__global__ void finalize_kernel(int rows, const int32_t* __restrict__ row_slot,
+__global__ void finalize_kernel(int cap, const int32_t* __restrict__ rows_dev,
+                                const int32_t* __restrict__ row_slot,
                                 unsigned long long* __restrict__ best, int32_t* slot_prev,
                                 int32_t* slot_step, const int32_t* __restrict__ slot_limit,
                                 int32_t* step_tokens, uint8_t* done, uint32_t* status) {
   pdl_enter();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= rows) return;
+  if (r >= launch_rows(rows_dev, cap)) return;
   const int slot = row_slot[r];
   const unsigned long long key = best[r];
   best[r] = 0ull;
@@ -488,11 +549,20 @@ __global__ void init_slots_kernel(int n, const int32_t* slots, const int32_t* li
                                   const int32_t* force, const int32_t* src_len, int32_t* slot_prev,
                                   int32_t* slot_step, int32_t* slot_limit, int32_t* slot_force,
                                   int32_t* slot_src, float* ssru_state, int layers, int max_slots,
-                                  int d) {
+                                  int d, const int32_t* __restrict__ page_rows, int32_t* cross_pages,
+                                  int32_t* self_pages, int pages_per_slot) {
   pdl_enter();
   const int i = blockIdx.x;
   if (i >= n) return;
   const int s = slots[i];
+  // page-table rows of the admitted slot: [n][pages_per_slot] cross, then
+  // [n][pages_per_slot] self
+  for (int k = threadIdx.x; k < pages_per_slot; k += blockDim.x) {
+    cross_pages[(size_t)s * pages_per_slot + k] = page_rows[(size_t)i * pages_per_slot + k];
+    if (self_pages)
+      self_pages[(size_t)s * pages_per_slot + k] =
+          page_rows[((size_t)n + i) * pages_per_slot + k];
+  }
   if (threadIdx.x == 0) {
     slot_prev[s] = -1;
     slot_step[s] = 0;
@@ -522,7 +592,8 @@ void launch_embed_encoder(const int32_t* tokens, const int32_t* pos_idx, int n_t
              emb_mult, emb_scale, positions, d, x, q, status);
 }
 
-void launch_embed_decoder(int rows, const int32_t* row_slot, const int32_t* slot_prev,
+void launch_embed_decoder(int rows, const int32_t* rows_dev, const int32_t* row_slot,
+                          const int32_t* slot_prev,
                           const int32_t* slot_step, const int32_t* slot_force, const int8_t* emb,
                           float emb_mult, float emb_scale, const float* positions, int d, float* x,
                           const QuantOut& q, uint8_t* eos_mask, const int32_t* self_pages,
@@ -530,31 +601,32 @@ void launch_embed_decoder(int rows, const int32_t* row_slot, const int32_t* slot
                           uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return;
   const long long n = (long long)rows * (d / 4);
-  launch_pdl(embed_decoder_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, s, 
-      rows, row_slot, slot_prev, slot_step, slot_force, emb, emb_mult, emb_scale, positions, d, x,
+  launch_pdl(embed_decoder_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, s,
+      rows, rows_dev, row_slot, slot_prev, slot_step, slot_force, emb, emb_mult, emb_scale, positions, d, x,
       q, eos_mask, self_pages, pages_per_slot, page_tokens, self_row_map, status);
 }
 
 void launch_residual_ln(const float* a, int lda, const float* r, int ldr, const float* gamma,
-                        const float* beta, int rows, int d, float* out, const QuantOut& q,
-                        uint32_t* status, cudaStream_t s) {
+                        const float* beta, int rows, const int32_t* rows_dev, int d, float* out,
+                        const QuantOut& q, uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return;
   const size_t smem = sizeof(float) * kLnRows * (d + 4);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(residual_ln_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   launch_pdl(residual_ln_kernel, dim3(blocks_for(rows, kLnRows)), dim3(kLnThreads), smem, s, a, lda, r, ldr, gamma, beta,
-                                                                         rows, d, out, q, status);
+             rows, rows_dev, d, out, q, status);
 }
 
 void launch_ssru(const float* cf, int ld, int fcol, float* state, const int32_t* row_slot,
-                 const float* residual, const float* gamma, const float* beta, int rows, int d,
-                 float* out, const QuantOut& q, uint32_t* status, cudaStream_t s) {
+                 const float* residual, const float* gamma, const float* beta, int rows,
+                 const int32_t* rows_dev, int d, float* out, const QuantOut& q, uint32_t* status,
+                 cudaStream_t s) {
   if (rows <= 0) return;
   const size_t smem = sizeof(float) * kLnRows * (d + 4);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(ssru_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   launch_pdl(ssru_kernel, dim3(blocks_for(rows, kLnRows)), dim3(kLnThreads), smem, s, cf, ld, fcol, state, row_slot, residual,
-                                                                  gamma, beta, rows, d, out, q, status);
+             gamma, beta, rows, rows_dev, d, out, q, status);
 }
 
 template <int HD>
@@ -589,34 +661,45 @@ cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens,
   }
 }
 
-cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t* row_slot,
-                               const int32_t* row_order, const int32_t* slot_len, int len_add,
-                               const int32_t* page_table, int pages_per_slot, int page_tokens,
-                               const float* k_pool, const float* v_pool, int d, int heads,
-                               int8_t* out_q, float alpha, uint32_t* status, cudaStream_t s) {
-  if (rows <= 0) return cudaSuccess;
-  const int hd = d / heads;
-  const size_t smem = sizeof(float) * ((size_t)heads * hd + (size_t)heads * kMaxSeq + kMaxSeq);
-  switch (hd) {
-    case 32:
-      launch_pdl(attn_decode_kernel<32>, dim3(rows), dim3(heads * 32), smem, s, q, ldq, row_slot, row_order, slot_len, len_add,
-                                                           page_table, pages_per_slot, page_tokens, k_pool,
-                                                           v_pool, d, heads, out_q, alpha, status);
-      break;
-    case 48:
-      launch_pdl(attn_decode_kernel<48>, dim3(rows), dim3(heads * 32), smem, s, q, ldq, row_slot, row_order, slot_len, len_add,
-                                                           page_table, pages_per_slot, page_tokens, k_pool,
-                                                           v_pool, d, heads, out_q, alpha, status);
-      break;
-    case 64:
-      launch_pdl(attn_decode_kernel<64>, dim3(rows), dim3(heads * 32), smem, s, q, ldq, row_slot, row_order, slot_len, len_add,
-                                                           page_table, pages_per_slot, page_tokens, k_pool,
-                                                           v_pool, d, heads, out_q, alpha, status);
-      break;
-    default:
-      return cudaErrorInvalidValue;
+template <int HD>
+cudaError_t launch_attn_decode_hd(const float* q, int ldq, int rows, const int32_t* rows_dev,
+                                  const int32_t* row_slot, const int32_t* row_order,
+                                  const int32_t* slot_len, int len_add, const int32_t* page_table,
+                                  int pages_per_slot, int page_tokens, const float* k_pool,
+                                  const float* v_pool, int d, int heads, int8_t* out_q,
+                                  float alpha, uint32_t* status, cudaStream_t s) {
+  constexpr int W = kDecGroup * HD;
+  const size_t smem = sizeof(float) * ((size_t)kDecChunk * (W + 4) + W + (size_t)kDecGroup * kMaxSeq) +
+                      sizeof(int) * kMaxSeq;
+  static unsigned long long configured = 0;  // one bit per device ordinal
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1ull << (dev & 63)))) {
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured |= 1ull << (dev & 63);
   }
+  launch_pdl(attn_decode_kernel<HD>, dim3(rows, heads / kDecGroup), dim3(kDecGroup * 32), smem, s, q,
+             ldq, rows_dev, rows, row_slot, row_order, slot_len, len_add, page_table,
+             pages_per_slot, page_tokens, k_pool, v_pool, d, heads, out_q, alpha, status);
   return cudaGetLastError();
+}
+
+cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t* rows_dev,
+                               const int32_t* row_slot, const int32_t* row_order,
+                               const int32_t* slot_len, int len_add, const int32_t* page_table,
+                               int pages_per_slot, int page_tokens, const float* k_pool,
+                               const float* v_pool, int d, int heads, int8_t* out_q, float alpha,
+                               uint32_t* status, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  if (heads % kDecGroup != 0 || d != heads * (d / heads)) return cudaErrorInvalidValue;
+  switch (d / heads) {
+    case 32: return launch_attn_decode_hd<32>(q, ldq, rows, rows_dev, row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, page_tokens, k_pool, v_pool, d, heads, out_q, alpha, status, s);
+    case 48: return launch_attn_decode_hd<48>(q, ldq, rows, rows_dev, row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, page_tokens, k_pool, v_pool, d, heads, out_q, alpha, status, s);
+    case 64: return launch_attn_decode_hd<64>(q, ldq, rows, rows_dev, row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, page_tokens, k_pool, v_pool, d, heads, out_q, alpha, status, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 void launch_quantize(const float* x, long long n, float alpha, int8_t* out, uint32_t* status,
@@ -626,22 +709,25 @@ void launch_quantize(const float* x, long long n, float alpha, int8_t* out, uint
   launch_pdl(quantize_kernel, dim3(blocks_for(n4, 256)), dim3(256), 0, s, x, n4, alpha, out, status);
 }
 
-void launch_finalize(int rows, const int32_t* row_slot, unsigned long long* best,
+void launch_finalize(int rows, const int32_t* rows_dev, const int32_t* row_slot,
+                     unsigned long long* best,
                      int32_t* slot_prev, int32_t* slot_step, const int32_t* slot_limit,
                      int32_t* step_tokens, uint8_t* done, uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return;
-  launch_pdl(finalize_kernel, dim3(blocks_for(rows, 128)), dim3(128), 0, s, rows, row_slot, best, slot_prev, slot_step,
+  launch_pdl(finalize_kernel, dim3(blocks_for(rows, 128)), dim3(128), 0, s, rows, rows_dev, row_slot, best, slot_prev, slot_step,
                                                         slot_limit, step_tokens, done, status);
 }
 
 void launch_init_slots(int n, const int32_t* slots, const int32_t* limits, const int32_t* force,
                        const int32_t* src_len, int32_t* slot_prev, int32_t* slot_step,
                        int32_t* slot_limit, int32_t* slot_force, int32_t* slot_src,
-                       float* ssru_state, int layers, int max_slots, int d, cudaStream_t s) {
+                       float* ssru_state, int layers, int max_slots, int d,
+                       const int32_t* page_rows, int32_t* cross_pages, int32_t* self_pages,
+                       int pages_per_slot, cudaStream_t s) {
   if (n <= 0) return;
   launch_pdl(init_slots_kernel, dim3(n), dim3(128), 0, s, n, slots, limits, force, src_len, slot_prev, slot_step,
                                       slot_limit, slot_force, slot_src, ssru_state, layers,
-                                      max_slots, d);
+             max_slots, d, page_rows, cross_pages, self_pages, pages_per_slot);
 }
 
 }  // namespace mc

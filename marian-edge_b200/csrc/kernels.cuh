@@ -35,7 +35,13 @@ void launch_embed_encoder(const int32_t* tokens, const int32_t* pos_idx, int n_t
 // q8_engine.rs:605-630 for one decode step of the active rows.  Also writes
 // the per-row EOS mask (harness rule) and the self-attention cache row of
 // this step (when self_pages != nullptr).
-void launch_embed_decoder(int rows, const int32_t* row_slot, const int32_t* slot_prev,
+//
+// Decode-step launchers take `rows` (the grid's row capacity) and a nullable
+// device row count `rows_dev` that, when given, the kernels read and clamp
+// to rows: a CUDA graph captured once for a lane's capacity then serves
+// every active-row count.
+void launch_embed_decoder(int rows, const int32_t* rows_dev, const int32_t* row_slot,
+                          const int32_t* slot_prev,
                           const int32_t* slot_step, const int32_t* slot_force, const int8_t* emb,
                           float emb_mult, float emb_scale, const float* positions, int d, float* x,
                           const QuantOut& q, uint8_t* eos_mask, const int32_t* self_pages,
@@ -44,15 +50,16 @@ void launch_embed_decoder(int rows, const int32_t* row_slot, const int32_t* slot
 
 // tensor.rs:132-155: out = LN(a + r) (eps 1e-6) plus quantized copies.
 void launch_residual_ln(const float* a, int lda, const float* r, int ldr, const float* gamma,
-                        const float* beta, int rows, int d, float* out, const QuantOut& q,
-                        uint32_t* status, cudaStream_t s);
+                        const float* beta, int rows, const int32_t* rows_dev, int d, float* out,
+                        const QuantOut& q, uint32_t* status, cudaStream_t s);
 
 // tensor.rs:184-218: SSRU gate/state update, ReLU + residual, LN, quantized
 // copies.  cand/fpre are [rows, ld] with the candidate at column 0 and the
 // forget pre-activation at column fcol; state is [slots, d] indexed by slot.
 void launch_ssru(const float* cf, int ld, int fcol, float* state, const int32_t* row_slot,
-                 const float* residual, const float* gamma, const float* beta, int rows, int d,
-                 float* out, const QuantOut& q, uint32_t* status, cudaStream_t s);
+                 const float* residual, const float* gamma, const float* beta, int rows,
+                 const int32_t* rows_dev, int d, float* out, const QuantOut& q, uint32_t* status,
+                 cudaStream_t s);
 
 // tensor.rs:251-318 for packed varlen sequences (no padding): qkv is
 // [tokens, 3d] (Q | K | V), cu_seqlens [batch+1]; this launch covers the
@@ -66,7 +73,8 @@ cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens,
 // are cache rows page_table[slot][j / page_tokens] * page_tokens +
 // j % page_tokens for j < slot_len[slot] + len_add.
 // row_order (nullable) lists the rows in the order CTAs take them.
-cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t* row_slot,
+cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t* rows_dev,
+                               const int32_t* row_slot,
                                const int32_t* row_order, const int32_t* slot_len, int len_add,
                                const int32_t* page_table, int pages_per_slot, int page_tokens,
                                const float* k_pool, const float* v_pool, int d, int heads,
@@ -75,7 +83,8 @@ cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t*
 // Turns the packed per-row maxima into tokens (q8_engine.rs:437-449):
 // advances each slot's step/previous token, reports the token and whether
 // the row finished (token 0 or its limit), and clears the maxima.
-void launch_finalize(int rows, const int32_t* row_slot, unsigned long long* best,
+void launch_finalize(int rows, const int32_t* rows_dev, const int32_t* row_slot,
+                     unsigned long long* best,
                      int32_t* slot_prev, int32_t* slot_step, const int32_t* slot_limit,
                      int32_t* step_tokens, uint8_t* done, uint32_t* status, cudaStream_t s);
 
@@ -85,10 +94,14 @@ void launch_quantize(const float* x, long long n, float alpha, int8_t* out, uint
                      cudaStream_t s);
 
 // Initializes newly admitted slots: prev = -1, step = 0, limit, force_len,
-// source length, SSRU states zeroed (state pools [layers][slots][d]).
+// source length, SSRU states zeroed (state pools [layers][slots][d]), and
+// copies each slot's page-table rows from page_rows ([n][pages_per_slot]
+// cross pages, then [n][pages_per_slot] self pages; self_pages nullable).
 void launch_init_slots(int n, const int32_t* slots, const int32_t* limits, const int32_t* force,
                        const int32_t* src_len, int32_t* slot_prev, int32_t* slot_step,
                        int32_t* slot_limit, int32_t* slot_force, int32_t* slot_src,
-                       float* ssru_state, int layers, int max_slots, int d, cudaStream_t s);
+                       float* ssru_state, int layers, int max_slots, int d,
+                       const int32_t* page_rows, int32_t* cross_pages, int32_t* self_pages,
+                       int pages_per_slot, cudaStream_t s);
 
 }  // namespace mc

@@ -254,8 +254,6 @@ __global__ void __launch_bounds__(kThreads, 2) q8_gemm_kernel(const __grid_const
   const int lane = threadIdx.x & 31;
   const int num_kb = (p.k + kBK - 1) / kBK;
   const int n_tiles = (p.max_n + BN - 1) / BN;
-  const int m_tiles = (p.m + kBM - 1) / kBM;
-  const int total = n_tiles * m_tiles * p.num_groups;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -281,6 +279,9 @@ __global__ void __launch_bounds__(kThreads, 2) q8_gemm_kernel(const __grid_const
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_s;
   pdl_enter();  // set-up above overlaps the previous kernel's tail
+  const int m = p.m_dev ? max(0, min(*p.m_dev, p.m)) : p.m;
+  const int m_tiles = (m + kBM - 1) / kBM;
+  const int total = n_tiles * m_tiles * p.num_groups;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -347,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 2) q8_gemm_kernel(const __grid_const
       if (!ready) break;
       tc_fence_after();
       const int row = c.m0 + quarter * 32 + lane;
-      const bool row_ok = row < p.m;
+      const bool row_ok = row < m;
       const int dest_row = row_ok ? (g.row_map ? g.row_map[row] : row) : 0;
       const float row_scale = (row_ok && g.row_scale) ? g.row_scale[row] : 1.0f;
       float best = -INFINITY;
@@ -398,17 +399,25 @@ int num_sms() {
 }
 
 template <int BN, int MAX_STAGES>
-cudaError_t launch_impl(GemmParams p, cudaStream_t stream) {
-  auto kern = q8_gemm_kernel<BN, MAX_STAGES>;
+cudaError_t configure_impl() {
   static unsigned long long configured = 0;  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured & (1ull << (dev & 63)))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(q8_gemm_kernel<BN, MAX_STAGES>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          MAX_STAGES * stage_bytes<BN>() + kStagingBytes + 1024);
     if (e != cudaSuccess) return e;
     configured |= 1ull << (dev & 63);
   }
+  return cudaSuccess;
+}
+
+template <int BN, int MAX_STAGES>
+cudaError_t launch_impl(GemmParams p, cudaStream_t stream) {
+  auto kern = q8_gemm_kernel<BN, MAX_STAGES>;
+  cudaError_t ce = configure_impl<BN, MAX_STAGES>();
+  if (ce != cudaSuccess) return ce;
   const int num_kb = (p.k + kBK - 1) / kBK;
   const int tiles = ((p.max_n + BN - 1) / BN) * ((p.m + kBM - 1) / kBM) * p.num_groups;
   // Two CTAs per SM for the narrow tile when a 3-stage ring covers short K.
@@ -460,6 +469,14 @@ int pick_bn(int m, int max_n) {
   if (m_tiles * ((max_n + 255) / 256) >= 148) return 256;
   if (m_tiles * ((max_n + 127) / 128) >= 148) return 128;
   return 64;
+}
+
+cudaError_t prepare_q8_gemm() {
+  num_sms();
+  cudaError_t e = configure_impl<256, 3>();
+  if (e == cudaSuccess) e = configure_impl<128, 5>();
+  if (e == cudaSuccess) e = configure_impl<64, 7>();
+  return e;
 }
 
 cudaError_t launch_q8_gemm(const GemmParams& p, int bn, cudaStream_t stream) {

@@ -48,7 +48,9 @@ constexpr int kMaxGemmGroups = 3;
 
 struct GemmParams {
   GemmGroup g[kMaxGemmGroups];
-  int32_t m;           // rows of A actually used
+  int32_t m;           // rows of A actually used (the capacity when m_dev is set)
+  const int32_t* m_dev;  // nullable: device row count, read by the kernel and
+                         // clamped to m (launches replayed from a CUDA graph)
   int32_t k;           // inner dimension (multiple of 16)
   int32_t num_groups;
   int32_t max_n;       // max over groups of n
@@ -64,6 +66,10 @@ bool encode_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
 
 // Picks the N tile (64, 128 or 256) for a launch.
 int pick_bn(int m, int max_n);
+
+// Sets the kernels' shared-memory limits on the current device (done before
+// any stream capture; launch_q8_gemm does it on first use otherwise).
+cudaError_t prepare_q8_gemm();
 
 // Launches the grouped GEMM.  The tensor maps in p must have been encoded with
 // box_rows == 128 for A and box_rows == bn for B.

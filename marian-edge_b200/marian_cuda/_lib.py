@@ -30,7 +30,8 @@ KERNEL_KINDS = ["embed", "gemm_qkv", "gemm_out", "gemm_ffn1", "gemm_ffn2", "gemm
 
 class Config(C.Structure):
     _fields_ = [("device", C.c_int32), ("max_inflight", C.c_uint32), ("max_encode_tokens", C.c_uint32),
-                ("page_tokens", C.c_uint32), ("kv_pages", C.c_uint32), ("max_length_factor", C.c_uint32)]
+                ("page_tokens", C.c_uint32), ("kv_pages", C.c_uint32), ("max_length_factor", C.c_uint32),
+                ("lanes", C.c_uint32)]
 
 
 class ModelInfo(C.Structure):

@@ -40,12 +40,14 @@ class BackendInfo:
 class CudaEngine:
     def __init__(self, model_bytes: bytes, device: int = 0, max_inflight: int = 1024,
                  max_encode_tokens: int = 65536, page_tokens: int = 16, kv_pages: int = 0,
-                 max_length_factor: int = 3):
+                 max_length_factor: int = 3, lanes: int = 0):
         self._lib = L.load()
         cfg = L.Config()
         self._lib.mc_config_default(C.byref(cfg))
         cfg.device, cfg.max_inflight, cfg.max_encode_tokens = device, max_inflight, max_encode_tokens
         cfg.page_tokens, cfg.kv_pages, cfg.max_length_factor = page_tokens, kv_pages, max_length_factor
+        if lanes:
+            cfg.lanes = lanes
         h = C.c_void_p()
         L.check(self._lib.mc_create(C.byref(cfg), C.byref(h)))
         self._h = h
