@@ -162,8 +162,8 @@ struct mc_engine {
   float enc_emb_mult = 1.0f;
   int8_t* dec_emb = nullptr;
   float dec_emb_mult = 1.0f;
-  DevLinear vocab;  // tied output projection over decoder_Wemb
-  uint32_t* cand_bits = nullptr;
+  DevLinear vocab;  // tied output projection over decoder_Wemb; its bias is
+                    // candidate-masked (-inf at excluded ids) and padded
   float* positions = nullptr;
   std::vector<DevAttention> enc_attn, dec_self, dec_ctx;
   std::vector<DevFfn> enc_ffn, dec_ffn;
@@ -401,7 +401,6 @@ mc_status gemm(mc_engine* e, Lane& L, int kind, int m, const int32_t* m_dev, dou
     g.mode = s.mode;
     g.relu = s.relu;
     g.argmax = argmax;
-    g.cand_bits = e->cand_bits;
     g.eos_mask = eos;
   }
   p.m = m;
@@ -1222,18 +1221,21 @@ extern "C" mc_status mc_load_marian_bin(mc_engine* e, const uint8_t* bytes, size
     std::vector<float> cs(e->vtgt, v.scale);
     CK(dalloc(e, &v.col_scale, cs.size()));
     CK(h2d(e, v.col_scale, cs.data(), cs.size() * 4));
-    if ((st = upload_f32(e, "decoder_ff_logit_out_b", &v.bias))) return st;
     for (int i = 0; i < 3; ++i)
       if (!encode_tmap_i8(&v.tmap_b[i], v.w, v.out, v.in, kBNs[i]))
         return fail(e, MC_MODEL, "vocabulary tensor map rejected");
-    // full-vocabulary candidates: every id but 1 and 7..38 (shortlist.rs:150-198)
-    std::vector<uint32_t> bits((e->vtgt + 31) / 32, 0xFFFFFFFFu);
-    if (e->vtgt % 32) bits.back() = (1u << (e->vtgt % 32)) - 1u;
-    auto clear = [&](int id) { bits[id >> 5] &= ~(1u << (id & 31)); };
-    if (e->vtgt > 1) clear(1);
-    for (int id = 7; id < std::min(e->vtgt, 39); ++id) clear(id);
-    CK(dalloc(e, &e->cand_bits, bits.size()));
-    CK(h2d(e, e->cand_bits, bits.data(), bits.size() * 4));
+    // full-vocabulary candidates: every id but 1 and 7..38 (shortlist.rs:150-198),
+    // folded into the bias: a non-candidate logit is -inf and never wins the
+    // strict '>' argmax; the bias is padded with -inf to whole 32-id chunks
+    const HostTensor& tb = m.tensors.at("decoder_ff_logit_out_b");
+    if ((int)tb.f32.size() != e->vtgt) return fail(e, MC_MODEL, "decoder_ff_logit_out_b has the wrong size");
+    std::vector<float> masked((size_t)(e->vtgt + 255) / 256 * 256, -INFINITY);
+    for (int id = 0; id < e->vtgt; ++id) masked[id] = tb.f32[id];
+    if (e->vtgt > 1) masked[1] = -INFINITY;
+    for (int id = 7; id < std::min(e->vtgt, 39); ++id) masked[id] = -INFINITY;
+    CK(dalloc(e, &v.bias, masked.size()));
+    CK(h2d(e, v.bias, masked.data(), masked.size() * 4));
+    e->weight_bytes += (size_t)e->vtgt * 4;
   }
   std::vector<float> pos = sinusoidal_positions(d);
   CK(dalloc(e, &e->positions, pos.size()));

@@ -44,7 +44,7 @@ __global__ void embed_encoder_kernel(const int32_t* __restrict__ tokens,
                                      const int32_t* __restrict__ pos_idx, int n_tokens,
                                      const int8_t* __restrict__ emb, float emb_mult,
                                      float emb_scale, const float* __restrict__ positions, int d,
-                                     float* __restrict__ x, QuantOut q, uint32_t* status) {
+                                     float* __restrict__ x, const __grid_constant__ QuantOut q, uint32_t* status) {
   pdl_enter();
   const int vec_per_row = d >> 2;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -72,7 +72,7 @@ __global__ void embed_decoder_kernel(int cap, const int32_t* __restrict__ rows_d
                                      const int32_t* __restrict__ slot_force,
                                      const int8_t* __restrict__ emb, float emb_mult,
                                      float emb_scale, const float* __restrict__ positions, int d,
-                                     float* __restrict__ x, QuantOut q, uint8_t* eos_mask,
+                                     float* __restrict__ x, const __grid_constant__ QuantOut q, uint8_t* eos_mask,
                                      const int32_t* __restrict__ self_pages, int pages_per_slot,
                                      int page_tokens, int32_t* self_row_map, uint32_t* status) {
   pdl_enter();
@@ -112,121 +112,152 @@ __global__ void embed_decoder_kernel(int cap, const int32_t* __restrict__ rows_d
 }
 
 // ---- LayerNorm (normalize_row, tensor.rs:372-385) ------------------------------
-// kLnRows rows per CTA are staged in shared memory with coalesced loads (row
-// stride d + 4: 16-byte aligned, and an odd number of 16-byte chunks so the
-// per-row threads' 128-bit reads hit distinct banks).  One thread
-// per row then sums the row left to right and sums the centred squares left
-// to right, exactly as the reference's Iterator::sum; the normalized rows and
-// their quantized copies are written back coalesced.
-constexpr int kLnRows = 8;
-constexpr int kLnThreads = 256;
+// One warp per row.  The lanes load the row with coalesced 128-bit accesses
+// (lane l holds float4 chunks l, l + 32, ...), form the pre-norm values and
+// write them to a per-warp shared-memory row.  Lane 0 then sums the row left
+// to right, exactly as the reference's Iterator::sum; every lane forms its
+// centred squares (x - mean) * (x - mean), the same two roundings as the
+// reference's `var += c * c`, and lane 0 sums those left to right.  Only
+// the two dependent add chains are serial; everything else is spread over
+// the warp.  The normalized values and their quantized copies are written
+// back coalesced.
+constexpr int kLnWarps = 4;
 
-__device__ __forceinline__ void ln_stats_and_store(float* tile, int nrows, int d, int row0,
-                                                   const float* __restrict__ gamma,
-                                                   const float* __restrict__ beta,
-                                                   float* __restrict__ out, const QuantOut& q,
-                                                   uint32_t* status) {
-  __shared__ float s_mean[kLnRows], s_inv[kLnRows];
-  const int ld = d + 4;
-  if (threadIdx.x < nrows) {
-    const float* row = tile + threadIdx.x * ld;
-    float sum = 0.0f;
-#pragma unroll 8
-    for (int i = 0; i < d; i += 4) {
-      const float4 v = *reinterpret_cast<const float4*>(row + i);
-      sum = sum + v.x;
-      sum = sum + v.y;
-      sum = sum + v.z;
-      sum = sum + v.w;
-    }
-    const float fd = (float)d;
-    const float mean = sum / fd;
-    float var = 0.0f;
-#pragma unroll 8
-    for (int i = 0; i < d; i += 4) {
-      const float4 v = *reinterpret_cast<const float4*>(row + i);
-      const float c0 = v.x - mean, c1 = v.y - mean, c2 = v.z - mean, c3 = v.w - mean;
-      var = var + c0 * c0;
-      var = var + c1 * c1;
-      var = var + c2 * c2;
-      var = var + c3 * c3;
-    }
-    var = var / fd;
-    s_mean[threadIdx.x] = mean;
-    s_inv[threadIdx.x] = 1.0f / sqrtf(var + kLnEps);
-  }
-  __syncthreads();
-  const int vec = d >> 2;
+// VPL = float4 chunks per lane = d / 128.
+template <int VPL>
+__device__ __forceinline__ float serial_sum(const float* row) {
+  constexpr int kVec = VPL * 32;  // float4 per row
+  const float4* r4 = reinterpret_cast<const float4*>(row);
+  float sum = 0.0f;
 #pragma unroll 4
-  for (int idx = threadIdx.x; idx < nrows * vec; idx += blockDim.x) {
-    const int rr = idx / vec, c = (idx % vec) * 4;
-    const float4 t = *reinterpret_cast<const float4*>(tile + rr * ld + c);
-    const float mean = s_mean[rr], inv = s_inv[rr];
-    const float4 g = *reinterpret_cast<const float4*>(gamma + c);
-    const float4 b = *reinterpret_cast<const float4*>(beta + c);
+  for (int i = 0; i < kVec; i += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = r4[i + u];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      sum = sum + v[u].x;
+      sum = sum + v[u].y;
+      sum = sum + v[u].z;
+      sum = sum + v[u].w;
+    }
+  }
+  return sum;
+}
+
+// x[k] (this lane's chunks, columns 4 * (lane + 32 k)) hold the pre-norm row;
+// row is the warp's shared-memory row buffer.  Writes out and the quantized
+// copies of global row `grow`.
+template <int VPL>
+__device__ __forceinline__ void ln_row(float4 (&x)[VPL], float* row, int grow,
+                                       const float* __restrict__ gamma,
+                                       const float* __restrict__ beta, float* __restrict__ out,
+                                       const QuantOut& q, uint32_t* status) {
+  constexpr int d = VPL * 128;
+  const int lane = threadIdx.x & 31;
+  float4* r4 = reinterpret_cast<float4*>(row);
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) r4[lane + 32 * k] = x[k];
+  __syncwarp();
+  const float fd = (float)d;
+  float mean = 0.0f;
+  if (lane == 0) mean = serial_sum<VPL>(row) / fd;
+  mean = __shfl_sync(0xffffffffu, mean, 0);
+  float4 c[VPL];
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    c[k] = make_float4(x[k].x - mean, x[k].y - mean, x[k].z - mean, x[k].w - mean);
+  }
+  __syncwarp();  // lane 0 is done reading the row
+#pragma unroll
+  for (int k = 0; k < VPL; ++k)
+    r4[lane + 32 * k] = make_float4(c[k].x * c[k].x, c[k].y * c[k].y, c[k].z * c[k].z, c[k].w * c[k].w);
+  __syncwarp();
+  float inv = 0.0f;
+  if (lane == 0) {
+    const float var = serial_sum<VPL>(row) / fd;
+    inv = 1.0f / sqrtf(var + kLnEps);
+  }
+  inv = __shfl_sync(0xffffffffu, inv, 0);
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int col = 4 * (lane + 32 * k);
+    const float4 g = *reinterpret_cast<const float4*>(gamma + col);
+    const float4 b = *reinterpret_cast<const float4*>(beta + col);
     float4 v;
-    v.x = (t.x - mean) * inv * g.x + b.x;
-    v.y = (t.y - mean) * inv * g.y + b.y;
-    v.z = (t.z - mean) * inv * g.z + b.z;
-    v.w = (t.w - mean) * inv * g.w + b.w;
-    const long long elem = (long long)(row0 + rr) * d + c;
+    v.x = c[k].x * inv * g.x + b.x;
+    v.y = c[k].y * inv * g.y + b.y;
+    v.z = c[k].z * inv * g.z + b.z;
+    v.w = c[k].w * inv * g.w + b.w;
+    const long long elem = (long long)grow * d + col;
     *reinterpret_cast<float4*>(out + elem) = v;
     store_quant4(q, elem, v.x, v.y, v.z, v.w, status);
   }
 }
 
-__global__ void __launch_bounds__(kLnThreads) residual_ln_kernel(
+template <int VPL>
+__global__ void __launch_bounds__(kLnWarps * 32) residual_ln_kernel(
     const float* __restrict__ a, int lda, const float* __restrict__ r, int ldr,
     const float* __restrict__ gamma, const float* __restrict__ beta, int cap,
-    const int32_t* __restrict__ rows_dev, int d, float* __restrict__ out, QuantOut q,
+    const int32_t* __restrict__ rows_dev, float* __restrict__ out, const __grid_constant__ QuantOut q,
     uint32_t* status) {
+  constexpr int d = VPL * 128;
+  __shared__ __align__(16) float rows_s[kLnWarps][d];
   pdl_enter();
-  extern __shared__ float tile[];  // [kLnRows][d + 4]
   const int rows = launch_rows(rows_dev, cap);
-  const int row0 = blockIdx.x * kLnRows;
-  const int nrows = min(kLnRows, rows - row0);
-  if (nrows <= 0) return;
-  const int vec = d >> 2, ld = d + 4;
-#pragma unroll 4
-  for (int idx = threadIdx.x; idx < nrows * vec; idx += blockDim.x) {
-    const int rr = idx / vec, c = (idx % vec) * 4;
-    const float4 x = *reinterpret_cast<const float4*>(a + (size_t)(row0 + rr) * lda + c);
-    const float4 y = *reinterpret_cast<const float4*>(r + (size_t)(row0 + rr) * ldr + c);
-    *reinterpret_cast<float4*>(tile + rr * ld + c) =
-        make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kLnWarps + warp;
+  if (row >= rows) return;
+  float4 x[VPL];
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int col = 4 * (lane + 32 * k);
+    const float4 u = *reinterpret_cast<const float4*>(a + (size_t)row * lda + col);
+    const float4 w = *reinterpret_cast<const float4*>(r + (size_t)row * ldr + col);
+    x[k] = make_float4(u.x + w.x, u.y + w.y, u.z + w.z, u.w + w.w);
   }
-  __syncthreads();
-  ln_stats_and_store(tile, nrows, d, row0, gamma, beta, out, q, status);
+  ln_row<VPL>(x, rows_s[warp], row, gamma, beta, out, q, status);
 }
 
-// tensor.rs:184-218: gate and state update per element (coalesced), then the
-// LayerNorm of ReLU(state) + residual as above.
-__global__ void __launch_bounds__(kLnThreads) ssru_kernel(
+// tensor.rs:184-218: gate and state update per element, then the LayerNorm
+// of ReLU(state) + residual as above.
+template <int VPL>
+__global__ void __launch_bounds__(kLnWarps * 32) ssru_kernel(
     const float* __restrict__ cf, int ld_cf, int fcol, float* __restrict__ state,
     const int32_t* __restrict__ row_slot, const float* __restrict__ residual,
     const float* __restrict__ gamma, const float* __restrict__ beta, int cap,
-    const int32_t* __restrict__ rows_dev, int d, float* __restrict__ out, QuantOut q,
+    const int32_t* __restrict__ rows_dev, float* __restrict__ out, const __grid_constant__ QuantOut q,
     uint32_t* status) {
+  constexpr int d = VPL * 128;
+  __shared__ __align__(16) float rows_s[kLnWarps][d];
   pdl_enter();
-  extern __shared__ float tile[];
   const int rows = launch_rows(rows_dev, cap);
-  const int row0 = blockIdx.x * kLnRows;
-  const int nrows = min(kLnRows, rows - row0);
-  if (nrows <= 0) return;
-  const int ld = d + 4;
-#pragma unroll 4
-  for (int idx = threadIdx.x; idx < nrows * d; idx += blockDim.x) {
-    const int rr = idx / d, c = idx % d;
-    const int row = row0 + rr;
-    const float* cand = cf + (size_t)row * ld_cf;
-    const float gate = 1.0f / (1.0f + exp_f32(-cand[fcol + c]));
-    float* st = state + (size_t)row_slot[row] * d + c;
-    const float next = gate * st[0] + (1.0f - gate) * cand[c];
-    st[0] = next;
-    tile[rr * ld + c] = fmaxf(next, 0.0f) + residual[(size_t)row * d + c];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kLnWarps + warp;
+  if (row >= rows) return;
+  const float* cand = cf + (size_t)row * ld_cf;
+  float* st = state + (size_t)row_slot[row] * d;
+  float4 x[VPL];
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int col = 4 * (lane + 32 * k);
+    const float4 cv = *reinterpret_cast<const float4*>(cand + col);
+    const float4 fv = *reinterpret_cast<const float4*>(cand + fcol + col);
+    const float4 sv = *reinterpret_cast<const float4*>(st + col);
+    const float4 rv = *reinterpret_cast<const float4*>(residual + (size_t)row * d + col);
+    const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ff[4] = {fv.x, fv.y, fv.z, fv.w};
+    const float ss[4] = {sv.x, sv.y, sv.z, sv.w}, rr[4] = {rv.x, rv.y, rv.z, rv.w};
+    float nx[4], o[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float gate = 1.0f / (1.0f + exp_f32(-ff[u]));
+      nx[u] = gate * ss[u] + (1.0f - gate) * cc[u];
+      o[u] = fmaxf(nx[u], 0.0f) + rr[u];
+    }
+    *reinterpret_cast<float4*>(st + col) = make_float4(nx[0], nx[1], nx[2], nx[3]);
+    x[k] = make_float4(o[0], o[1], o[2], o[3]);
   }
-  __syncthreads();
-  ln_stats_and_store(tile, nrows, d, row0, gamma, beta, out, q, status);
+  ln_row<VPL>(x, rows_s[warp], row, gamma, beta, out, q, status);
 }
 
 // ---- attention (attention_into, tensor.rs:251-318) ------------------------------
@@ -576,6 +607,14 @@ __global__ void init_slots_kernel(int n, const int32_t* slots, const int32_t* li
         ssru_state[((size_t)l * max_slots + s) * d + k] = 0.0f;
 }
 
+__global__ void flag_status_kernel(uint32_t* status) {
+  if (threadIdx.x == 0) flag_status(status, kStatusBadIndex);
+}
+
+inline void flag_status_host(uint32_t* status, cudaStream_t s) {
+  flag_status_kernel<<<1, 32, 0, s>>>(status);
+}
+
 inline unsigned blocks_for(long long n, int threads) {
   return static_cast<unsigned>((n + threads - 1) / threads);
 }
@@ -610,11 +649,18 @@ void launch_residual_ln(const float* a, int lda, const float* r, int ldr, const 
                         const float* beta, int rows, const int32_t* rows_dev, int d, float* out,
                         const QuantOut& q, uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return;
-  const size_t smem = sizeof(float) * kLnRows * (d + 4);
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(residual_ln_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch_pdl(residual_ln_kernel, dim3(blocks_for(rows, kLnRows)), dim3(kLnThreads), smem, s, a, lda, r, ldr, gamma, beta,
-             rows, rows_dev, d, out, q, status);
+  const dim3 grid(blocks_for(rows, kLnWarps)), block(kLnWarps * 32);
+  switch (d) {
+    case 128: launch_pdl(residual_ln_kernel<1>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 256: launch_pdl(residual_ln_kernel<2>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 384: launch_pdl(residual_ln_kernel<3>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 512: launch_pdl(residual_ln_kernel<4>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 640: launch_pdl(residual_ln_kernel<5>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 768: launch_pdl(residual_ln_kernel<6>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 896: launch_pdl(residual_ln_kernel<7>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 1024: launch_pdl(residual_ln_kernel<8>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
+    default: flag_status_host(status, s); break;
+  }
 }
 
 void launch_ssru(const float* cf, int ld, int fcol, float* state, const int32_t* row_slot,
@@ -622,11 +668,18 @@ void launch_ssru(const float* cf, int ld, int fcol, float* state, const int32_t*
                  const int32_t* rows_dev, int d, float* out, const QuantOut& q, uint32_t* status,
                  cudaStream_t s) {
   if (rows <= 0) return;
-  const size_t smem = sizeof(float) * kLnRows * (d + 4);
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(ssru_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch_pdl(ssru_kernel, dim3(blocks_for(rows, kLnRows)), dim3(kLnThreads), smem, s, cf, ld, fcol, state, row_slot, residual,
-             gamma, beta, rows, rows_dev, d, out, q, status);
+  const dim3 grid(blocks_for(rows, kLnWarps)), block(kLnWarps * 32);
+  switch (d) {
+    case 128: launch_pdl(ssru_kernel<1>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 256: launch_pdl(ssru_kernel<2>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 384: launch_pdl(ssru_kernel<3>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 512: launch_pdl(ssru_kernel<4>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 640: launch_pdl(ssru_kernel<5>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 768: launch_pdl(ssru_kernel<6>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 896: launch_pdl(ssru_kernel<7>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 1024: launch_pdl(ssru_kernel<8>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
+    default: flag_status_host(status, s); break;
+  }
 }
 
 template <int HD>

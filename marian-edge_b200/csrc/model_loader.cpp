@@ -207,8 +207,11 @@ std::string validate_schema(HostModel* m) {
     if (p != std::string::npos) m->heads = std::atoi(text.c_str() + p + 18);
   }
   const int d = m->dim, f = m->ffn;
-  if (m->heads <= 0 || d % m->heads != 0 || d % 16 != 0 || f % 16 != 0 || d > 1024 ||
-      (d / m->heads != 32 && d / m->heads != 48 && d / m->heads != 64) || m->heads > 16)
+  // the kernels take d a multiple of 128 up to 1024, head dims 32/48/64 and
+  // heads in groups of 4 (the shipped graph: d 384, 8 heads of 48)
+  if (m->heads <= 0 || d % m->heads != 0 || d % 128 != 0 || f % 16 != 0 || d > 1024 ||
+      (d / m->heads != 32 && d / m->heads != 48 && d / m->heads != 64) || m->heads > 16 ||
+      m->heads % 4 != 0)
     return "unsupported dimensions";
   if (m->vocab_src <= 2 || m->vocab_tgt <= 2)
     return "unsupported vocabulary size";

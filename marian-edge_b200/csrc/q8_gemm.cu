@@ -53,41 +53,36 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
   const int n_end = g.n;
   const int lane = threadIdx.x & 31;
   if (g.mode == kEpiArgmax) {
+    // bias is the candidate-masked bias: -inf for ids that are not
+    // candidates and past the last column (padded to whole 32-column
+    // chunks), so no per-column mask or bounds test is needed.
     if (!ok) return;
-    const bool mask_eos = g.eos_mask != nullptr && g.eos_mask[row] != 0;
-    uint32_t cand = g.cand_bits[nb >> 5];  // nb is a multiple of 32
-    if (nb == 0 && mask_eos) cand &= ~1u;
-    if (nb + 32 > n_end) cand &= (n_end - nb >= 32) ? 0xFFFFFFFFu : ((1u << (n_end - nb)) - 1u);
     const float uscale = g.row_scale ? __fmul_rn(row_scale, g.uniform_scale) : g.uniform_scale;
     const float4* b4 = reinterpret_cast<const float4*>(g.bias + nb);
-    const bool full = nb + 32 <= n_end;
+    float v[32];
 #pragma unroll
     for (int j4 = 0; j4 < 8; ++j4) {
-      float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (g.bias) {
-        if (full) {
-          b = b4[j4];
-        } else {
-          const int n = nb + 4 * j4;
-          b.x = n < n_end ? g.bias[n] : 0.f;
-          b.y = n + 1 < n_end ? g.bias[n + 1] : 0.f;
-          b.z = n + 2 < n_end ? g.bias[n + 2] : 0.f;
-          b.w = n + 3 < n_end ? g.bias[n + 3] : 0.f;
-        }
-      }
-      const float bb[4] = {b.x, b.y, b.z, b.w};
+      const float4 b = b4[j4];
+      v[4 * j4 + 0] = dequant(static_cast<int32_t>(r[4 * j4 + 0]), uscale, b.x);
+      v[4 * j4 + 1] = dequant(static_cast<int32_t>(r[4 * j4 + 1]), uscale, b.y);
+      v[4 * j4 + 2] = dequant(static_cast<int32_t>(r[4 * j4 + 2]), uscale, b.z);
+      v[4 * j4 + 3] = dequant(static_cast<int32_t>(r[4 * j4 + 3]), uscale, b.w);
+    }
+    if (nb == 0 && g.eos_mask != nullptr && g.eos_mask[row] != 0) v[0] = -INFINITY;
+    float t16[16];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = 4 * j4 + u;
-        float scale = uscale;
-        if (g.col_scale && nb + j < n_end)
-          scale = g.row_scale ? __fmul_rn(row_scale, g.col_scale[nb + j]) : g.col_scale[nb + j];
-        const float logit = dequant(static_cast<int32_t>(r[j]), scale, bb[u]);
-        if (((cand >> j) & 1u) && logit > best) {  // strict: the lowest index wins ties
-          best = logit;
-          best_n = nb + j;
-        }
-      }
+    for (int j = 0; j < 16; ++j) t16[j] = fmaxf(v[j], v[j + 16]);
+#pragma unroll
+    for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+      for (int j = 0; j < w; ++j) t16[j] = fmaxf(t16[j], t16[j + w]);
+    const float m = t16[0];
+    if (m > best) {  // strict: an earlier chunk keeps ties
+      int jj = 31;
+#pragma unroll
+      for (int j = 30; j >= 0; --j) jj = (v[j] == m) ? j : jj;  // lowest index of the maximum
+      best = m;
+      best_n = nb + jj;
     }
     return;
   }

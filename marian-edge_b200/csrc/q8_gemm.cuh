@@ -27,12 +27,12 @@ struct alignas(64) GemmGroup {
   const float* col_scale;      // [N]: 1/(alpha_a * w_mult) per output column, or null
                                // to use uniform_scale for every column
   const float* row_scale;      // [M] or null: extra per-row factor (microbench)
-  const float* bias;           // [N] or null
+  const float* bias;           // [N] or null; kEpiArgmax: [N rounded up to 32] with
+                               // -inf at non-candidate ids and past N
   const float* residual;       // [M, ldr] or null (kEpiF32)
   void* out;                   // float / int8 / int32 output base
   const int32_t* row_map;      // [M] destination row per source row, or null
   unsigned long long* argmax;  // [dest rows] packed (value, index) maxima (kEpiArgmax)
-  const uint32_t* cand_bits;   // [ceil(N/32)] candidate bitmask (kEpiArgmax)
   const uint8_t* eos_mask;     // [M] 1 = token 0 excluded for this row (kEpiArgmax)
   int32_t n;                   // output columns of this group
   int32_t ldo;                 // output row stride (elements)
