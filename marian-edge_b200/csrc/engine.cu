@@ -97,8 +97,11 @@ struct ProfRec {
 struct Lane {
   int id = 0;
   int cap = 0;                       // scheduling limit on active rows
-  cudaStream_t stream = nullptr;
+  cudaStream_t stream = nullptr;     // decode steps
   bool own_stream = false;
+  cudaStream_t enc_stream = nullptr; // encoder passes of admissions
+  cudaEvent_t enc_done = nullptr;    // the last admission's encoder pass is complete
+  cudaStream_t cur = nullptr;        // stream the launch helpers use
   uint32_t* d_status = nullptr;      // error bits of this lane's kernels
   uint32_t* h_status = nullptr;      // pinned
 
@@ -131,8 +134,10 @@ struct Lane {
   int32_t* h_step_tokens = nullptr;  // pinned
   uint8_t* h_done = nullptr;         // pinned
 
-  std::vector<int32_t> active;  // slots in row order
-  int launched = 0;             // rows of the step in flight (0: none)
+  std::vector<int32_t> active;   // slots in row order
+  std::vector<int32_t> pending;  // admitted slots whose encoder pass is in flight
+  bool enc_in_flight = false;
+  int launched = 0;              // rows of the step in flight (0: none)
   float* last_state = nullptr;  // final decoder state of the last step
   int eager_steps = 0;
   cudaGraphExec_t graph = nullptr;  // decode step for up to `cap` rows
@@ -231,13 +236,13 @@ int prof_begin(mc_engine* e, Lane& L, int kind, double flops, double bytes) {
     return x;
   };
   ProfRec r{kind, flops, bytes, ev(), ev()};
-  cudaEventRecord(r.a, L.stream);
+  cudaEventRecord(r.a, L.cur);
   L.prof_pending.push_back(r);
   return (int)L.prof_pending.size() - 1;
 }
 
 void prof_end(Lane& L, int idx) {
-  if (idx >= 0) cudaEventRecord(L.prof_pending[idx].b, L.stream);
+  if (idx >= 0) cudaEventRecord(L.prof_pending[idx].b, L.cur);
 }
 
 // Call after the lane's stream is synchronized.
@@ -418,7 +423,7 @@ mc_status gemm(mc_engine* e, Lane& L, int kind, int m, const int32_t* m_dev, dou
                                                          : 4.0 * m_prof * n;
     bytes += m_prof * k + n * k + 4.0 * n * (specs[i].w->bias ? 2 : 1) + out_bytes;
   }
-  PROFILED(kind, flops, bytes, CK(launch_q8_gemm(p, bn, L.stream)));
+  PROFILED(kind, flops, bytes, CK(launch_q8_gemm(p, bn, L.cur)));
   ++e->launches;
   return MC_OK;
 }
@@ -499,7 +504,7 @@ mc_status run_encoder(mc_engine* e, Lane& L, const AdmLayout& A, double sum_len_
            launch_embed_encoder(adm + A.tok, adm + A.pos, T, e->enc_emb, e->enc_emb_mult,
                                 e->emb_scale, e->positions, d, L.enc_x,
                                 quant_out_vec(L.enc_q, enc_input_alphas(e, 0)), L.d_status,
-                                L.stream));
+                                L.cur));
   ++e->launches;
   mc_status st;
   for (int l = 0; l < e->enc_layers; ++l) {
@@ -514,14 +519,14 @@ mc_status run_encoder(mc_engine* e, Lane& L, const AdmLayout& A, double sum_len_
       for (const auto& bk : L.buckets)
         CK(launch_attn_encoder(L.enc_qkv, adm + A.cu, adm + A.seq_ids + bk.offset, bk.count,
                                bk.max_len, d, e->heads, L.enc_o.p, a.wo.alpha, L.d_status,
-                               L.stream));
+                               L.cur));
     });
     e->launches += L.buckets.size();
     GroupSpec wo = {&L.enc_o, &a.wo, kEpiF32, L.enc_proj, d, 0, nullptr, false, 0.f};
     if ((st = gemm(e, L, MC_K_GEMM_OUT, T, nullptr, T, &wo, 1))) return st;
     PROFILED(MC_K_LAYERNORM, 0.0, rows_d * 13,
              launch_residual_ln(L.enc_proj, d, L.enc_x, d, a.ln_g, a.ln_b, T, nullptr, d, L.enc_x1,
-                                quant_out(L.enc_q, {f.w1.alpha}), L.d_status, L.stream));
+                                quant_out(L.enc_q, {f.w1.alpha}), L.d_status, L.cur));
     GroupSpec w1 = {&L.enc_q[0], &f.w1, kEpiQ8, L.enc_h.p, e->ffn, 0, nullptr, true, f.w2.alpha};
     if ((st = gemm(e, L, MC_K_GEMM_FFN1, T, nullptr, T, &w1, 1))) return st;
     GroupSpec w2 = {&L.enc_h, &f.w2, kEpiF32, L.enc_proj, d, 0, nullptr, false, 0.f};
@@ -529,7 +534,7 @@ mc_status run_encoder(mc_engine* e, Lane& L, const AdmLayout& A, double sum_len_
     PROFILED(MC_K_LAYERNORM, 0.0, rows_d * (12 + enc_input_alphas(e, l + 1).size()),
              launch_residual_ln(L.enc_proj, d, L.enc_x1, d, f.ln_g, f.ln_b, T, nullptr, d, L.enc_x,
                                 quant_out_vec(L.enc_q, enc_input_alphas(e, l + 1)), L.d_status,
-                                L.stream));
+                                L.cur));
     e->launches += 2;
   }
   // cross keys/values of every decoder layer into the paged pools
@@ -577,7 +582,7 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap) {
                                 e->dec_emb, e->dec_emb_mult, e->emb_scale, e->positions, d, x,
                                 quant_out_vec(L.dec_q, dec_input_alphas(e, 0)), L.eos_mask,
                                 e->kind == 1 ? e->self_pages_d : nullptr, e->pages_per_slot,
-                                e->page_tokens, L.self_row_map, L.d_status, L.stream));
+                                e->page_tokens, L.self_row_map, L.d_status, L.cur));
   ++e->launches;
   mc_status st;
   for (int l = 0; l < e->dec_layers; ++l) {
@@ -594,12 +599,12 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap) {
                CK(launch_attn_decode(L.dec_qkv, d, cap, nrows, row_slot, order_self, e->slot_step, 1,
                                      e->self_pages_d, e->pages_per_slot, e->page_tokens,
                                      e->self_k[l], e->self_v[l], d, e->heads, L.dec_o.p,
-                                     a.wo.alpha, L.d_status, L.stream)));
+                                     a.wo.alpha, L.d_status, L.cur)));
       GroupSpec wo = {&L.dec_o, &a.wo, kEpiF32, L.dec_proj, d, 0, nullptr, false, 0.f};
       if ((st = gemm(e, L, MC_K_GEMM_OUT, cap, nrows, R, &wo, 1))) return st;
       PROFILED(MC_K_LAYERNORM, 0.0, rows_d * 13,
                launch_residual_ln(L.dec_proj, d, x, d, a.ln_g, a.ln_b, cap, nrows, d, y,
-                                  quant_out(L.dec_q, {c.wq.alpha}), L.d_status, L.stream));
+                                  quant_out(L.dec_q, {c.wq.alpha}), L.d_status, L.cur));
       e->launches += 2;
     } else {
       const DevSsru& s = e->dec_ssru[l];
@@ -610,7 +615,7 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap) {
       PROFILED(MC_K_SSRU, 0.0, rows_d * 25,
                launch_ssru(L.dec_qkv, 2 * d, d, e->ssru_state + (size_t)l * e->rmax * d,
                            row_slot, x, s.ln_g, s.ln_b, cap, nrows, d, y,
-                           quant_out(L.dec_q, {c.wq.alpha}), L.d_status, L.stream));
+                           quant_out(L.dec_q, {c.wq.alpha}), L.d_status, L.cur));
       ++e->launches;
     }
     std::swap(x, y);
@@ -620,12 +625,12 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap) {
              CK(launch_attn_decode(L.dec_qkv, d, cap, nrows, row_slot, order_cross, e->slot_src, 0,
                                    e->cross_pages_d, e->pages_per_slot, e->page_tokens,
                                    e->cross_k[l], e->cross_v[l], d, e->heads, L.dec_o.p,
-                                   c.wo.alpha, L.d_status, L.stream)));
+                                   c.wo.alpha, L.d_status, L.cur)));
     GroupSpec wo = {&L.dec_o, &c.wo, kEpiF32, L.dec_proj, d, 0, nullptr, false, 0.f};
     if ((st = gemm(e, L, MC_K_GEMM_OUT, cap, nrows, R, &wo, 1))) return st;
     PROFILED(MC_K_LAYERNORM, 0.0, rows_d * 13,
              launch_residual_ln(L.dec_proj, d, x, d, c.ln_g, c.ln_b, cap, nrows, d, y,
-                                quant_out(L.dec_q, {f.w1.alpha}), L.d_status, L.stream));
+                                quant_out(L.dec_q, {f.w1.alpha}), L.d_status, L.cur));
     std::swap(x, y);
     GroupSpec w1 = {&L.dec_q[0], &f.w1, kEpiQ8, L.dec_h.p, e->ffn, 0, nullptr, true, f.w2.alpha};
     if ((st = gemm(e, L, MC_K_GEMM_FFN1, cap, nrows, R, &w1, 1))) return st;
@@ -634,7 +639,7 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap) {
     PROFILED(MC_K_LAYERNORM, 0.0, rows_d * (12 + dec_input_alphas(e, l + 1).size()),
              launch_residual_ln(L.dec_proj, d, x, d, f.ln_g, f.ln_b, cap, nrows, d, y,
                                 quant_out_vec(L.dec_q, dec_input_alphas(e, l + 1)), L.d_status,
-                                L.stream));
+                                L.cur));
     std::swap(x, y);
     e->launches += 3;
   }
@@ -643,7 +648,7 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap) {
   if ((st = gemm(e, L, MC_K_GEMM_VOCAB, cap, nrows, R, &voc, 1, L.best, L.eos_mask))) return st;
   PROFILED(MC_K_FINALIZE, 0.0, R * 29,
            launch_finalize(cap, nrows, row_slot, L.best, e->slot_prev, e->slot_step, e->slot_limit,
-                           L.step_tokens, L.done, L.d_status, L.stream));
+                           L.step_tokens, L.done, L.d_status, L.cur));
   ++e->launches;
   L.last_state = x;
   return MC_OK;
@@ -656,8 +661,10 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap) {
 // ============================================================================
 
 mc_engine::~mc_engine() {
-  for (Lane& L : lanes)
+  for (Lane& L : lanes) {
     if (L.stream) cudaStreamSynchronize(L.stream);
+    if (L.enc_stream) cudaStreamSynchronize(L.enc_stream);
+  }
   if (stream) cudaStreamSynchronize(stream);
   for (Lane& L : lanes) {
     for (auto& r : L.prof_pending) {
@@ -671,6 +678,8 @@ mc_engine::~mc_engine() {
     if (L.h_step_tokens) cudaFreeHost(L.h_step_tokens);
     if (L.h_done) cudaFreeHost(L.h_done);
     if (L.own_stream && L.stream) cudaStreamDestroy(L.stream);
+    if (L.enc_stream) cudaStreamDestroy(L.enc_stream);
+    if (L.enc_done) cudaEventDestroy(L.enc_done);
   }
   for (cudaEvent_t ev : event_pool) cudaEventDestroy(ev);
   for (void* p : allocations) cudaFree(p);
@@ -791,6 +800,9 @@ mc_status allocate_buffers(mc_engine* e) {
       CK(cudaStreamCreateWithFlags(&L.stream, cudaStreamNonBlocking));
       L.own_stream = true;
     }
+    CK(cudaStreamCreateWithFlags(&L.enc_stream, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&L.enc_done, cudaEventDisableTiming));
+    L.cur = L.stream;
     mc_status st = allocate_lane(e, L);
     if (st) return st;
   }
@@ -832,6 +844,9 @@ void finish_request(mc_engine* e, Request* r) {
 void abort_all(mc_engine* e) {
   for (Lane& L : e->lanes) {
     cudaStreamSynchronize(L.stream);
+    cudaStreamSynchronize(L.enc_stream);
+    L.enc_in_flight = false;
+    L.cur = L.stream;
     for (auto& r : L.prof_pending) {
       e->event_pool.push_back(r.a);
       e->event_pool.push_back(r.b);
@@ -842,14 +857,16 @@ void abort_all(mc_engine* e) {
   for (Request* r : e->queue) delete r;
   e->queue.clear();
   for (Lane& L : e->lanes) {
-    for (int s : L.active) {
-      Request* r = e->slot_req[s];
-      if (r) {
-        release_slot(e, r);
-        delete r;
+    for (auto* list : {&L.active, &L.pending}) {
+      for (int s : *list) {
+        Request* r = e->slot_req[s];
+        if (r) {
+          release_slot(e, r);
+          delete r;
+        }
       }
+      list->clear();
     }
-    L.active.clear();
   }
 }
 
@@ -872,14 +889,19 @@ mc_status check_status(mc_engine* e, Lane& L) {
 }
 
 // Admits queued requests into free slots of lane L and enqueues one packed
-// encoder pass on its stream (asynchronous: the staging block is pinned and
-// the lane's previous step has completed).  `cap` overrides the lane's row
-// limit (per-layer capture).
+// encoder pass for them on the lane's encoder stream, which runs alongside
+// the lane's decode steps; the admitted slots wait in L.pending until the
+// pass completes (join_pending).  Asynchronous: the staging block is pinned
+// and the lane's previous pass has completed.  `cap` overrides the lane's
+// row limit (per-layer capture).  With profiling on, the pass runs on the
+// decode stream so kernel times are not shared.
 mc_status admit(mc_engine* e, Lane& L, int cap) {
+  if (L.enc_in_flight) return MC_OK;
   int T = 0;
   const int pt = e->page_tokens;
   const int pps = e->pages_per_slot;
-  const size_t room = cap > (int)L.active.size() ? (size_t)(cap - (int)L.active.size()) : 0;
+  const int used = (int)(L.active.size() + L.pending.size());
+  const size_t room = cap > used ? (size_t)(cap - used) : 0;
   const size_t avail = std::min(room, e->free_slots.size());
   // Admission granularity: an encoder pass over a handful of sources costs
   // nearly as much launch latency as one over hundreds, so wait until an
@@ -961,9 +983,13 @@ mc_status admit(mc_engine* e, Lane& L, int cap) {
       lo = hi;
     }
   }
-  cudaStream_t s = L.stream;
+  cudaStream_t s = e->profiling ? L.stream : L.enc_stream;
+  for (Request* r : admitted) L.pending.push_back(r->slot);
+  L.enc_in_flight = true;
+  L.cur = s;
   CK(cudaMemcpyAsync(L.adm_d, L.adm_h, A.end * sizeof(int32_t), cudaMemcpyHostToDevice, s));
   mc_status st = run_encoder(e, L, A, sum_len_sq);
+  L.cur = L.stream;
   if (st) return st;
   const int32_t* ad = L.adm_d;
   launch_init_slots(B, ad + A.slots, ad + A.lims, ad + A.force, ad + A.src, e->slot_prev,
@@ -971,7 +997,26 @@ mc_status admit(mc_engine* e, Lane& L, int cap) {
                     e->dec_layers, e->rmax, e->d, ad + A.pages, e->cross_pages_d,
                     e->kind == 1 ? e->self_pages_d : nullptr, pps, s);
   ++e->launches;
-  for (Request* r : admitted) L.active.push_back(r->slot);
+  CK(cudaEventRecord(L.enc_done, s));
+  return MC_OK;
+}
+
+// Moves the slots of lane L's completed admission into its active rows and
+// orders the lane's decode stream after the encoder pass.  With wait =
+// false an encoder pass still running is left pending.
+mc_status join_pending(mc_engine* e, Lane& L, bool wait) {
+  if (!L.enc_in_flight) return MC_OK;
+  if (wait) {
+    CK(cudaEventSynchronize(L.enc_done));
+  } else {
+    const cudaError_t q = cudaEventQuery(L.enc_done);
+    if (q == cudaErrorNotReady) return MC_OK;
+    CK(q);
+  }
+  CK(cudaStreamWaitEvent(L.stream, L.enc_done, 0));
+  L.active.insert(L.active.end(), L.pending.begin(), L.pending.end());
+  L.pending.clear();
+  L.enc_in_flight = false;
   return MC_OK;
 }
 
@@ -1086,9 +1131,10 @@ mc_status complete_lane(mc_engine* e, Lane& L) {
   return MC_OK;
 }
 
+// Rows admitted to any lane: decoding, or waiting for their encoder pass.
 size_t total_active(const mc_engine* e) {
   size_t n = 0;
-  for (const Lane& L : e->lanes) n += L.active.size();
+  for (const Lane& L : e->lanes) n += L.active.size() + L.pending.size();
   return n;
 }
 
@@ -1104,7 +1150,9 @@ mc_status engine_step(mc_engine* e) {
   if (st) return st;
   for (Lane& L : e->lanes) {
     if ((st = complete_lane(e, L))) return st;
-    if ((st = admit(e, L, L.cap)) || (st = launch_decode(e, L, true))) {
+    // a finished encoder pass joins now; with nothing to decode, wait for it
+    if ((st = join_pending(e, L, L.active.empty())) || (st = admit(e, L, L.cap)) ||
+        (L.active.empty() && (st = join_pending(e, L, true))) || (st = launch_decode(e, L, true))) {
       abort_all(e);
       return st;
     }
@@ -1452,7 +1500,7 @@ extern "C" mc_status mc_trace_first_step(mc_engine* e, const int32_t* tokens, si
     r->force = 0;
     e->queue.push_back(r);
   }
-  if ((st = admit(e, L, e->rmax))) {
+  if ((st = admit(e, L, e->rmax)) || (st = join_pending(e, L, true))) {
     abort_all(e);
     return st;
   }
