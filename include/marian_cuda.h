@@ -57,7 +57,7 @@ typedef struct {
     int32_t device;              /* CUDA device ordinal */
     uint32_t max_inflight;       /* decode slots (default 1024) */
     uint32_t max_encode_tokens;  /* packed source tokens per encoder pass (default 65536) */
-    uint32_t page_tokens;        /* tokens per KV-cache page (default 16) */
+    uint32_t page_tokens;        /* tokens per KV-cache page: 8, 16 (default) or 32 */
     uint32_t kv_pages;           /* pages per cache pool; 0 = enough for every slot at full length */
     uint32_t max_length_factor;  /* Architecture::max_length_factor, 1..8 (default 3) */
     uint32_t lanes;              /* concurrent decode lanes, 1..8 (default 1; 0 = default):

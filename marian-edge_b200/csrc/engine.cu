@@ -185,6 +185,8 @@ struct mc_engine {
   int cross_pool_pages = 0, self_pool_pages = 0;
   int32_t *cross_pages_d = nullptr, *self_pages_d = nullptr;
   std::vector<float*> cross_k, cross_v, self_k, self_v;
+  // tensor maps of the pools for the decode attention (encode_tmap_kv)
+  std::vector<CUtensorMap> cross_k_map, cross_v_map, self_k_map, self_v_map;
   std::vector<int32_t> free_cross, free_self, free_slots;
 
   std::vector<Lane> lanes;
@@ -598,7 +600,7 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap) {
       PROFILED(MC_K_ATTN_SELF, 4.0 * self_keys * d, 8.0 * self_keys * d + rows_d * 5,
                CK(launch_attn_decode(L.dec_qkv, d, cap, nrows, row_slot, order_self, e->slot_step, 1,
                                      e->self_pages_d, e->pages_per_slot, e->page_tokens,
-                                     e->self_k[l], e->self_v[l], d, e->heads, L.dec_o.p,
+                                     &e->self_k_map[l], &e->self_v_map[l], d, e->heads, L.dec_o.p,
                                      a.wo.alpha, L.d_status, L.cur)));
       GroupSpec wo = {&L.dec_o, &a.wo, kEpiF32, L.dec_proj, d, 0, nullptr, false, 0.f};
       if ((st = gemm(e, L, MC_K_GEMM_OUT, cap, nrows, R, &wo, 1))) return st;
@@ -624,7 +626,7 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap) {
     PROFILED(MC_K_ATTN_CROSS, 4.0 * cross_keys * d, 8.0 * cross_keys * d + rows_d * 5,
              CK(launch_attn_decode(L.dec_qkv, d, cap, nrows, row_slot, order_cross, e->slot_src, 0,
                                    e->cross_pages_d, e->pages_per_slot, e->page_tokens,
-                                   e->cross_k[l], e->cross_v[l], d, e->heads, L.dec_o.p,
+                                   &e->cross_k_map[l], &e->cross_v_map[l], d, e->heads, L.dec_o.p,
                                    c.wo.alpha, L.d_status, L.cur)));
     GroupSpec wo = {&L.dec_o, &c.wo, kEpiF32, L.dec_proj, d, 0, nullptr, false, 0.f};
     if ((st = gemm(e, L, MC_K_GEMM_OUT, cap, nrows, R, &wo, 1))) return st;
@@ -778,6 +780,16 @@ mc_status allocate_buffers(mc_engine* e) {
       CK(dalloc(e, &e->self_v[l], pool_rows * d));
     }
   }
+  const int group_cols = 4 * (d / e->heads);
+  auto kv_maps = [&](const std::vector<float*>& pools, std::vector<CUtensorMap>* maps) {
+    maps->resize(pools.size());
+    for (size_t l = 0; l < pools.size(); ++l)
+      if (!encode_tmap_kv(&(*maps)[l], pools[l], pool_rows, d, e->page_tokens, group_cols)) return false;
+    return true;
+  };
+  if (!kv_maps(e->cross_k, &e->cross_k_map) || !kv_maps(e->cross_v, &e->cross_v_map) ||
+      !kv_maps(e->self_k, &e->self_k_map) || !kv_maps(e->self_v, &e->self_v_map))
+    return fail(e, MC_MODEL, "KV-cache tensor map rejected");
   CK(dalloc(e, &e->cross_pages_d, (size_t)R * e->pages_per_slot));
   CK(dalloc(e, &e->self_pages_d, (size_t)R * e->pages_per_slot));
   e->free_cross.clear();
@@ -1207,7 +1219,8 @@ extern "C" mc_status mc_create(const mc_config* cfg, mc_engine** out) {
   if (!cfg || !out) return MC_INVALID_INPUT;
   *out = nullptr;
   if (cfg->max_inflight == 0 || cfg->max_inflight > 65536 || cfg->max_encode_tokens < 256 ||
-      cfg->page_tokens == 0 || cfg->page_tokens > 256 || cfg->max_length_factor < 1 ||
+      (cfg->page_tokens != 8 && cfg->page_tokens != 16 && cfg->page_tokens != 32) ||
+      cfg->max_length_factor < 1 ||
       cfg->max_length_factor > 8 || cfg->lanes > (uint32_t)kMaxLanes)
     return MC_INVALID_INPUT;
   mc_engine* e = new mc_engine();

@@ -8,6 +8,8 @@
 // double-rounding corner cases; the reference's libm expf is correctly
 // rounded to within a few thousandths of an ulp, so the two agree except on
 // rare inputs.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -398,91 +400,156 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
   }
 }
 
-// Decode: one CTA of 4 warps per (active row, group of 4 heads); warp h of
-// the CTA is head 4 * blockIdx.y + h.  Rows are taken in row_order (longest
-// first, so long rows start in the first wave).  The group's slices of the
-// cached keys, then values, are staged in shared memory 64 keys at a time
-// with 16-byte cp.async copies: each key's slice of the group is
-// 4 * HD * 4 contiguous bytes of a page row, so every copy instruction of a
-// warp reads whole 128-byte lines.  Rows in shared memory are padded by 16
-// bytes so the lanes' 128-bit reads of different keys fall on distinct
+// Decode: a persistent kernel over work items (active row, group of 4
+// heads), taken in row_order (longest rows first) round-robin by the CTAs.
+// Lane 0 of warp 4 is the producer: for every item it streams the group's
+// slices of the cached keys, then of the values, into a 3-slot shared-memory
+// ring, one chunk of 32 keys per slot, with one 3-D TMA copy per cache page
+// (a page's 16 rows x 4 * HD floats, through the pool's tensor map; see
+// encode_tmap_kv) completing on the slot's mbarrier.  The copies of the next
+// chunks and items are in flight while warps 0..3 (one per head of the
+// group) consume the current slot.  The 128-byte swizzle of the copies
+// puts the 16-byte chunk c of key row r at chunk c ^ (r % 8) of its line,
+// so the lanes' reads of different keys in the score loop fall on distinct
 // banks.  Per head the operation order is the reference's: lane t scores
-// key t with an in-order dot product, max, exp, a left-to-right sum by
-// lane 0, scaling, and a left-to-right weighted sum of V per output dim
-// (lane i owns dims 2i and 2i + 1).
-constexpr int kDecGroup = 4;   // heads per CTA
-constexpr int kDecChunk = 64;  // keys staged per round
+// key t with an in-order dot product, max, exp, a left-to-right sum by lane
+// 0, scaling, and a left-to-right weighted sum of V per output dim (lane i
+// owns dims 2i and 2i + 1).  Every mbarrier wait is bounded; on a timeout
+// the kernel records kStatusWaitTimeout and stops, after waiting (bounded)
+// for the copies it issued.
+constexpr int kDecGroup = 4;    // heads per item
+constexpr int kDecChunk = 32;   // keys per ring slot
+constexpr int kDecSlots = 3;    // ring depth
+constexpr int kDecThreads = (kDecGroup + 1) * 32;
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
-               "l"(gmem_src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
-
-// Copies the group's slice of cache rows rows_s[c0 .. c0 + n) into
-// stage[t][0 .. W) (row stride W + 4 floats).
-template <int W>
-__device__ __forceinline__ void stage_rows(float* stage, const float* __restrict__ pool,
-                                           const int* rows_s, int c0, int n, int d, int col0) {
-  constexpr int kVec = W / 4;
-  for (int idx = threadIdx.x; idx < n * kVec; idx += kDecGroup * 32) {
-    const int t = idx / kVec, c = (idx - t * kVec) * 4;
-    cp_async16(stage + t * (W + 4) + c, pool + (size_t)rows_s[c0 + t] * d + col0 + c);
-  }
+__device__ __forceinline__ void bulk_copy_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                              uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kDecGroup * 32) attn_decode_kernel(
+__device__ __forceinline__ void mbar_arrive_cta(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Item -> (row, head group, key count); false for a row whose length fails
+// its bounds check (both roles skip it alike).
+__device__ __forceinline__ bool decode_item(int item, int groups,
+                                            const int32_t* __restrict__ row_order,
+                                            const int32_t* __restrict__ row_slot,
+                                            const int32_t* __restrict__ slot_len, int len_add,
+                                            int limit, int* r, int* g, int* slot, int* len) {
+  const int ro = item / groups;
+  *g = item - ro * groups;
+  *r = row_order ? row_order[ro] : ro;
+  *slot = row_slot[*r];
+  *len = slot_len[*slot] + len_add;
+  return *len > 0 && *len <= limit;
+}
+
+// Shared-memory float offset of float f (0 <= f < W) of key row r of a
+// page box [W / 32 column blocks][PT rows][32 floats], 128-byte swizzled.
+template <int PT>
+__device__ __forceinline__ int swz(int r, int f) {
+  const int cb = f >> 5, c = (f & 31) >> 2;
+  return cb * (PT * 32) + r * 32 + ((c ^ (r & 7)) << 2) + (f & 3);
+}
+
+template <int HD, int PT>
+__global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
     const float* __restrict__ q, int ldq, const int32_t* __restrict__ rows_dev, int cap,
     const int32_t* __restrict__ row_slot,
     const int32_t* __restrict__ row_order, const int32_t* __restrict__ slot_len, int len_add,
-    const int32_t* __restrict__ page_table, int pages_per_slot, int page_tokens,
-    const float* __restrict__ k_pool, const float* __restrict__ v_pool, int d, int heads,
-    int8_t* __restrict__ out_q, float alpha, uint32_t* status) {
+    const int32_t* __restrict__ page_table, int pages_per_slot,
+    const __grid_constant__ CUtensorMap k_map, const __grid_constant__ CUtensorMap v_map, int d,
+    int heads, int8_t* __restrict__ out_q, float alpha, uint32_t* status) {
   constexpr int W = kDecGroup * HD;
-  constexpr int SLD = W + 4;
+  constexpr int kPages = kDecChunk / PT;                  // pages per slot
+  constexpr int kPageFloats = ((PT * W * 4 + 1023) / 1024) * 256;  // 1 KB aligned
+  constexpr int kSlotFloats = kPages * kPageFloats + 256;           // pages, then q (1 KB)
+  extern __shared__ uint8_t dsm_raw[];
+  float* dsm = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[kDecSlots], empty_bar[kDecSlots];
+  float* ps = dsm + kDecSlots * kSlotFloats;        // [4][kMaxSeq] scores
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kDecSlots; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kDecGroup);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&k_map);
+    tma_prefetch_desc(&v_map);
+  }
+  __syncthreads();
   pdl_enter();
-  extern __shared__ __align__(16) float dsm[];
-  if ((int)blockIdx.x >= launch_rows(rows_dev, cap)) return;
-  const int r = row_order ? row_order[blockIdx.x] : blockIdx.x;
-  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int col0 = blockIdx.y * W;  // first column of this head group
-  const int slot = row_slot[r];
-  const int len = slot_len[slot] + len_add;
-  if (len <= 0 || len > kMaxSeq || len > pages_per_slot * page_tokens) {
-    if (threadIdx.x == 0) flag_status(status, kStatusBadIndex);
+  const int groups = heads / kDecGroup;
+  const int items = launch_rows(rows_dev, cap) * groups;
+  const int limit = min(kMaxSeq, pages_per_slot * PT);
+  if (warp == kDecGroup) {
+    // ---- producer ---------------------------------------------------------
+    if (lane == 0) {
+      int k = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        int r, g, slot, len;
+        if (!decode_item(item, groups, row_order, row_slot, slot_len, len_add, limit, &r, &g, &slot,
+                         &len)) {
+          flag_status(status, kStatusBadIndex);
+          continue;
+        }
+        const int32_t* pages = page_table + (size_t)slot * pages_per_slot;
+        for (int pass = 0; pass < 2 && ok; ++pass) {
+          const CUtensorMap* map = pass == 0 ? &k_map : &v_map;
+          for (int c0 = 0; c0 < len; c0 += kDecChunk, ++k) {
+            const int np = (min(kDecChunk, len - c0) + PT - 1) / PT;
+            const int sl = k % kDecSlots;
+            if (!(ok = mbar_wait(&empty_bar[sl], ((k / kDecSlots) & 1) ^ 1, status))) break;
+            float* dst = dsm + sl * kSlotFloats;
+            const uint32_t page_bytes = PT * W * 4, q_bytes = W * 4;
+            mbar_arrive_expect_tx(&full_bar[sl], np * page_bytes + (pass == 0 ? q_bytes : 0));
+            if (pass == 0)
+              bulk_copy_g2s(dst + kPages * kPageFloats, q + (size_t)r * ldq + g * W, q_bytes, &full_bar[sl]);
+            for (int p = 0; p < np; ++p)
+              tma_load_3d(dst + p * kPageFloats, map, 0, pages[c0 / PT + p] * PT, g * (W / 32),
+                          &full_bar[sl]);
+          }
+        }
+      }
+      // every issued copy lands before the CTA can exit: wait (bounded) for
+      // the last fill of each slot
+      for (int kk = max(0, k - kDecSlots); kk < k; ++kk)
+        mbar_wait(&full_bar[kk % kDecSlots], (kk / kDecSlots) & 1, status);
+    }
     return;
   }
-  float* stage = dsm;                                  // [kDecChunk][W + 4]
-  float* qs = stage + kDecChunk * SLD;                 // [4][HD]
-  float* ps = qs + W;                                  // [4][kMaxSeq]
-  int* rows_s = reinterpret_cast<int*>(ps + kDecGroup * kMaxSeq);  // [kMaxSeq]
-  const int32_t* pages = page_table + (size_t)slot * pages_per_slot;
-  for (int j = threadIdx.x; j < len; j += blockDim.x)
-    rows_s[j] = pages[j / page_tokens] * page_tokens + j % page_tokens;
-  for (int i = threadIdx.x; i < W; i += blockDim.x) qs[i] = q[(size_t)r * ldq + col0 + i];
-  __syncthreads();
-  const float* qh = qs + h * HD;
+  // ---- consumers: warp h = head h of the item's group -------------------------
+  const int h = warp;
   float* ph = ps + h * kMaxSeq;
   const float scale = 1.0f / sqrtf((float)HD);
-  float mx = -INFINITY;
-  for (int c0 = 0; c0 < len; c0 += kDecChunk) {
-    const int n = min(kDecChunk, len - c0);
-    stage_rows<W>(stage, k_pool, rows_s, c0, n, d, col0);
-    cp_async_wait_all();
-    __syncthreads();
-#pragma unroll
-    for (int u = 0; u < kDecChunk / 32; ++u) {
-      const int t = lane + 32 * u;
-      if (t < n) {
-        const float* kr = stage + t * SLD + h * HD;
+  const bool active = 2 * lane < HD;
+  const int kp = lane / PT, kr = lane & (PT - 1);  // this lane's key: page, row
+  int k = 0;
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    int r, g, slot, len;
+    if (!decode_item(item, groups, row_order, row_slot, slot_len, len_add, limit, &r, &g, &slot, &len))
+      continue;
+    float mx = -INFINITY;
+    for (int c0 = 0; c0 < len; c0 += kDecChunk, ++k) {
+      const int n = min(kDecChunk, len - c0);
+      const int sl = k % kDecSlots;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[sl], (k / kDecSlots) & 1, status))) return;
+      const float* base = dsm + sl * kSlotFloats;
+      if (lane < n) {
+        const float* pg = base + kp * kPageFloats;
+        const float* qh = base + kPages * kPageFloats + h * HD;
         float dot = 0.0f;
 #pragma unroll
         for (int i = 0; i < HD; i += 4) {
-          const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
+          const float4 k4 = *reinterpret_cast<const float4*>(pg + swz<PT>(kr, h * HD + i));
           const float4 q4 = *reinterpret_cast<const float4*>(qh + i);
           dot = dot + q4.x * k4.x;
           dot = dot + q4.y * k4.y;
@@ -490,50 +557,49 @@ __global__ void __launch_bounds__(kDecGroup * 32) attn_decode_kernel(
           dot = dot + q4.w * k4.w;
         }
         const float sc = dot * scale;
-        ph[c0 + t] = sc;
+        ph[c0 + lane] = sc;
         mx = fmaxf(mx, sc);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cta(&empty_bar[sl]);
     }
-    __syncthreads();  // the stage is refilled next
-  }
-  // the first value rows load while the softmax runs
-  stage_rows<W>(stage, v_pool, rows_s, 0, min(kDecChunk, len), d, col0);
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  for (int j = lane; j < len; j += 32) ph[j] = exp_f32(ph[j] - mx);
-  __syncwarp();
-  float inv = 0.0f;
-  if (lane == 0) {
-    float sum = 0.0f;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int j = lane; j < len; j += 32) ph[j] = exp_f32(ph[j] - mx);
+    __syncwarp();
+    float inv = 0.0f;
+    if (lane == 0) {
+      float sum = 0.0f;
 #pragma unroll 8
-    for (int j = 0; j < len; ++j) sum = sum + ph[j];
-    inv = 1.0f / sum;
-  }
-  inv = __shfl_sync(0xffffffffu, inv, 0);
-  for (int j = lane; j < len; j += 32) ph[j] = ph[j] * inv;
-  __syncwarp();
-  const bool active = 2 * lane < HD;
-  float acc0 = 0.0f, acc1 = 0.0f;
-  for (int c0 = 0; c0 < len; c0 += kDecChunk) {
-    const int n = min(kDecChunk, len - c0);
-    if (c0 > 0) stage_rows<W>(stage, v_pool, rows_s, c0, n, d, col0);
-    cp_async_wait_all();
-    __syncthreads();
-    if (active) {
-      const float* vb = stage + h * HD + 2 * lane;
-#pragma unroll 8
-      for (int t = 0; t < n; ++t) {
-        const float2 v2 = *reinterpret_cast<const float2*>(vb + t * SLD);
-        const float p = ph[c0 + t];
-        acc0 = acc0 + v2.x * p;
-        acc1 = acc1 + v2.y * p;
+      for (int j = 0; j < len; ++j) sum = sum + ph[j];
+      inv = 1.0f / sum;
+    }
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    for (int j = lane; j < len; j += 32) ph[j] = ph[j] * inv;
+    __syncwarp();
+    float acc0 = 0.0f, acc1 = 0.0f;
+    for (int c0 = 0; c0 < len; c0 += kDecChunk, ++k) {
+      const int n = min(kDecChunk, len - c0);
+      const int sl = k % kDecSlots;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[sl], (k / kDecSlots) & 1, status))) return;
+      if (active) {
+        const float* base = dsm + sl * kSlotFloats;
+        const int f = h * HD + 2 * lane;
+#pragma unroll 4
+        for (int t = 0; t < n; ++t) {
+          const float2 v2 = *reinterpret_cast<const float2*>(base + (t / PT) * kPageFloats + swz<PT>(t & (PT - 1), f));
+          const float p = ph[c0 + t];
+          acc0 = acc0 + v2.x * p;
+          acc1 = acc1 + v2.y * p;
+        }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cta(&empty_bar[sl]);
     }
-    __syncthreads();
-  }
-  if (active) {
-    const uint16_t w2 = (uint16_t)(uint8_t)quantize_one(acc0, alpha, status) |
-                        ((uint16_t)(uint8_t)quantize_one(acc1, alpha, status) << 8);
-    *reinterpret_cast<uint16_t*>(out_q + (size_t)r * d + col0 + h * HD + 2 * lane) = w2;
+    if (active) {
+      const uint16_t w2 = (uint16_t)(uint8_t)quantize_one(acc0, alpha, status) |
+                          ((uint16_t)(uint8_t)quantize_one(acc1, alpha, status) << 8);
+      *reinterpret_cast<uint16_t*>(out_q + (size_t)r * d + g * W + h * HD + 2 * lane) = w2;
+    }
   }
 }
 
@@ -714,43 +780,67 @@ cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens,
   }
 }
 
-template <int HD>
+template <int HD, int PT>
 cudaError_t launch_attn_decode_hd(const float* q, int ldq, int rows, const int32_t* rows_dev,
                                   const int32_t* row_slot, const int32_t* row_order,
                                   const int32_t* slot_len, int len_add, const int32_t* page_table,
-                                  int pages_per_slot, int page_tokens, const float* k_pool,
-                                  const float* v_pool, int d, int heads, int8_t* out_q,
+                                  int pages_per_slot, const CUtensorMap* k_map,
+                                  const CUtensorMap* v_map, int d, int heads, int8_t* out_q,
                                   float alpha, uint32_t* status, cudaStream_t s) {
   constexpr int W = kDecGroup * HD;
-  const size_t smem = sizeof(float) * ((size_t)kDecChunk * (W + 4) + W + (size_t)kDecGroup * kMaxSeq) +
-                      sizeof(int) * kMaxSeq;
+  constexpr int kPageFloats = ((PT * W * 4 + 1023) / 1024) * 256;
+  const size_t smem = 1024 + sizeof(float) * ((size_t)kDecSlots * ((kDecChunk / PT) * kPageFloats + 256) +
+                                              (size_t)kDecGroup * kMaxSeq);
   static unsigned long long configured = 0;  // one bit per device ordinal
+  static int sms[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD>,
+  dev &= 63;
+  if (!(configured & (1ull << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD, PT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    configured |= 1ull << (dev & 63);
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    sms[dev] = n > 0 ? n : 148;
+    configured |= 1ull << dev;
   }
-  launch_pdl(attn_decode_kernel<HD>, dim3(rows, heads / kDecGroup), dim3(kDecGroup * 32), smem, s, q,
-             ldq, rows_dev, rows, row_slot, row_order, slot_len, len_add, page_table,
-             pages_per_slot, page_tokens, k_pool, v_pool, d, heads, out_q, alpha, status);
+  // two CTAs per SM (the ring takes ~100 KB of shared memory per CTA)
+  const long long items = (long long)rows * (heads / kDecGroup);
+  const int grid = (int)std::min<long long>(items, 2LL * sms[dev]);
+  launch_pdl(attn_decode_kernel<HD, PT>, dim3(grid), dim3(kDecThreads), smem, s, q, ldq, rows_dev, rows,
+             row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, *k_map, *v_map, d,
+             heads, out_q, alpha, status);
   return cudaGetLastError();
+}
+
+template <int HD>
+cudaError_t launch_attn_decode_pt(const float* q, int ldq, int rows, const int32_t* rows_dev,
+                                  const int32_t* row_slot, const int32_t* row_order,
+                                  const int32_t* slot_len, int len_add, const int32_t* page_table,
+                                  int pages_per_slot, int page_tokens, const CUtensorMap* k_map,
+                                  const CUtensorMap* v_map, int d, int heads, int8_t* out_q,
+                                  float alpha, uint32_t* status, cudaStream_t s) {
+  switch (page_tokens) {
+    case 8: return launch_attn_decode_hd<HD, 8>(q, ldq, rows, rows_dev, row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, k_map, v_map, d, heads, out_q, alpha, status, s);
+    case 16: return launch_attn_decode_hd<HD, 16>(q, ldq, rows, rows_dev, row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, k_map, v_map, d, heads, out_q, alpha, status, s);
+    case 32: return launch_attn_decode_hd<HD, 32>(q, ldq, rows, rows_dev, row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, k_map, v_map, d, heads, out_q, alpha, status, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t* rows_dev,
                                const int32_t* row_slot, const int32_t* row_order,
                                const int32_t* slot_len, int len_add, const int32_t* page_table,
-                               int pages_per_slot, int page_tokens, const float* k_pool,
-                               const float* v_pool, int d, int heads, int8_t* out_q, float alpha,
-                               uint32_t* status, cudaStream_t s) {
+                               int pages_per_slot, int page_tokens, const CUtensorMap* k_map,
+                               const CUtensorMap* v_map, int d, int heads, int8_t* out_q,
+                               float alpha, uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
   if (heads % kDecGroup != 0 || d != heads * (d / heads)) return cudaErrorInvalidValue;
   switch (d / heads) {
-    case 32: return launch_attn_decode_hd<32>(q, ldq, rows, rows_dev, row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, page_tokens, k_pool, v_pool, d, heads, out_q, alpha, status, s);
-    case 48: return launch_attn_decode_hd<48>(q, ldq, rows, rows_dev, row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, page_tokens, k_pool, v_pool, d, heads, out_q, alpha, status, s);
-    case 64: return launch_attn_decode_hd<64>(q, ldq, rows, rows_dev, row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, page_tokens, k_pool, v_pool, d, heads, out_q, alpha, status, s);
+    case 32: return launch_attn_decode_pt<32>(q, ldq, rows, rows_dev, row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, page_tokens, k_map, v_map, d, heads, out_q, alpha, status, s);
+    case 48: return launch_attn_decode_pt<48>(q, ldq, rows, rows_dev, row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, page_tokens, k_map, v_map, d, heads, out_q, alpha, status, s);
+    case 64: return launch_attn_decode_pt<64>(q, ldq, rows, rows_dev, row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, page_tokens, k_map, v_map, d, heads, out_q, alpha, status, s);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -7,6 +7,7 @@
 // by one thread each.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -71,14 +72,16 @@ cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens,
 
 // tensor.rs:251-318 with one query per row over a paged cache: keys of row r
 // are cache rows page_table[slot][j / page_tokens] * page_tokens +
-// j % page_tokens for j < slot_len[slot] + len_add.
-// row_order (nullable) lists the rows in the order CTAs take them.
+// j % page_tokens for j < slot_len[slot] + len_add, read through the
+// pools' tensor maps (encode_tmap_kv with group_cols = 4 * d / heads).
+// row_order (nullable) lists the rows in the order the kernel takes them.
+// page_tokens is 8, 16 or 32.
 cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t* rows_dev,
-                               const int32_t* row_slot,
-                               const int32_t* row_order, const int32_t* slot_len, int len_add,
-                               const int32_t* page_table, int pages_per_slot, int page_tokens,
-                               const float* k_pool, const float* v_pool, int d, int heads,
-                               int8_t* out_q, float alpha, uint32_t* status, cudaStream_t s);
+                               const int32_t* row_slot, const int32_t* row_order,
+                               const int32_t* slot_len, int len_add, const int32_t* page_table,
+                               int pages_per_slot, int page_tokens, const CUtensorMap* k_map,
+                               const CUtensorMap* v_map, int d, int heads, int8_t* out_q,
+                               float alpha, uint32_t* status, cudaStream_t s);
 
 // Turns the packed per-row maxima into tokens (q8_engine.rs:437-449):
 // advances each slot's step/previous token, reports the token and whether
