@@ -404,14 +404,14 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
 // heads), taken in row_order (longest rows first) round-robin by the CTAs.
 // Lane 0 of warp 4 is the producer: for every item it streams the group's
 // slices of the cached keys, then of the values, into a 3-slot shared-memory
-// ring, one chunk of 32 keys per slot, with one 3-D TMA copy per cache page
-// (a page's 16 rows x 4 * HD floats, through the pool's tensor map; see
-// encode_tmap_kv) completing on the slot's mbarrier.  The copies of the next
-// chunks and items are in flight while warps 0..3 (one per head of the
-// group) consume the current slot.  The 128-byte swizzle of the copies
-// puts the 16-byte chunk c of key row r at chunk c ^ (r % 8) of its line,
-// so the lanes' reads of different keys in the score loop fall on distinct
-// banks.  Per head the operation order is the reference's: lane t scores
+// ring, one chunk of 32 keys per slot, with one 3-D TMA copy per 8 cache
+// rows (8 rows x 4 * HD floats of one page, through the pool's tensor map;
+// see encode_tmap_kv) completing on the slot's mbarrier, so at most 7 rows
+// past an item's last key are read.  The copies of the next chunks and
+// items are in flight while warps 0..3 (one per head of the group) consume
+// the current slot.  The 128-byte swizzle of the copies puts the 16-byte
+// chunk c of key row r at chunk c ^ (r % 8) of its line, so the lanes'
+// reads of different keys in the score loop fall on distinct banks.  Per head the operation order is the reference's: lane t scores
 // key t with an in-order dot product, max, exp, a left-to-right sum by lane
 // 0, scaling, and a left-to-right weighted sum of V per output dim (lane i
 // owns dims 2i and 2i + 1).  Every mbarrier wait is bounded; on a timeout
@@ -450,12 +450,12 @@ __device__ __forceinline__ bool decode_item(int item, int groups,
   return *len > 0 && *len <= limit;
 }
 
-// Shared-memory float offset of float f (0 <= f < W) of key row r of a
-// page box [W / 32 column blocks][PT rows][32 floats], 128-byte swizzled.
-template <int PT>
-__device__ __forceinline__ int swz(int r, int f) {
-  const int cb = f >> 5, c = (f & 31) >> 2;
-  return cb * (PT * 32) + r * 32 + ((c ^ (r & 7)) << 2) + (f & 3);
+// Shared-memory float offset of float f (0 <= f < W) of key t of a chunk
+// staged as 8-row boxes [W / 32 column blocks][8 rows][32 floats], 128-byte
+// swizzled, box_floats apart.
+__device__ __forceinline__ int swz(int t, int f, int box_floats) {
+  const int r = t & 7, cb = f >> 5, c = (f & 31) >> 2;
+  return (t >> 3) * box_floats + cb * 256 + r * 32 + ((c ^ r) << 2) + (f & 3);
 }
 
 template <int HD, int PT>
@@ -467,9 +467,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
     const __grid_constant__ CUtensorMap k_map, const __grid_constant__ CUtensorMap v_map, int d,
     int heads, int8_t* __restrict__ out_q, float alpha, uint32_t* status) {
   constexpr int W = kDecGroup * HD;
-  constexpr int kPages = kDecChunk / PT;                  // pages per slot
-  constexpr int kPageFloats = ((PT * W * 4 + 1023) / 1024) * 256;  // 1 KB aligned
-  constexpr int kSlotFloats = kPages * kPageFloats + 256;           // pages, then q (1 KB)
+  constexpr int kBoxFloats = 8 * W;                         // 8 rows (a multiple of 1 KB)
+  constexpr int kSlotFloats = (kDecChunk / 8) * kBoxFloats + 256;  // boxes, then q (1 KB)
   extern __shared__ uint8_t dsm_raw[];
   float* dsm = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[kDecSlots], empty_bar[kDecSlots];
@@ -505,17 +504,20 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
         for (int pass = 0; pass < 2 && ok; ++pass) {
           const CUtensorMap* map = pass == 0 ? &k_map : &v_map;
           for (int c0 = 0; c0 < len; c0 += kDecChunk, ++k) {
-            const int np = (min(kDecChunk, len - c0) + PT - 1) / PT;
+            const int nb = (min(kDecChunk, len - c0) + 7) / 8;  // 8-row boxes
             const int sl = k % kDecSlots;
             if (!(ok = mbar_wait(&empty_bar[sl], ((k / kDecSlots) & 1) ^ 1, status))) break;
             float* dst = dsm + sl * kSlotFloats;
-            const uint32_t page_bytes = PT * W * 4, q_bytes = W * 4;
-            mbar_arrive_expect_tx(&full_bar[sl], np * page_bytes + (pass == 0 ? q_bytes : 0));
+            const uint32_t box_bytes = kBoxFloats * 4, q_bytes = W * 4;
+            mbar_arrive_expect_tx(&full_bar[sl], nb * box_bytes + (pass == 0 ? q_bytes : 0));
             if (pass == 0)
-              bulk_copy_g2s(dst + kPages * kPageFloats, q + (size_t)r * ldq + g * W, q_bytes, &full_bar[sl]);
-            for (int p = 0; p < np; ++p)
-              tma_load_3d(dst + p * kPageFloats, map, 0, pages[c0 / PT + p] * PT, g * (W / 32),
+              bulk_copy_g2s(dst + (kDecChunk / 8) * kBoxFloats, q + (size_t)r * ldq + g * W, q_bytes,
+                            &full_bar[sl]);
+            for (int b = 0; b < nb; ++b) {
+              const int j = c0 + 8 * b;  // first key of the box (boxes never straddle pages)
+              tma_load_3d(dst + b * kBoxFloats, map, 0, pages[j / PT] * PT + j % PT, g * (W / 32),
                           &full_bar[sl]);
+            }
           }
         }
       }
@@ -531,7 +533,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
   float* ph = ps + h * kMaxSeq;
   const float scale = 1.0f / sqrtf((float)HD);
   const bool active = 2 * lane < HD;
-  const int kp = lane / PT, kr = lane & (PT - 1);  // this lane's key: page, row
   int k = 0;
   for (int item = blockIdx.x; item < items; item += gridDim.x) {
     int r, g, slot, len;
@@ -544,12 +545,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
       if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[sl], (k / kDecSlots) & 1, status))) return;
       const float* base = dsm + sl * kSlotFloats;
       if (lane < n) {
-        const float* pg = base + kp * kPageFloats;
-        const float* qh = base + kPages * kPageFloats + h * HD;
+        const float* qh = base + (kDecChunk / 8) * kBoxFloats + h * HD;
         float dot = 0.0f;
 #pragma unroll
         for (int i = 0; i < HD; i += 4) {
-          const float4 k4 = *reinterpret_cast<const float4*>(pg + swz<PT>(kr, h * HD + i));
+          const float4 k4 = *reinterpret_cast<const float4*>(base + swz(lane, h * HD + i, kBoxFloats));
           const float4 q4 = *reinterpret_cast<const float4*>(qh + i);
           dot = dot + q4.x * k4.x;
           dot = dot + q4.y * k4.y;
@@ -586,7 +586,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
         const int f = h * HD + 2 * lane;
 #pragma unroll 4
         for (int t = 0; t < n; ++t) {
-          const float2 v2 = *reinterpret_cast<const float2*>(base + (t / PT) * kPageFloats + swz<PT>(t & (PT - 1), f));
+          const float2 v2 = *reinterpret_cast<const float2*>(base + swz(t, f, kBoxFloats));
           const float p = ph[c0 + t];
           acc0 = acc0 + v2.x * p;
           acc1 = acc1 + v2.y * p;
@@ -788,8 +788,7 @@ cudaError_t launch_attn_decode_hd(const float* q, int ldq, int rows, const int32
                                   const CUtensorMap* v_map, int d, int heads, int8_t* out_q,
                                   float alpha, uint32_t* status, cudaStream_t s) {
   constexpr int W = kDecGroup * HD;
-  constexpr int kPageFloats = ((PT * W * 4 + 1023) / 1024) * 256;
-  const size_t smem = 1024 + sizeof(float) * ((size_t)kDecSlots * ((kDecChunk / PT) * kPageFloats + 256) +
+  const size_t smem = 1024 + sizeof(float) * ((size_t)kDecSlots * ((kDecChunk / 8) * 8 * W + 256) +
                                               (size_t)kDecGroup * kMaxSeq);
   static unsigned long long configured = 0;  // one bit per device ordinal
   static int sms[64] = {0};

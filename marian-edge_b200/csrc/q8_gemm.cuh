@@ -66,11 +66,11 @@ bool encode_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
 
 // Encodes a 3-D f32 tensor map over a KV-cache pool [rows, d] (row-major)
 // for the decode attention: dims {32 floats, rows, d / 32 column blocks}
-// (strides d * 4 and 128 bytes), box {32, page_tokens, group_cols / 32} --
-// one page's slice of group_cols columns per copy -- with the 128-byte
-// swizzle, which lands the slice in shared memory as [column block][page
-// row][32 floats] with each 16-byte chunk c of a 128-byte line stored at
-// chunk c ^ (line index % 8).
+// (strides d * 4 and 128 bytes), box {32, 8, group_cols / 32} -- eight
+// cache rows' slice of group_cols columns per copy (page_tokens, a multiple
+// of 8, keeps a box inside one page) -- with the 128-byte swizzle, which
+// lands the slice in shared memory as [column block][8 rows][32 floats]
+// with the 16-byte chunk c of row r stored at chunk c ^ r.
 bool encode_tmap_kv(CUtensorMap* map, const float* base, uint64_t rows, int d, int page_tokens,
                     int group_cols);
 
