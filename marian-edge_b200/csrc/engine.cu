@@ -316,6 +316,8 @@ mc_status upload_linear(mc_engine* e, const std::string& wname, const char* bnam
   CK(dalloc(e, &L->w, w.i8.size()));
   CK(cudaMemcpyAsync(L->w, w.i8.data(), w.i8.size(), cudaMemcpyHostToDevice, e->stream));
   const float inv = 1.0f / (L->alpha * w.quant_mult);  // q8_gemm.rs:438
+  if (!std::isfinite(inv) || inv <= 0.0f)
+    return fail(e, MC_MODEL, wname + ": 1 / (activation scale * quantization multiplier) is not finite");
   L->scale = inv;
   std::vector<float> cs(L->out, inv);
   CK(dalloc(e, &L->col_scale, cs.size()));
@@ -1279,6 +1281,8 @@ extern "C" mc_status mc_load_marian_bin(mc_engine* e, const uint8_t* bytes, size
     v.out = e->vtgt;
     if (!(err = activation_scale(m, "decoder_Wemb", &v.alpha)).empty()) return fail(e, MC_MODEL, err);
     v.scale = 1.0f / (v.alpha * e->dec_emb_mult);  // q8_engine.rs:772
+    if (!std::isfinite(v.scale) || v.scale <= 0.0f)
+      return fail(e, MC_MODEL, "decoder_Wemb: 1 / (activation scale * quantization multiplier) is not finite");
     std::vector<float> cs(e->vtgt, v.scale);
     CK(dalloc(e, &v.col_scale, cs.size()));
     CK(h2d(e, v.col_scale, cs.data(), cs.size() * 4));

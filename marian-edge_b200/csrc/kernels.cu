@@ -114,15 +114,154 @@ __global__ void embed_decoder_kernel(int cap, const int32_t* __restrict__ rows_d
 }
 
 // ---- LayerNorm (normalize_row, tensor.rs:372-385) ------------------------------
-// One warp per row.  The lanes load the row with coalesced 128-bit accesses
-// (lane l holds float4 chunks l, l + 32, ...), form the pre-norm values and
-// write them to a per-warp shared-memory row.  Lane 0 then sums the row left
-// to right, exactly as the reference's Iterator::sum; every lane forms its
-// centred squares (x - mean) * (x - mean), the same two roundings as the
-// reference's `var += c * c`, and lane 0 sums those left to right.  Only
-// the two dependent add chains are serial; everything else is spread over
-// the warp.  The normalized values and their quantized copies are written
-// back coalesced.
+// A CTA of 4 warps normalizes RPC = 8 rows.  The warps load the rows
+// with coalesced 128-bit accesses, form the pre-norm values and stage them in
+// shared memory (row stride d + 4 floats, so lanes reading different rows
+// at the same column hit distinct banks).  Then lane i of warp 0 owns row i:
+// it sums the row left to right, exactly as the reference's
+// Iterator::sum, and sums the centred squares (x - mean) * (x - mean) left
+// to right (the reference's `var += c * c`, two roundings) -- one warp
+// instruction advances RPC rows' ordered sums at once.  All warps then
+// normalize and write the rows and their quantized copies coalesced.  The
+// staging and normalizing loops have compile-time trip counts, so each
+// thread's loads are all in flight at once.
+constexpr int kLnThreads = 128;
+
+template <int VPL, int RPC>
+__device__ __forceinline__ void ln_rows(float* tile, int row0, int nrows,
+                                        const float* __restrict__ gamma,
+                                        const float* __restrict__ beta, float* __restrict__ out,
+                                        const QuantOut& q, uint32_t* status) {
+  constexpr int d = VPL * 128;
+  constexpr int ld = d + 4;
+  __shared__ float s_mean[RPC], s_inv[RPC];
+  __syncthreads();
+  if (threadIdx.x < RPC) {
+    const int i = threadIdx.x;
+    const float* row = tile + i * ld;
+    const float fd = (float)d;
+    float sum = 0.0f;
+#pragma unroll 8
+    for (int j = 0; j < d; j += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(row + j);
+      sum = sum + v.x;
+      sum = sum + v.y;
+      sum = sum + v.z;
+      sum = sum + v.w;
+    }
+    const float mean = sum / fd;
+    float var = 0.0f;
+#pragma unroll 8
+    for (int j = 0; j < d; j += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(row + j);
+      const float c0 = v.x - mean, c1 = v.y - mean, c2 = v.z - mean, c3 = v.w - mean;
+      var = var + c0 * c0;
+      var = var + c1 * c1;
+      var = var + c2 * c2;
+      var = var + c3 * c3;
+    }
+    var = var / fd;
+    s_mean[i] = mean;
+    s_inv[i] = 1.0f / sqrtf(var + kLnEps);
+  }
+  __syncthreads();
+  constexpr int kVec = d / 4;
+#pragma unroll
+  for (int it = 0; it < RPC * kVec / kLnThreads; ++it) {
+    const int idx = threadIdx.x + it * kLnThreads;
+    const int rr = idx / kVec, c = (idx - rr * kVec) * 4;
+    if (rr >= nrows) break;
+    const float4 t = *reinterpret_cast<const float4*>(tile + rr * ld + c);
+    const float mean = s_mean[rr], inv = s_inv[rr];
+    const float4 g = *reinterpret_cast<const float4*>(gamma + c);
+    const float4 b = *reinterpret_cast<const float4*>(beta + c);
+    float4 v;
+    v.x = (t.x - mean) * inv * g.x + b.x;
+    v.y = (t.y - mean) * inv * g.y + b.y;
+    v.z = (t.z - mean) * inv * g.z + b.z;
+    v.w = (t.w - mean) * inv * g.w + b.w;
+    const long long elem = (long long)(row0 + rr) * d + c;
+    *reinterpret_cast<float4*>(out + elem) = v;
+    store_quant4(q, elem, v.x, v.y, v.z, v.w, status);
+  }
+}
+
+template <int VPL, int RPC>
+__global__ void __launch_bounds__(kLnThreads) residual_ln_kernel(
+    const float* __restrict__ a, int lda, const float* __restrict__ r, int ldr,
+    const float* __restrict__ gamma, const float* __restrict__ beta, int cap,
+    const int32_t* __restrict__ rows_dev, float* __restrict__ out, const __grid_constant__ QuantOut q,
+    uint32_t* status) {
+  constexpr int d = VPL * 128;
+  constexpr int ld = d + 4, kVec = d / 4;
+  extern __shared__ __align__(16) float tile[];  // [RPC][d + 4]
+  pdl_enter();
+  const int rows = launch_rows(rows_dev, cap);
+  const int row0 = blockIdx.x * RPC;
+  const int nrows = min(RPC, rows - row0);
+  if (nrows <= 0) return;
+#pragma unroll
+  for (int it = 0; it < RPC * kVec / kLnThreads; ++it) {
+    const int idx = threadIdx.x + it * kLnThreads;
+    const int rr = idx / kVec, c = (idx - rr * kVec) * 4;
+    if (rr >= nrows) break;
+    const float4 x = *reinterpret_cast<const float4*>(a + (size_t)(row0 + rr) * lda + c);
+    const float4 y = *reinterpret_cast<const float4*>(r + (size_t)(row0 + rr) * ldr + c);
+    *reinterpret_cast<float4*>(tile + rr * ld + c) = make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+  }
+  ln_rows<VPL, RPC>(tile, row0, nrows, gamma, beta, out, q, status);
+}
+
+// tensor.rs:184-218: gate and state update per element, then the LayerNorm
+// of ReLU(state) + residual as above.
+template <int VPL, int RPC>
+__global__ void __launch_bounds__(kLnThreads) ssru_kernel(
+    const float* __restrict__ cf, int ld_cf, int fcol, float* __restrict__ state,
+    const int32_t* __restrict__ row_slot, const float* __restrict__ residual,
+    const float* __restrict__ gamma, const float* __restrict__ beta, int cap,
+    const int32_t* __restrict__ rows_dev, float* __restrict__ out, const __grid_constant__ QuantOut q,
+    uint32_t* status) {
+  constexpr int d = VPL * 128;
+  constexpr int ld = d + 4, kVec = d / 4;
+  extern __shared__ __align__(16) float tile[];
+  pdl_enter();
+  const int rows = launch_rows(rows_dev, cap);
+  const int row0 = blockIdx.x * RPC;
+  const int nrows = min(RPC, rows - row0);
+  if (nrows <= 0) return;
+#pragma unroll
+  for (int it = 0; it < RPC * kVec / kLnThreads; ++it) {
+    const int idx = threadIdx.x + it * kLnThreads;
+    const int rr = idx / kVec, c = (idx - rr * kVec) * 4;
+    if (rr >= nrows) break;
+    const int row = row0 + rr;
+    const float4 cv = *reinterpret_cast<const float4*>(cf + (size_t)row * ld_cf + c);
+    const float4 fv = *reinterpret_cast<const float4*>(cf + (size_t)row * ld_cf + fcol + c);
+    float* st = state + (size_t)row_slot[row] * d + c;
+    const float4 sv = *reinterpret_cast<const float4*>(st);
+    const float4 rv = *reinterpret_cast<const float4*>(residual + (size_t)row * d + c);
+    const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ff[4] = {fv.x, fv.y, fv.z, fv.w};
+    const float ss[4] = {sv.x, sv.y, sv.z, sv.w}, rs[4] = {rv.x, rv.y, rv.z, rv.w};
+    float nx[4], o[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float gate = 1.0f / (1.0f + exp_f32(-ff[u]));
+      nx[u] = gate * ss[u] + (1.0f - gate) * cc[u];
+      o[u] = fmaxf(nx[u], 0.0f) + rs[u];
+    }
+    *reinterpret_cast<float4*>(st) = make_float4(nx[0], nx[1], nx[2], nx[3]);
+    *reinterpret_cast<float4*>(tile + rr * ld + c) = make_float4(o[0], o[1], o[2], o[3]);
+  }
+  ln_rows<VPL, RPC>(tile, row0, nrows, gamma, beta, out, q, status);
+}
+
+// Warp-per-row variant for small launches (decode steps): each warp owns one
+// row end to end, so rows proceed without CTA-wide barriers.  The lanes load
+// the row with coalesced 128-bit accesses (lane l holds float4 chunks l,
+// l + 32, ...), form the pre-norm values and write them to a per-warp
+// shared-memory row; lane 0 sums the row left to right, every lane forms its
+// centred squares (x - mean) * (x - mean), and lane 0 sums those left to
+// right.
 constexpr int kLnWarps = 4;
 
 // VPL = float4 chunks per lane = d / 128.
@@ -198,7 +337,7 @@ __device__ __forceinline__ void ln_row(float4 (&x)[VPL], float* row, int grow,
 }
 
 template <int VPL>
-__global__ void __launch_bounds__(kLnWarps * 32) residual_ln_kernel(
+__global__ void __launch_bounds__(kLnWarps * 32) residual_ln_warp_kernel(
     const float* __restrict__ a, int lda, const float* __restrict__ r, int ldr,
     const float* __restrict__ gamma, const float* __restrict__ beta, int cap,
     const int32_t* __restrict__ rows_dev, float* __restrict__ out, const __grid_constant__ QuantOut q,
@@ -221,10 +360,9 @@ __global__ void __launch_bounds__(kLnWarps * 32) residual_ln_kernel(
   ln_row<VPL>(x, rows_s[warp], row, gamma, beta, out, q, status);
 }
 
-// tensor.rs:184-218: gate and state update per element, then the LayerNorm
-// of ReLU(state) + residual as above.
+// SSRU (tensor.rs:184-218) with the warp-per-row LayerNorm above.
 template <int VPL>
-__global__ void __launch_bounds__(kLnWarps * 32) ssru_kernel(
+__global__ void __launch_bounds__(kLnWarps * 32) ssru_warp_kernel(
     const float* __restrict__ cf, int ld_cf, int fcol, float* __restrict__ state,
     const int32_t* __restrict__ row_slot, const float* __restrict__ residual,
     const float* __restrict__ gamma, const float* __restrict__ beta, int cap,
@@ -711,20 +849,62 @@ void launch_embed_decoder(int rows, const int32_t* rows_dev, const int32_t* row_
       q, eos_mask, self_pages, pages_per_slot, page_tokens, self_row_map, status);
 }
 
+template <int VPL, int RPC, class Kern, class... Args>
+void launch_ln_cfg(Kern kernel, int rows, cudaStream_t s, Args... args) {
+  const size_t smem = sizeof(float) * RPC * (VPL * 128 + 4);
+  if (smem > 48 * 1024) {
+    static unsigned long long configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(configured & (1ull << (dev & 63)))) {
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      configured |= 1ull << (dev & 63);
+    }
+  }
+  launch_pdl(kernel, dim3(blocks_for(rows, RPC)), dim3(kLnThreads), smem, s, args...);
+}
+
+// Launches of up to kLnWarpRows rows (decode steps) take the warp-per-row
+// kernels, whose per-row latency is lower; larger ones (encoder passes) the
+// 8-rows-per-CTA kernels, which issue far fewer instructions per row.
+constexpr int kLnWarpRows = 2048;
+
+template <int VPL>
+void launch_residual_ln_v(const float* a, int lda, const float* r, int ldr, const float* gamma,
+                          const float* beta, int rows, const int32_t* rows_dev, float* out,
+                          const QuantOut& q, uint32_t* status, cudaStream_t s) {
+  if (rows <= kLnWarpRows)
+    launch_pdl(residual_ln_warp_kernel<VPL>, dim3(blocks_for(rows, kLnWarps)), dim3(kLnWarps * 32), 0, s,
+               a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status);
+  else
+    launch_ln_cfg<VPL, 8>(residual_ln_kernel<VPL, 8>, rows, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status);
+}
+
+template <int VPL>
+void launch_ssru_v(const float* cf, int ld, int fcol, float* state, const int32_t* row_slot,
+                   const float* residual, const float* gamma, const float* beta, int rows,
+                   const int32_t* rows_dev, float* out, const QuantOut& q, uint32_t* status,
+                   cudaStream_t s) {
+  if (rows <= kLnWarpRows)
+    launch_pdl(ssru_warp_kernel<VPL>, dim3(blocks_for(rows, kLnWarps)), dim3(kLnWarps * 32), 0, s, cf, ld,
+               fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status);
+  else
+    launch_ln_cfg<VPL, 8>(ssru_kernel<VPL, 8>, rows, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status);
+}
+
 void launch_residual_ln(const float* a, int lda, const float* r, int ldr, const float* gamma,
                         const float* beta, int rows, const int32_t* rows_dev, int d, float* out,
                         const QuantOut& q, uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return;
-  const dim3 grid(blocks_for(rows, kLnWarps)), block(kLnWarps * 32);
   switch (d) {
-    case 128: launch_pdl(residual_ln_kernel<1>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 256: launch_pdl(residual_ln_kernel<2>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 384: launch_pdl(residual_ln_kernel<3>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 512: launch_pdl(residual_ln_kernel<4>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 640: launch_pdl(residual_ln_kernel<5>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 768: launch_pdl(residual_ln_kernel<6>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 896: launch_pdl(residual_ln_kernel<7>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 1024: launch_pdl(residual_ln_kernel<8>, grid, block, 0, s, a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 128: launch_residual_ln_v<1>(a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 256: launch_residual_ln_v<2>(a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 384: launch_residual_ln_v<3>(a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 512: launch_residual_ln_v<4>(a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 640: launch_residual_ln_v<5>(a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 768: launch_residual_ln_v<6>(a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 896: launch_residual_ln_v<7>(a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 1024: launch_residual_ln_v<8>(a, lda, r, ldr, gamma, beta, rows, rows_dev, out, q, status, s); break;
     default: flag_status_host(status, s); break;
   }
 }
@@ -734,16 +914,15 @@ void launch_ssru(const float* cf, int ld, int fcol, float* state, const int32_t*
                  const int32_t* rows_dev, int d, float* out, const QuantOut& q, uint32_t* status,
                  cudaStream_t s) {
   if (rows <= 0) return;
-  const dim3 grid(blocks_for(rows, kLnWarps)), block(kLnWarps * 32);
   switch (d) {
-    case 128: launch_pdl(ssru_kernel<1>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 256: launch_pdl(ssru_kernel<2>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 384: launch_pdl(ssru_kernel<3>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 512: launch_pdl(ssru_kernel<4>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 640: launch_pdl(ssru_kernel<5>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 768: launch_pdl(ssru_kernel<6>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 896: launch_pdl(ssru_kernel<7>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
-    case 1024: launch_pdl(ssru_kernel<8>, grid, block, 0, s, cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status); break;
+    case 128: launch_ssru_v<1>(cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 256: launch_ssru_v<2>(cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 384: launch_ssru_v<3>(cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 512: launch_ssru_v<4>(cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 640: launch_ssru_v<5>(cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 768: launch_ssru_v<6>(cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 896: launch_ssru_v<7>(cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status, s); break;
+    case 1024: launch_ssru_v<8>(cf, ld, fcol, state, row_slot, residual, gamma, beta, rows, rows_dev, out, q, status, s); break;
     default: flag_status_host(status, s); break;
   }
 }

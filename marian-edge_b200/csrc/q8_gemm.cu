@@ -4,18 +4,18 @@
 // (crates/marian-cpu/src/q8_gemm.rs:380-448, q8_avx2.rs:125-229) and the
 // tied-vocabulary scoring of select_token (q8_engine.rs:749-790).
 //
-// One CTA computes a 128 x BN output tile:
+// One CTA computes 128 x BN output tiles (persistent over the tile list):
 //   warp 0      TMA producer: A and W tiles (128 K-bytes each) into a
 //               STAGES-deep ring of 128-byte-swizzled shared-memory buffers;
 //   warp 1      allocates TMEM and issues tcgen05.mma.kind::i8 (K = 32 per
 //               instruction) from one elected thread, committing each stage
 //               back to the producer and the finished accumulator to the
 //               epilogue;
-//   warps 2..5  epilogue: tcgen05.ld of the int32 accumulators (one row per
-//               thread, lanes = rows), dequantize/bias/ReLU/residual, and
-//               either an f32 store, an int8 store quantized for the next
-//               linear, or a per-row masked argmax merged with a 64-bit
-//               atomicMax.
+//   warps 2..   EPI epilogue warps (16 for BN 128/256, 8 for BN 64):
+//               tcgen05.ld of the int32 accumulators (one row per thread,
+//               lanes = rows), dequantize/bias/ReLU/residual, and either an
+//               f32 store, an int8 store quantized for the next linear, or a
+//               per-row masked argmax merged with a 64-bit atomicMax.
 #include "common.cuh"
 #include "q8_gemm.cuh"
 
@@ -27,8 +27,14 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 128;  // bytes of K per stage (= int8 elements)
-constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, each half the columns
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+
+// Epilogue warps per CTA: EPI / 4 per TMEM lane quarter, each taking an
+// equal share of the tile's columns.  16 for the one-CTA-per-SM tiles (BN 128
+// and 256), 8 for BN 64 (two CTAs per SM).
+template <int EPI>
+constexpr int threads_for() {
+  return 64 + 32 * EPI;
+}
 
 __device__ __forceinline__ unsigned long long pack_argmax(float v, int32_t n) {
   v = v + 0.0f;  // -0 -> +0: equal logits must compare equal (strict '>')
@@ -41,7 +47,26 @@ __device__ __forceinline__ unsigned long long pack_argmax(float v, int32_t n) {
 // stride keeps both the row-wise writes and the column-wise reads of the 32
 // lanes on distinct banks).
 constexpr int kStageLd = 33;
-constexpr int kStagingBytes = kEpiWarps * 32 * kStageLd * 4;
+template <int EPI>
+constexpr int staging_bytes() {
+  return EPI * 32 * kStageLd * 4;
+}
+
+// round(x * alpha) for the int8 store: ties-to-even, saturated to
+// [-128, 127] by the conversion; the caller bounds x * alpha below at -127
+// (unnecessary after ReLU).  NaN cannot reach here (see the Q8 epilogue).
+__device__ __forceinline__ int cvt_rni_sat_s8(float x) {
+  int r;
+  asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+// Low bytes of four ints -> one word (byte i = q[i]).
+__device__ __forceinline__ uint32_t pack4_s8(int q0, int q1, int q2, int q3) {
+  const uint32_t lo = __byte_perm((uint32_t)q0, (uint32_t)q1, 0x0040);
+  const uint32_t hi = __byte_perm((uint32_t)q2, (uint32_t)q3, 0x0040);
+  return __byte_perm(lo, hi, 0x5410);
+}
 
 // One 32-column chunk of one tile row per lane.  `ok` is this lane's row
 // validity; the call itself is warp-uniform (tcgen05.ld precedes it).
@@ -164,20 +189,29 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
         if (nb + j < n_end) out[j] = v[j];
     }
   } else {  // kEpiQ8
+    // quantize(v, alpha) as quantize_one does: rint(v * alpha) clamped to
+    // [-127, 127].  v comes from an integer accumulator times a finite scale
+    // plus a finite bias (the loader rejects non-finite payloads and
+    // scales), so it is finite unless it overflowed to +-inf, which the
+    // running |v| maximum detects.
     uint32_t q4[8];
-    bool finite = true;
+    float amax = 0.0f;
+    const float al = g.alpha;
+    const bool lower = !g.relu;  // after ReLU, v * alpha >= 0
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
-      uint32_t word = 0;
+      int qv[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int j = 4 * w + u;
-        finite &= fabsf(v[j]) <= 3.402823466e38f;  // false for NaN and +-inf
-        const int qi = (ok && nb + j < n_end) ? quantize_rte_clamped(v[j], g.alpha) : 0;
-        word |= (uint32_t)(uint8_t)(int8_t)qi << (8 * u);
+        amax = fmaxf(amax, fabsf(v[j]));
+        float t = __fmul_rn(v[j], al);
+        if (lower) t = fmaxf(t, -127.0f);
+        qv[u] = (ok && nb + j < n_end) ? cvt_rni_sat_s8(t) : 0;
       }
-      q4[w] = word;
+      q4[w] = pack4_s8(qv[0], qv[1], qv[2], qv[3]);
     }
+    const bool finite = amax <= 3.402823466e38f;
     if (!finite && ok) flag_status(status, kStatusNonFinite);
     const bool aligned = ((reinterpret_cast<uintptr_t>(g.out) | (uintptr_t)g.ldo |
                            (uintptr_t)(g.col_off + nb)) & 3) == 0;
@@ -231,14 +265,15 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 // The shared-memory ring continues across tiles, and the accumulator is
 // double-buffered in TMEM (2 x BN columns) so the epilogue of one tile
 // overlaps the MMAs of the next.
-template <int BN, int MAX_STAGES>
-__global__ void __launch_bounds__(kThreads, 2) q8_gemm_kernel(const __grid_constant__ GemmParams p) {
+template <int BN, int MAX_STAGES, int EPI>
+__global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_kernel(
+    const __grid_constant__ GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int stages = p.stages;
   uint8_t* smem_a = smem;                           // stages x 16 KB
   uint8_t* smem_b = smem + stages * kBM * kBK;      // stages x BN*128
-  uint32_t* staging = reinterpret_cast<uint32_t*>(smem_b + stages * BN * kBK);  // kStagingBytes
+  uint32_t* staging = reinterpret_cast<uint32_t*>(smem_b + stages * BN * kBK);  // staging_bytes<EPI>()
   __shared__ __align__(8) uint64_t full_bar[MAX_STAGES];
   __shared__ __align__(8) uint64_t empty_bar[MAX_STAGES];
   __shared__ __align__(8) uint64_t tfull_bar[2];
@@ -257,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 2) q8_gemm_kernel(const __grid_const
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], kEpiWarps);
+      mbar_init(&tempty_bar[b], EPI);
     }
     fence_barrier_init();
     for (int z = 0; z < p.num_groups; ++z) {
@@ -327,10 +362,10 @@ __global__ void __launch_bounds__(kThreads, 2) q8_gemm_kernel(const __grid_const
       }
     }
   } else {
-    // Epilogue warps 2..9: warp % 4 selects the TMEM lane quarter (rows),
-    // (warp - 2) / 4 the half of the tile's columns.
+    // Epilogue warps 2 .. EPI + 1: warp % 4 selects the TMEM lane quarter
+    // (rows), (warp - 2) / 4 the share of the tile's columns.
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int part = (warp - 2) >> 2;
     uint32_t* stage = staging + (warp - 2) * 32 * kStageLd;
     int it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -349,9 +384,9 @@ __global__ void __launch_bounds__(kThreads, 2) q8_gemm_kernel(const __grid_const
       float best = -INFINITY;
       int best_n = -1;
       const uint32_t lane_base = tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
-      constexpr int kHalf = BN / 2 >= 32 ? BN / 2 : 32;
+      constexpr int kShare = BN / (EPI / 4) >= 32 ? BN / (EPI / 4) : 32;
 #pragma unroll 1
-      for (int c0 = half * kHalf; c0 < BN && c0 < (half + 1) * kHalf; c0 += 32) {
+      for (int c0 = part * kShare; c0 < BN && c0 < (part + 1) * kShare; c0 += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(lane_base + c0, r);
         tmem_ld_wait();
@@ -393,25 +428,25 @@ int num_sms() {
   return cached[dev];
 }
 
-template <int BN, int MAX_STAGES>
+template <int BN, int MAX_STAGES, int EPI>
 cudaError_t configure_impl() {
   static unsigned long long configured = 0;  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured & (1ull << (dev & 63)))) {
-    cudaError_t e = cudaFuncSetAttribute(q8_gemm_kernel<BN, MAX_STAGES>,
+    cudaError_t e = cudaFuncSetAttribute(q8_gemm_kernel<BN, MAX_STAGES, EPI>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         MAX_STAGES * stage_bytes<BN>() + kStagingBytes + 1024);
+                                         MAX_STAGES * stage_bytes<BN>() + staging_bytes<EPI>() + 1024);
     if (e != cudaSuccess) return e;
     configured |= 1ull << (dev & 63);
   }
   return cudaSuccess;
 }
 
-template <int BN, int MAX_STAGES>
+template <int BN, int MAX_STAGES, int EPI>
 cudaError_t launch_impl(GemmParams p, cudaStream_t stream) {
-  auto kern = q8_gemm_kernel<BN, MAX_STAGES>;
-  cudaError_t ce = configure_impl<BN, MAX_STAGES>();
+  auto kern = q8_gemm_kernel<BN, MAX_STAGES, EPI>;
+  cudaError_t ce = configure_impl<BN, MAX_STAGES, EPI>();
   if (ce != cudaSuccess) return ce;
   const int num_kb = (p.k + kBK - 1) / kBK;
   const int tiles = ((p.max_n + BN - 1) / BN) * ((p.m + kBM - 1) / kBM) * p.num_groups;
@@ -424,7 +459,8 @@ cudaError_t launch_impl(GemmParams p, cudaStream_t stream) {
   }
   const int grid = tiles < num_sms() * ctas_per_sm ? tiles : num_sms() * ctas_per_sm;
   p.stages = stages;
-  launch_pdl(kern, dim3(grid), dim3(kThreads), stages * stage_bytes<BN>() + kStagingBytes + 1024, stream, p);
+  launch_pdl(kern, dim3(grid), dim3(threads_for<EPI>()),
+             stages * stage_bytes<BN>() + staging_bytes<EPI>() + 1024, stream, p);
   return cudaGetLastError();
 }
 
@@ -484,18 +520,18 @@ int pick_bn(int m, int max_n) {
 
 cudaError_t prepare_q8_gemm() {
   num_sms();
-  cudaError_t e = configure_impl<256, 3>();
-  if (e == cudaSuccess) e = configure_impl<128, 5>();
-  if (e == cudaSuccess) e = configure_impl<64, 7>();
+  cudaError_t e = configure_impl<256, 3, 16>();
+  if (e == cudaSuccess) e = configure_impl<128, 4, 16>();
+  if (e == cudaSuccess) e = configure_impl<64, 7, 8>();
   return e;
 }
 
 cudaError_t launch_q8_gemm(const GemmParams& p, int bn, cudaStream_t stream) {
   if (p.m <= 0 || p.num_groups <= 0) return cudaSuccess;
   switch (bn) {
-    case 256: return launch_impl<256, 3>(p, stream);
-    case 128: return launch_impl<128, 5>(p, stream);
-    default: return launch_impl<64, 7>(p, stream);
+    case 256: return launch_impl<256, 3, 16>(p, stream);
+    case 128: return launch_impl<128, 4, 16>(p, stream);
+    default: return launch_impl<64, 7, 8>(p, stream);
   }
 }
 
