@@ -51,7 +51,11 @@ def test_config_validation_rejects_bad_values():
     lib = L.load()
     cfg = L.Config()
     lib.mc_config_default(C.byref(cfg))
-    assert (cfg.max_inflight, cfg.page_tokens, cfg.max_length_factor) == (1024, 16, 3)
-    cfg.max_length_factor = 9
+    assert (cfg.max_inflight, cfg.page_tokens, cfg.max_length_factor, cfg.lanes) == (1024, 16, 3, 1)
     h = C.c_void_p()
-    assert lib.mc_create(C.byref(cfg), C.byref(h)) == L.MC_INVALID_INPUT
+    for field, bad in (("max_length_factor", 9), ("page_tokens", 12), ("lanes", 9), ("max_inflight", 0)):
+        c2 = L.Config()
+        lib.mc_config_default(C.byref(c2))
+        setattr(c2, field, bad)
+        assert lib.mc_create(C.byref(c2), C.byref(h)) == L.MC_INVALID_INPUT, field
+        assert not h.value

@@ -234,3 +234,80 @@ def test_full_shapes_are_bit_exact_on_reference_legal_batches(name):
                 np.testing.assert_array_equal(gtr["cross_value"][:, valid], tr["cross_value"][:, valid])
                 st, rs = gtr["decoder_state_step0"], tr["decoder_state_step0"]
                 assert np.abs(st - rs).max() <= 1e-6 * np.abs(rs).max()
+
+
+def test_wide_batch_is_bit_exact_through_large_tile_paths():
+    # 160 sentences in one encoder pass (> 2,048 packed tokens) and 160 decode
+    # rows: exercises the 8-rows-per-CTA LayerNorm of encoder passes and the
+    # 128/256-column GEMM tiles with 16 epilogue warps (f32, int8 FFN and
+    # vocabulary-argmax epilogues).  Every sentence is compared with the
+    # oracle, which runs reference-legal sub-batches (a sentence's encoder
+    # rows, cross keys/values and tokens do not depend on its batch).
+    mb = model("graph_b")
+    full = W.short_batch(n=160, vocab=32000, seed=77, lo=18, hi=40)
+    assert int(full.offsets[-1]) > 2048
+    om = O.OracleModel(mb)
+    with CudaEngine(mb, max_inflight=256, max_encode_tokens=8192) as eng:
+        gtr = eng.trace_first_step(full.tokens, full.offsets)
+        got, got_off = eng.translate_token_ids(full.tokens, full.offsets, full.max_out, full.force_len)
+    lens = np.diff(full.offsets.astype(np.int64))
+    lmax = int(lens.max())
+    for grp in W.legal_cpu_batches(full):
+        sb = W.subset(full, grp)
+        ref, ref_off, tr = om.translate(sb.tokens, sb.offsets, sb.max_out, sb.force_len, trace=True)
+        sl = int(np.diff(sb.offsets.astype(np.int64)).max())
+        for j, row in enumerate(grp):
+            n = int(lens[row])
+            g_rows = slice(row * lmax, row * lmax + n)
+            r_rows = slice(j * sl, j * sl + n)
+            np.testing.assert_array_equal(gtr["encoder_output"][g_rows], tr["encoder_output"][r_rows])
+            np.testing.assert_array_equal(gtr["cross_key"][:, g_rows], tr["cross_key"][:, r_rows])
+            np.testing.assert_array_equal(gtr["cross_value"][:, g_rows], tr["cross_value"][:, r_rows])
+            st, rs = gtr["decoder_state_step0"][row], tr["decoder_state_step0"][j]
+            assert np.abs(st - rs).max() <= 1e-6 * np.abs(rs).max()
+            np.testing.assert_array_equal(got[got_off[row]:got_off[row + 1]],
+                                          ref[ref_off[j]:ref_off[j + 1]])
+
+
+@pytest.mark.parametrize("name,lanes,page_tokens", [("tiny_self", 2, 16), ("tiny_self", 3, 8),
+                                                     ("tiny_ssru", 2, 32), ("tiny_self", 1, 32)])
+def test_lanes_and_page_sizes_match_oracle(name, lanes, page_tokens):
+    # Rows split over several decode lanes (each with its own stream, CUDA
+    # graph and encoder stream) and 8/16/32-token KV pages must not change a
+    # single token.
+    batch = W.short_batch(n=24, vocab=512, seed=13, lo=4, hi=40)
+    ref, ref_off = O.OracleModel(model(name)).translate(batch.tokens, batch.offsets, batch.max_out,
+                                                        batch.force_len)
+    with CudaEngine(model(name), max_inflight=12, max_encode_tokens=1024, lanes=lanes,
+                    page_tokens=page_tokens) as eng:
+        for _ in range(2):  # the second call replays the lanes' captured graphs
+            got, got_off = eng.translate_token_ids(batch.tokens, batch.offsets, batch.max_out,
+                                                   batch.force_len)
+            np.testing.assert_array_equal(got_off, ref_off)
+            np.testing.assert_array_equal(got, ref)
+
+
+def test_streaming_with_lanes_matches_static_batch():
+    # Requests arrive while others decode: admissions encode on the lanes'
+    # encoder streams and join between steps; every result equals the static
+    # batch's.
+    name = "tiny_ssru"
+    batch = W.short_batch(n=40, vocab=512, seed=17, lo=3, hi=30)
+    with CudaEngine(model(name), max_inflight=64, max_encode_tokens=1024) as eng:
+        ref, ref_off = eng.translate_token_ids(batch.tokens, batch.offsets, batch.max_out, batch.force_len)
+    with CudaEngine(model(name), max_inflight=10, max_encode_tokens=512, lanes=2) as eng:
+        results, nxt = {}, 0
+        for _ in range(8000):
+            for _ in range(3):  # a few arrivals per step
+                if nxt < batch.size:
+                    s, e = batch.offsets[nxt], batch.offsets[nxt + 1]
+                    eng.submit(nxt, batch.tokens[s:e], int(batch.max_out[nxt]), int(batch.force_len[nxt]))
+                    nxt += 1
+            active, queued = eng.step()
+            for rid, toks in eng.poll():
+                results[rid] = toks
+            if nxt == batch.size and active == 0 and queued == 0:
+                break
+    assert sorted(results) == list(range(batch.size))
+    for b in range(batch.size):
+        np.testing.assert_array_equal(results[b], ref[ref_off[b]:ref_off[b + 1]])
