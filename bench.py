@@ -211,15 +211,15 @@ def reduce_job(tokens, dev_ms, wall_s, world, device):
 
 
 # DRAM traffic per algorithmic byte, from one ncu --set full capture of each
-# kernel class on the benchmark stream (2,048-request run, steady-state
-# launch; dram__bytes_read.sum + dram__bytes_write.sum divided by the
-# engine's algorithmic byte count for the same launch).  The bench scales it
-# to its own launches; classes without a capture report null.
+# kernel class on the benchmark stream (2,048-request run; launches and
+# figures in profiles/: dram__bytes_read.sum + dram__bytes_write.sum divided
+# by the engine's algorithmic byte count for the same launch).  The bench
+# scales it to its own launches; classes without a capture report null.
 DRAM_PER_ALGO_BYTE = {
-    "attn_cross": 151.4 / 147.3,   # 1,024 rows, 35,325 keys
-    "attn_self": 151.4 / 147.3,    # same kernel, same page layout
-    "gemm_vocab": 17.13 / 17.16,   # M=1,024, N=32,000, K=512
-    "layernorm": 4.25 / 6.82,      # 1,024 rows; outputs still in L2 at exit
+    "attn_cross": 165.4 / 147.3,   # 1,024 rows, 35,325 keys, 8-row TMA boxes
+    "attn_self": 165.4 / 147.3,    # same kernel and page layout
+    "gemm_vocab": 17.12 / 17.16,   # M=1,024, N=32,000, K=512
+    "layernorm": 4.24 / 6.82,      # 1,024 rows; outputs still in L2 at exit
 }
 
 
