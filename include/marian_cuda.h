@@ -86,6 +86,18 @@ mc_status mc_load_marian_bin(mc_engine *e, const uint8_t *bytes, size_t len);
 
 mc_status mc_model_info_get(const mc_engine *e, mc_model_info *info);
 
+/* Loads a Marian lexical shortlist (LexicalShortlist::from_bytes and
+ * ::candidates, marian-model/src/shortlist.rs:59-198; the engine's
+ * prepare_candidates, marian-cpu/src/q8_engine.rs:576-584): each sentence's
+ * output token is then the argmax over its own candidates -- ids below
+ * firstNum, the shortlist targets of its source tokens, minus UNK and ids
+ * 7..38, padded to a multiple of 8 with the first absent ids from 50.
+ * bytes == NULL restores the full vocabulary.  Requires a loaded model and
+ * no requests in flight.  Malformed files return MC_MODEL; a sentence whose
+ * candidates lack EOS (0) is rejected with MC_INFERENCE, as the reference
+ * rejects it. */
+mc_status mc_load_shortlist(mc_engine *e, const uint8_t *bytes, size_t len);
+
 void mc_destroy(mc_engine *e);
 
 /* Copies the last error message (NUL-terminated, truncated to cap) and

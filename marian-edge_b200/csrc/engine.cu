@@ -177,6 +177,15 @@ struct mc_engine {
   int tmax = 0;  // packed tokens per encoder pass
   int rmax = 0;  // slots
 
+  // lexical shortlist (mc_load_shortlist): device copy of the offsets and
+  // targets, per-slot candidate bitmasks, and per source token whether it
+  // maps to EOS (the reference requires EOS among a sentence's candidates)
+  bool has_shortlist = false;
+  int sl_first_num = 0, sl_words = 0;
+  int32_t *sl_offsets = nullptr, *sl_targets = nullptr;
+  uint32_t* sl_masks = nullptr;
+  std::vector<uint8_t> sl_maps_eos;
+
   // slots and caches (shared by the lanes)
   int32_t *slot_prev = nullptr, *slot_step = nullptr, *slot_limit = nullptr, *slot_force = nullptr,
           *slot_src = nullptr;
@@ -411,6 +420,11 @@ mc_status gemm(mc_engine* e, Lane& L, int kind, int m, const int32_t* m_dev, dou
     g.relu = s.relu;
     g.argmax = argmax;
     g.eos_mask = eos;
+    if (s.mode == kEpiArgmax && e->has_shortlist) {
+      g.cand_rows = e->sl_masks;
+      g.cand_slot = L.row_slot();
+      g.cand_words = e->sl_words;
+    }
   }
   p.m = m;
   p.m_dev = m_dev;
@@ -1011,6 +1025,11 @@ mc_status admit(mc_engine* e, Lane& L, int cap) {
                     e->dec_layers, e->rmax, e->d, ad + A.pages, e->cross_pages_d,
                     e->kind == 1 ? e->self_pages_d : nullptr, pps, s);
   ++e->launches;
+  if (e->has_shortlist) {
+    launch_shortlist_masks(B, ad + A.slots, ad + A.tok, ad + A.cu, e->sl_offsets, e->sl_targets,
+                           e->sl_first_num, e->vtgt, e->sl_masks, s);
+    ++e->launches;
+  }
   CK(cudaEventRecord(L.enc_done, s));
   return MC_OK;
 }
@@ -1184,6 +1203,17 @@ mc_status drain_lanes(mc_engine* e) {
   return MC_OK;
 }
 
+mc_status validate_source(const mc_engine* e, const int32_t* tokens, size_t n, std::string* why);
+
+// shortlist.rs:193-196: a sentence whose candidates lack EOS is an error.
+mc_status validate_shortlist(const mc_engine* e, const int32_t* tokens, size_t n, std::string* why) {
+  if (!e->has_shortlist || e->sl_first_num > 0) return MC_OK;
+  for (size_t i = 0; i < n; ++i)
+    if (e->sl_maps_eos[tokens[i]]) return MC_OK;
+  *why = "lexical shortlist does not contain EOS token 0";
+  return MC_INFERENCE;
+}
+
 mc_status validate_source(const mc_engine* e, const int32_t* tokens, size_t n, std::string* why) {
   if (n == 0) {
     *why = "each input must contain at least one token";
@@ -1199,7 +1229,7 @@ mc_status validate_source(const mc_engine* e, const int32_t* tokens, size_t n, s
              std::to_string(e->vsrc);
       return MC_INVALID_INPUT;
     }
-  return MC_OK;
+  return validate_shortlist(e, tokens, n, why);
 }
 
 }  // namespace
@@ -1557,6 +1587,99 @@ extern "C" mc_status mc_trace_first_step(mc_engine* e, const int32_t* tokens, si
   if (decoder_state)
     CK(cudaMemcpy(decoder_state, L.last_state, (size_t)batch * row_bytes, cudaMemcpyDeviceToHost));
   abort_all(e);
+  return MC_OK;
+}
+
+namespace {
+
+uint64_t read_le64(const uint8_t* p) {
+  uint64_t v = 0;
+  for (int i = 7; i >= 0; --i) v = (v << 8) | p[i];
+  return v;
+}
+
+uint32_t read_le32(const uint8_t* p) {
+  return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+// LexicalShortlist::from_bytes (marian-model/src/shortlist.rs:59-148).
+std::string parse_shortlist(const uint8_t* b, size_t len, uint64_t source_vocab, uint64_t target_vocab,
+                            uint64_t* first_num, std::vector<uint64_t>* offsets,
+                            std::vector<uint32_t>* targets) {
+  constexpr uint64_t kMagic = 17373278592220534773ull;     // shortlist.rs:3
+  constexpr uint64_t kMaxTargets = 4000000;                // shortlist.rs:4
+  const uint64_t maximum = 48 + (source_vocab + 1) * 8 + kMaxTargets * 4;
+  if (len > maximum)
+    return "lexical shortlist has " + std::to_string(len) + " bytes; maximum is " + std::to_string(maximum);
+  if (len < 48) return "truncated lexical shortlist header";
+  const uint64_t magic = read_le64(b), fn = read_le64(b + 16), n_off = read_le64(b + 32),
+                 n_tgt = read_le64(b + 40);
+  if (magic != kMagic || n_off != source_vocab + 1 || fn > target_vocab || n_tgt > kMaxTargets)
+    return "unsupported lexical shortlist format";
+  const uint64_t expected = 48 + n_off * 8 + n_tgt * 4;
+  if (len != expected)
+    return "lexical shortlist has " + std::to_string(len) + " bytes, expected " + std::to_string(expected);
+  offsets->resize(n_off);
+  for (uint64_t i = 0; i < n_off; ++i) (*offsets)[i] = read_le64(b + 48 + 8 * i);
+  bool bad = offsets->front() != 0 || offsets->back() != n_tgt;
+  for (uint64_t i = 1; i < n_off && !bad; ++i)
+    bad = (*offsets)[i - 1] > (*offsets)[i] || (*offsets)[i] > n_tgt;
+  if (bad) return "lexical shortlist offsets are invalid";
+  targets->resize(n_tgt);
+  const uint8_t* tp = b + 48 + n_off * 8;
+  for (uint64_t i = 0; i < n_tgt; ++i) {
+    const uint32_t t = read_le32(tp + 4 * i);
+    if (t >= target_vocab)
+      return "lexical shortlist target " + std::to_string(t) + " exceeds vocabulary " +
+             std::to_string(target_vocab);
+    (*targets)[i] = t;
+  }
+  *first_num = fn;
+  return "";
+}
+
+}  // namespace
+
+extern "C" mc_status mc_load_shortlist(mc_engine* e, const uint8_t* bytes, size_t len) {
+  if (!e) return MC_INVALID_INPUT;
+  if (!e->loaded) return fail(e, MC_MODEL, "no model loaded");
+  if (!e->queue.empty() || total_active(e) != 0)
+    return fail(e, MC_INVALID_INPUT, "engine has requests in flight");
+  mc_status st = set_device(e);
+  if (st) return st;
+  if (!bytes) {  // back to the full vocabulary
+    e->has_shortlist = false;
+  } else {
+    uint64_t first_num = 0;
+    std::vector<uint64_t> offsets;
+    std::vector<uint32_t> targets;
+    const std::string err = parse_shortlist(bytes, len, (uint64_t)e->vsrc, (uint64_t)e->vtgt, &first_num,
+                                            &offsets, &targets);
+    if (!err.empty()) return fail(e, MC_MODEL, err);
+    if (e->vtgt > 393216) return fail(e, MC_MODEL, "target vocabulary too large for a shortlist");
+    std::vector<int32_t> off32(offsets.begin(), offsets.end()), tg32(targets.begin(), targets.end());
+    if (tg32.empty()) tg32.push_back(0);
+    e->sl_maps_eos.assign(e->vsrc, 0);
+    for (int t = 0; t < e->vsrc; ++t)
+      for (uint64_t j = offsets[t]; j < offsets[t + 1]; ++j)
+        if (targets[j] == 0) e->sl_maps_eos[t] = 1;
+    // allocations grow only; they are released with the engine
+    CK(dalloc(e, &e->sl_offsets, off32.size()));
+    CK(h2d(e, e->sl_offsets, off32.data(), off32.size() * 4));
+    CK(dalloc(e, &e->sl_targets, tg32.size()));
+    CK(h2d(e, e->sl_targets, tg32.data(), tg32.size() * 4));
+    e->sl_words = (e->vtgt + 31) / 32;
+    if (!e->sl_masks) CK(dalloc(e, &e->sl_masks, (size_t)e->rmax * e->sl_words));
+    e->sl_first_num = (int)first_num;
+    e->has_shortlist = true;
+  }
+  // the decode graphs captured so far bake the vocabulary launch's arguments
+  for (Lane& L : e->lanes) {
+    if (L.graph) cudaGraphExecDestroy(L.graph);
+    L.graph = nullptr;
+    L.graph_tried = false;
+    L.eager_steps = 0;
+  }
   return MC_OK;
 }
 

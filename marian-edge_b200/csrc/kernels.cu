@@ -811,6 +811,62 @@ __global__ void init_slots_kernel(int n, const int32_t* slots, const int32_t* li
         ssru_state[((size_t)l * max_slots + s) * d + k] = 0.0f;
 }
 
+// ---- lexical shortlist candidates (shortlist.rs:150-198) ------------------
+// One CTA per admitted request builds the slot's candidate bitmask in shared
+// memory: ids below first_num, every target of every source token, minus
+// UNK (1) and the byte/control fallbacks 7..38, then the first absent ids
+// from 50 up until the count is a multiple of 8 -- the reference's set
+// (which it then sorts; a bitmask is already in id order).
+__global__ void shortlist_mask_kernel(int n, const int32_t* __restrict__ slots,
+                                      const int32_t* __restrict__ tokens,
+                                      const int32_t* __restrict__ cu,
+                                      const int32_t* __restrict__ offsets,
+                                      const int32_t* __restrict__ targets, int first_num, int vocab,
+                                      int words, uint32_t* __restrict__ masks) {
+  extern __shared__ uint32_t cm[];
+  __shared__ int s_count;
+  pdl_enter();
+  const int b = blockIdx.x;
+  if (b >= n) return;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) {
+    const int lo = w * 32;
+    cm[w] = first_num >= lo + 32 ? 0xFFFFFFFFu : (first_num > lo ? (1u << (first_num - lo)) - 1u : 0u);
+  }
+  if (threadIdx.x == 0) s_count = 0;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int i = cu[b] + warp; i < cu[b + 1]; i += nwarps) {
+    const int t = tokens[i];
+    for (int j = offsets[t] + lane; j < offsets[t + 1]; j += 32) {
+      const int id = targets[j];
+      atomicOr(&cm[id >> 5], 1u << (id & 31));
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (vocab > 1) cm[0] &= ~2u;
+    for (int id = 7; id < min(vocab, 39); ++id) cm[id >> 5] &= ~(1u << (id & 31));
+  }
+  __syncthreads();
+  int c = 0;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) c += __popc(cm[w]);
+  atomicAdd(&s_count, c);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int need = (8 - s_count % 8) % 8;
+    for (int id = 50; id < vocab && need > 0; ++id) {
+      const uint32_t bit = 1u << (id & 31);
+      if (!(cm[id >> 5] & bit)) {
+        cm[id >> 5] |= bit;
+        --need;
+      }
+    }
+  }
+  __syncthreads();
+  uint32_t* out = masks + (size_t)slots[b] * words;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) out[w] = cm[w];
+}
+
 __global__ void flag_status_kernel(uint32_t* status) {
   if (threadIdx.x == 0) flag_status(status, kStatusBadIndex);
 }
@@ -1037,6 +1093,15 @@ void launch_finalize(int rows, const int32_t* rows_dev, const int32_t* row_slot,
   if (rows <= 0) return;
   launch_pdl(finalize_kernel, dim3(blocks_for(rows, 128)), dim3(128), 0, s, rows, rows_dev, row_slot, best, slot_prev, slot_step,
                                                         slot_limit, step_tokens, done, status);
+}
+
+void launch_shortlist_masks(int n, const int32_t* slots, const int32_t* tokens, const int32_t* cu,
+                            const int32_t* offsets, const int32_t* targets, int first_num, int vocab,
+                            uint32_t* masks, cudaStream_t s) {
+  if (n <= 0) return;
+  const int words = (vocab + 31) / 32;
+  launch_pdl(shortlist_mask_kernel, dim3(n), dim3(256), (size_t)words * 4, s, n, slots, tokens, cu,
+             offsets, targets, first_num, vocab, words, masks);
 }
 
 void launch_init_slots(int n, const int32_t* slots, const int32_t* limits, const int32_t* force,

@@ -96,6 +96,14 @@ void launch_finalize(int rows, const int32_t* rows_dev, const int32_t* row_slot,
 void launch_quantize(const float* x, long long n, float alpha, int8_t* out, uint32_t* status,
                      cudaStream_t s);
 
+// shortlist.rs:150-198 on the device: for admitted request i (slot
+// slots[i], source tokens tokens[cu[i] .. cu[i + 1])) writes the candidate
+// bitmask masks[slot][(vocab + 31) / 32] of the lexical shortlist
+// (offsets[source_vocab + 1], targets, first_num).  vocab <= 393,216.
+void launch_shortlist_masks(int n, const int32_t* slots, const int32_t* tokens, const int32_t* cu,
+                            const int32_t* offsets, const int32_t* targets, int first_num, int vocab,
+                            uint32_t* masks, cudaStream_t s);
+
 // Initializes newly admitted slots: prev = -1, step = 0, limit, force_len,
 // source length, SSRU states zeroed (state pools [layers][slots][d]), and
 // copies each slot's page-table rows from page_rows ([n][pages_per_slot]

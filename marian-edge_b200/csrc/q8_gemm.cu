@@ -93,6 +93,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
       v[4 * j4 + 2] = dequant(static_cast<int32_t>(r[4 * j4 + 2]), uscale, b.z);
       v[4 * j4 + 3] = dequant(static_cast<int32_t>(r[4 * j4 + 3]), uscale, b.w);
     }
+    if (g.cand_rows) {  // the row's shortlist candidates (shortlist.rs:150-198)
+      const uint32_t word = g.cand_rows[(size_t)g.cand_slot[row] * g.cand_words + (nb >> 5)];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (!((word >> j) & 1u)) v[j] = -INFINITY;
+    }
     if (nb == 0 && g.eos_mask != nullptr && g.eos_mask[row] != 0) v[0] = -INFINITY;
     float t16[16];
 #pragma unroll

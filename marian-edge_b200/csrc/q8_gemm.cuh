@@ -34,6 +34,10 @@ struct alignas(64) GemmGroup {
   const int32_t* row_map;      // [M] destination row per source row, or null
   unsigned long long* argmax;  // [dest rows] packed (value, index) maxima (kEpiArgmax)
   const uint8_t* eos_mask;     // [M] 1 = token 0 excluded for this row (kEpiArgmax)
+  const uint32_t* cand_rows;   // kEpiArgmax, nullable: per-slot candidate bitmasks
+                               // [slots][cand_words] (lexical shortlist)
+  const int32_t* cand_slot;    // [M] slot of each row (indexes cand_rows)
+  int32_t cand_words;          // words per candidate bitmask
   int32_t n;                   // output columns of this group
   int32_t ldo;                 // output row stride (elements)
   int32_t col_off;             // first output column of this group

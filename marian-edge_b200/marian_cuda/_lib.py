@@ -18,7 +18,7 @@ EXPORTS = [
     "mc_config_default", "mc_create", "mc_load_marian_bin", "mc_model_info_get", "mc_destroy",
     "mc_last_error", "mc_is_ready", "mc_translate_token_ids", "mc_submit", "mc_step", "mc_poll",
     "mc_trace_first_step", "mc_stream", "mc_q8_gemm", "mc_op_status", "mc_profile",
-    "mc_profile_read", "mc_launch_count", "mc_q8_linear", "mc_q8_linear_noalloc",
+    "mc_profile_read", "mc_launch_count", "mc_q8_linear", "mc_q8_linear_noalloc", "mc_load_shortlist",
 ]
 
 # MC_Q8_LINEAR_NOALLOC_MAX_ACTIVATIONS in include/marian_cuda.h
@@ -90,6 +90,7 @@ def load(build_if_missing: bool = True):
     lib.mc_profile.argtypes = [vp, i32]
     lib.mc_profile_read.argtypes = [vp, i32, C.POINTER(u64), C.POINTER(C.c_double),
                                     C.POINTER(C.c_double), C.POINTER(C.c_double)]
+    lib.mc_load_shortlist.argtypes = [vp, C.c_char_p, sz]
     lib.mc_launch_count.argtypes = [vp]
     lib.mc_launch_count.restype = u64
     _lib = lib

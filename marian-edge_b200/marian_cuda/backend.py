@@ -40,7 +40,7 @@ class BackendInfo:
 class CudaEngine:
     def __init__(self, model_bytes: bytes, device: int = 0, max_inflight: int = 1024,
                  max_encode_tokens: int = 65536, page_tokens: int = 16, kv_pages: int = 0,
-                 max_length_factor: int = 3, lanes: int = 0):
+                 max_length_factor: int = 3, lanes: int = 0, shortlist: bytes | None = None):
         self._lib = L.load()
         cfg = L.Config()
         self._lib.mc_config_default(C.byref(cfg))
@@ -53,6 +53,8 @@ class CudaEngine:
         self._h = h
         self.device = device
         L.check(self._lib.mc_load_marian_bin(h, model_bytes, len(model_bytes)), h)
+        if shortlist is not None:
+            L.check(self._lib.mc_load_shortlist(h, shortlist, len(shortlist)), h)
         info = L.ModelInfo()
         L.check(self._lib.mc_model_info_get(h, C.byref(info)), h)
         self.info = info

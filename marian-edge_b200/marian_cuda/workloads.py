@@ -243,3 +243,34 @@ def subset(batch: Batch, rows) -> Batch:
     srcs = [batch.tokens[batch.offsets[r]:batch.offsets[r + 1] - 1] for r in rows]
     b = pack(srcs, max_out=batch.max_out[rows], force=batch.force_len is not None)
     return b
+
+
+# ---- lexical shortlist files (marian-model/src/shortlist.rs:59-148 format) ---
+SHORTLIST_MAGIC = 17_373_278_592_220_534_773
+
+
+def shortlist_bytes(first_num: int, offsets, targets) -> bytes:
+    """A Marian lexical shortlist file: six little-endian u64 header fields
+    (magic, 0, firstNum, 0, offset count, target count), u64 offsets, u32
+    targets -- the layout the reference's test fixture writes
+    (shortlist.rs:239-257)."""
+    offsets = np.asarray(offsets, dtype="<u8")
+    targets = np.asarray(targets, dtype="<u4")
+    head = np.array([SHORTLIST_MAGIC, 0, first_num, 0, offsets.size, targets.size], dtype="<u8")
+    return head.tobytes() + offsets.tobytes() + targets.tobytes()
+
+
+def synthetic_shortlist(source_vocab: int, target_vocab: int, seed: int = 0, first_num: int = 100,
+                        max_per_token: int = 40) -> bytes:
+    """Seeded random shortlist: each source id gets 0..max_per_token distinct
+    uniformly drawn target ids in [2, target_vocab); ids below first_num (EOS
+    among them when first_num > 0) are always candidates."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    offsets = [0]
+    targets = []
+    for _ in range(source_vocab):
+        k = int(rng.integers(0, max_per_token + 1))
+        ids = np.unique(rng.integers(2, target_vocab, size=k)) if k else np.zeros(0, np.int64)
+        targets.extend(int(t) for t in ids)
+        offsets.append(len(targets))
+    return shortlist_bytes(first_num, offsets, targets)

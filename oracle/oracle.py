@@ -8,6 +8,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import struct
 import subprocess
 import sys
 
@@ -48,6 +49,10 @@ class SsruBlock(C.Structure):
     _fields_ = [("w", Linear), ("wf", Linear), ("ln_scale", C.c_void_p), ("ln_bias", C.c_void_p)]
 
 
+class Shortlist(C.Structure):
+    _fields_ = [("first_num", C.c_uint64), ("offsets", C.c_void_p), ("targets", C.c_void_p)]
+
+
 class Model(C.Structure):
     _fields_ = [("dim", C.c_int32), ("heads", C.c_int32), ("ffn_dim", C.c_int32),
                 ("encoder_layers", C.c_int32), ("decoder_layers", C.c_int32),
@@ -61,7 +66,8 @@ class Model(C.Structure):
                 ("decoder_ssru", SsruBlock * MAX_LAYERS),
                 ("decoder_self", AttentionBlock * MAX_LAYERS),
                 ("decoder_context", AttentionBlock * MAX_LAYERS),
-                ("decoder_ffn", FfnBlock * MAX_LAYERS)]
+                ("decoder_ffn", FfnBlock * MAX_LAYERS),
+                ("shortlist", Shortlist)]
 
 
 class Trace(C.Structure):
@@ -93,6 +99,9 @@ def lib():
         _lib.oq_select_token.restype = C.c_int64
         _lib.oq_select_token.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_float, C.c_float,
                                          C.c_void_p, C.c_void_p, C.c_size_t]
+        _lib.oq_shortlist_candidates.restype = C.c_int64
+        _lib.oq_shortlist_candidates.argtypes = [C.POINTER(Shortlist), C.c_size_t, C.c_size_t, C.c_void_p,
+                                                 C.c_size_t, C.c_void_p]
         _lib.oq_translate.argtypes = [C.POINTER(Model), C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
                                       C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
                                       C.POINTER(Trace), C.c_char_p, C.c_size_t]
@@ -203,6 +212,65 @@ def full_vocab_candidates(vocab):
     return out[:n].copy()
 
 
+# ---- lexical shortlist (marian-model/src/shortlist.rs) -----------------------
+
+SHORTLIST_MAGIC = 17_373_278_592_220_534_773       # shortlist.rs:3
+SHORTLIST_MAX_TARGET_ENTRIES = 4_000_000           # shortlist.rs:4
+
+
+def parse_shortlist(data: bytes, source_vocab: int, target_vocab: int):
+    """LexicalShortlist::from_bytes (shortlist.rs:59-148): a 48-byte header of
+    six little-endian u64 (magic, -, firstNum, -, offset count, target count),
+    the u64 offsets (source_vocab + 1, from 0 up to the target count) and the
+    u32 target ids.  Returns (first_num, offsets, targets); raises ValueError
+    with the reference's messages."""
+    maximum = 48 + (source_vocab + 1) * 8 + SHORTLIST_MAX_TARGET_ENTRIES * 4
+    if len(data) > maximum:
+        raise ValueError(f"lexical shortlist has {len(data)} bytes; maximum is {maximum}")
+    if len(data) < 48:
+        raise ValueError("truncated lexical shortlist header")
+    magic, _, first_num, _, offset_count, target_count = struct.unpack_from("<6Q", data, 0)
+    if (magic != SHORTLIST_MAGIC or offset_count != source_vocab + 1 or first_num > target_vocab
+            or target_count > SHORTLIST_MAX_TARGET_ENTRIES):
+        raise ValueError("unsupported lexical shortlist format")
+    expected = 48 + offset_count * 8 + target_count * 4
+    if len(data) != expected:
+        raise ValueError(f"lexical shortlist has {len(data)} bytes, expected {expected}")
+    offsets = np.frombuffer(data, "<u8", offset_count, 48).astype(np.uint64)
+    if (offsets[0] != 0 or offsets[-1] != target_count or np.any(offsets[1:] < offsets[:-1])
+            or np.any(offsets > target_count)):
+        raise ValueError("lexical shortlist offsets are invalid")
+    targets = np.frombuffer(data, "<u4", target_count, 48 + offset_count * 8).astype(np.uint32)
+    bad = np.nonzero(targets >= target_vocab)[0]
+    if bad.size:
+        raise ValueError(f"lexical shortlist target {targets[bad[0]]} exceeds vocabulary {target_vocab}")
+    return int(first_num), offsets, targets
+
+
+def _shortlist_struct(parsed, keep):
+    if parsed is None:
+        return Shortlist(0, None, None)
+    first_num, offsets, targets = parsed
+    keep.extend([offsets, targets])
+    return Shortlist(first_num, offsets.ctypes.data, targets.ctypes.data)
+
+
+def shortlist_candidates(parsed, source_vocab, target_vocab, tokens):
+    """LexicalShortlist::candidates (shortlist.rs:150-198) for one sentence;
+    parsed is parse_shortlist's result or None (no shortlist file)."""
+    keep = []
+    sl = _shortlist_struct(parsed, keep)
+    t = np.ascontiguousarray(tokens, dtype=np.int32)
+    out = np.empty(max(1, target_vocab), dtype=np.uint32)
+    n = lib().oq_shortlist_candidates(C.byref(sl), source_vocab, target_vocab, _p(t), t.size, _p(out))
+    messages = {-1: "source token ID is negative", -2: "source token exceeds vocabulary",
+                -3: "lexical shortlist produced no candidates",
+                -4: "lexical shortlist does not contain EOS token 0"}
+    if n < 0:
+        raise ValueError(messages[n])
+    return out[:n].copy()
+
+
 def select_token(state, embedding, embedding_mult, activation_mult, output_bias, candidates):
     st = np.ascontiguousarray(state, dtype=np.float32)
     e = np.ascontiguousarray(embedding, dtype=np.int8)
@@ -217,7 +285,7 @@ def select_token(state, embedding, embedding_mult, activation_mult, output_bias,
 class OracleModel:
     """A parsed Marian binary v1 model bound to the oracle's C structs."""
 
-    def __init__(self, model_bytes: bytes, max_length_factor: int = 3):
+    def __init__(self, model_bytes: bytes, max_length_factor: int = 3, shortlist: bytes | None = None):
         t = mb.parse(model_bytes)
         self.tensors = t
         self._keep = []
@@ -263,6 +331,10 @@ class OracleModel:
                 self._attn(m.decoder_self[i], p + "_self")
             self._attn(m.decoder_context[i], p + "_context")
             self._ffn(m.decoder_ffn[i], p + "_ffn")
+        self.shortlist = None
+        if shortlist is not None:
+            self.shortlist = parse_shortlist(shortlist, m.source_vocab, m.target_vocab)
+        m.shortlist = _shortlist_struct(self.shortlist, self._keep)
         self.model = m
         self.dim = dim
         self.heads = heads

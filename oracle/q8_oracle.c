@@ -241,6 +241,46 @@ size_t oq_full_vocab_candidates(size_t target_vocab, uint32_t *out) {
     return count;  /* already ascending */
 }
 
+/* ---- marian-model/src/shortlist.rs:150-198 (with a shortlist file) ------- */
+static int cmp_u32(const void *a, const void *b) {
+    uint32_t x = *(const uint32_t *)a, y = *(const uint32_t *)b;
+    return x < y ? -1 : (x > y ? 1 : 0);
+}
+
+int64_t oq_shortlist_candidates(const oq_shortlist *sl, size_t source_vocab, size_t target_vocab,
+                                const int32_t *tokens, size_t n, uint32_t *out) {
+    unsigned char *present = (unsigned char *)malloc(target_vocab ? target_vocab : 1);
+    memset(present, sl->offsets ? 0 : 1, target_vocab);
+    if (sl->offsets) {
+        for (size_t i = 0; i < sl->first_num && i < target_vocab; ++i) present[i] = 1;
+        for (size_t i = 0; i < n; ++i) {
+            if (tokens[i] < 0) { free(present); return -1; }
+            size_t t = (size_t)tokens[i];
+            if (t >= source_vocab) { free(present); return -2; }
+            for (uint64_t j = sl->offsets[t]; j < sl->offsets[t + 1]; ++j) present[sl->targets[j]] = 1;
+        }
+    }
+    /* Marian's generation mask: UNK and the byte/control fallbacks */
+    if (target_vocab > 1) present[1] = 0;
+    if (target_vocab > 7) {
+        size_t end = target_vocab < 39 ? target_vocab : 39;
+        for (size_t i = 7; i < end; ++i) present[i] = 0;
+    }
+    size_t count = 0;
+    for (size_t i = 0; i < target_vocab; ++i)
+        if (present[i]) out[count++] = (uint32_t)i;
+    /* pad to a multiple of 8 with the first absent ids from 50 up */
+    for (size_t i = 50; i < target_vocab; ++i) {
+        if (count % 8 == 0) break;
+        if (!present[i]) out[count++] = (uint32_t)i;
+    }
+    free(present);
+    qsort(out, count, sizeof(uint32_t), cmp_u32);
+    if (count == 0) return -3;
+    if (out[0] != 0) return -4;
+    return (int64_t)count;
+}
+
 /* ---- q8_engine.rs:749-790 select_token ----------------------------------- */
 static int64_t select_token_impl(const float *state, size_t dim, const int8_t *embedding,
                                  float embedding_mult, float activation_mult,
@@ -340,6 +380,7 @@ int oq_translate(const oq_model *m, const float *positions,
                  int32_t *out_tokens, uint32_t *out_offsets, size_t out_capacity,
                  oq_trace *trace, char *err, size_t errcap) {
     const int dim = m->dim, heads = m->heads, ffn = m->ffn_dim;
+    if (err && errcap) err[0] = 0;
     /* validate_batch, q8_engine.rs:468-509 */
     if (batch == 0 || offsets[0] != 0) { set_err(err, errcap, "invalid packed batch offsets"); return -1; }
     if (batch > OQ_MAXIMUM_ENGINE_BATCH) {
@@ -405,9 +446,25 @@ int oq_translate(const oq_model *m, const float *positions,
         if (trace->cross_value) memcpy(trace->cross_value, cross_v, (size_t)L * rows * dim * sizeof(float));
     }
 
-    /* candidates: full vocabulary mask (shortlist.rs:150-198) */
-    uint32_t *cands = (uint32_t *)malloc((size_t)m->target_vocab * sizeof(uint32_t));
-    size_t n_cands = oq_full_vocab_candidates((size_t)m->target_vocab, cands);
+    /* prepare_candidates, q8_engine.rs:576-584: one list per sentence (the
+     * same full-vocabulary list for every row without a shortlist) */
+    const size_t tv = (size_t)m->target_vocab;
+    uint32_t *cands = (uint32_t *)malloc((m->shortlist.offsets ? batch : 1) * tv * sizeof(uint32_t));
+    size_t *n_cands = (size_t *)malloc(batch * sizeof(size_t));
+    if (!m->shortlist.offsets) {
+        size_t n0 = oq_full_vocab_candidates(tv, cands);
+        for (size_t b = 0; b < batch; ++b) n_cands[b] = n0;
+    } else {
+        for (size_t b = 0; b < batch && rc == 0; ++b) {
+            int64_t nc = oq_shortlist_candidates(&m->shortlist, (size_t)m->source_vocab, tv,
+                                                 tokens + offsets[b], offsets[b + 1] - offsets[b],
+                                                 cands + b * tv);
+            if (nc == -3) { set_err(err, errcap, "lexical shortlist produced no candidates"); rc = -1; }
+            else if (nc == -4) { set_err(err, errcap, "lexical shortlist does not contain EOS token 0"); rc = -1; }
+            else if (nc < 0) { set_err(err, errcap, "invalid source token for the lexical shortlist"); rc = -1; }
+            else n_cands[b] = (size_t)nc;
+        }
+    }
 
     /* limits, q8_engine.rs:369-379 */
     uint32_t *limits = (uint32_t *)malloc(batch * sizeof(uint32_t));
@@ -496,7 +553,8 @@ int oq_translate(const oq_model *m, const float *positions,
             int64_t tok = select_token_impl(dx + b * dim, dim, m->decoder_embedding,
                                             m->decoder_embedding_mult,
                                             m->decoder_output_activation_mult, m->output_bias,
-                                            cands, n_cands, mask_eos, &gap);
+                                            cands + (m->shortlist.offsets ? b * tv : 0), n_cands[b],
+                                            mask_eos, &gap);
             if (tok < 0) { rc = -2; break; }
             if (trace && trace->top2_gap) trace->top2_gap[b * OQ_MAXIMUM_GENERATION_STEPS + step] = gap;
             previous[b] = (int32_t)tok;
@@ -505,7 +563,8 @@ int oq_translate(const oq_model *m, const float *positions,
         }
     }
     if (rc != 0) {
-        set_err(err, errcap, "activation contains a non-finite value or the shape is invalid");
+        if (!err || !errcap || err[0] == 0)
+            set_err(err, errcap, "activation contains a non-finite value or the shape is invalid");
     } else {
         size_t pos = 0;
         out_offsets[0] = 0;
@@ -521,7 +580,7 @@ int oq_translate(const oq_model *m, const float *positions,
         }
     }
     free(lengths); free(padded); free(x); free(tmp); free(kbuf); free(vbuf);
-    free(cross_k); free(cross_v); free(cands); free(limits); free(states);
+    free(cross_k); free(cross_v); free(cands); free(n_cands); free(limits); free(states);
     free(self_k); free(self_v); free(previous); free(finished); free(generated);
     free(gen_count); free(dx); free(d1); free(d2); free(dq); free(self_len);
     return rc;

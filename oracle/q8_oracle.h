@@ -62,6 +62,16 @@ typedef struct {
     const float *ln_scale, *ln_bias;
 } oq_ssru_block;
 
+/* A parsed lexical shortlist (marian-model/src/shortlist.rs:56-148): source
+ * token t maps to targets[offsets[t] .. offsets[t + 1]); ids below
+ * first_num are always candidates.  offsets == NULL means no shortlist file
+ * (every id is a candidate, shortlist.rs:66-73). */
+typedef struct {
+    uint64_t first_num;
+    const uint64_t *offsets;   /* [source_vocab + 1] */
+    const uint32_t *targets;
+} oq_shortlist;
+
 typedef struct {
     int32_t dim, heads, ffn_dim;
     int32_t encoder_layers, decoder_layers, decoder_kind;
@@ -77,6 +87,7 @@ typedef struct {
     oq_attention_block decoder_self[OQ_MAX_LAYERS];
     oq_attention_block decoder_context[OQ_MAX_LAYERS];
     oq_ffn_block decoder_ffn[OQ_MAX_LAYERS];
+    oq_shortlist shortlist;  /* per-sentence candidates (q8_engine.rs:576-584) */
 } oq_model;
 
 /* Optional capture of intermediate activations for per-layer checks.
@@ -132,6 +143,13 @@ int oq_sinusoidal_positions(size_t dim, float *out);
 /* shortlist.rs:150-198 with no shortlist file: writes candidate ids in
  * ascending order, returns the count. */
 size_t oq_full_vocab_candidates(size_t target_vocab, uint32_t *out);
+
+/* shortlist.rs:150-198 LexicalShortlist::candidates for one sentence:
+ * writes the ascending candidate ids to out (capacity target_vocab) and
+ * returns their count, or -1 for a negative token, -2 for a token beyond
+ * the source vocabulary, -3 for no candidates, -4 when EOS (0) is missing. */
+int64_t oq_shortlist_candidates(const oq_shortlist *sl, size_t source_vocab, size_t target_vocab,
+                                const int32_t *tokens, size_t n, uint32_t *out);
 
 /* q8_engine.rs:749-790 */
 int64_t oq_select_token(const float *state, size_t dim, const int8_t *embedding,

@@ -14,7 +14,7 @@ torch = pytest.importorskip("torch")
 
 import oracle as O  # noqa: E402
 from marian_cuda import workloads as W  # noqa: E402
-from marian_cuda._lib import MC_INVALID_INPUT, MarianCudaError  # noqa: E402
+from marian_cuda._lib import MC_INFERENCE, MC_INVALID_INPUT, MC_MODEL, MarianCudaError  # noqa: E402
 from marian_cuda.backend import CudaEngine  # noqa: E402
 
 NEAR_TIE = 1e-3
@@ -311,3 +311,56 @@ def test_streaming_with_lanes_matches_static_batch():
     assert sorted(results) == list(range(batch.size))
     for b in range(batch.size):
         np.testing.assert_array_equal(results[b], ref[ref_off[b]:ref_off[b + 1]])
+
+
+@pytest.mark.parametrize("name,first_num,per_token", [("tiny_self", 16, 8), ("tiny_ssru", 0, 12),
+                                                       ("graph_b", 100, 40)])
+def test_lexical_shortlist_matches_oracle(name, first_num, per_token):
+    # Each sentence picks its tokens among its own shortlist candidates
+    # (shortlist.rs:150-198); the device-built candidate masks and the
+    # masked argmax must give the oracle's tokens exactly, with slots reused
+    # by later sentences and for several lanes.
+    shape = W.SHAPES[name]
+    raw = W.synthetic_shortlist(shape.vocab, shape.vocab, seed=3, first_num=first_num,
+                                max_per_token=per_token)
+    if first_num == 0:  # EOS must be a candidate: let every source id map to it
+        first, offs, tg = O.parse_shortlist(raw, shape.vocab, shape.vocab)
+        per = [np.append(tg[offs[i]:offs[i + 1]], 0) for i in range(shape.vocab)]
+        raw = W.shortlist_bytes(0, np.concatenate([[0], np.cumsum([len(p) for p in per])]),
+                                np.concatenate(per))
+    batch = W.short_batch(n=24, vocab=shape.vocab, seed=19, lo=4, hi=30)
+    om = O.OracleModel(model(name), shortlist=raw)
+    ref, ref_off = om.translate(batch.tokens, batch.offsets, batch.max_out, batch.force_len)
+    full, _ = O.OracleModel(model(name)).translate(batch.tokens, batch.offsets, batch.max_out,
+                                                   batch.force_len)
+    for lanes in (1, 2):
+        with CudaEngine(model(name), max_inflight=10, max_encode_tokens=2048, lanes=lanes,
+                        shortlist=raw) as eng:
+            for _ in range(2):
+                got, got_off = eng.translate_token_ids(batch.tokens, batch.offsets, batch.max_out,
+                                                       batch.force_len)
+                np.testing.assert_array_equal(got_off, ref_off)
+                np.testing.assert_array_equal(got, ref)
+    assert not np.array_equal(ref, full)  # the shortlist changed the outputs
+
+
+def test_lexical_shortlist_errors_follow_the_reference():
+    name = "tiny_self"
+    with CudaEngine(model(name), max_inflight=8, max_encode_tokens=1024) as eng:
+        lib = eng._lib
+        bad = W.shortlist_bytes(0, [0] * (W.SHAPES[name].vocab + 2), [])  # wrong offset count
+        assert lib.mc_load_shortlist(eng.handle, bad, len(bad)) == MC_MODEL
+        # no EOS among the candidates of a sentence: rejected as the reference does
+        n = W.SHAPES[name].vocab
+        raw = W.shortlist_bytes(0, list(range(n + 1)), [5] * n)
+        assert lib.mc_load_shortlist(eng.handle, raw, len(raw)) == 0
+        with pytest.raises(MarianCudaError) as ei:
+            eng.translate_token_ids(np.array([4, 0], np.int32), np.array([0, 2], np.uint32),
+                                    np.array([4], np.uint32))
+        assert ei.value.status == MC_INFERENCE
+        assert eng.is_ready()
+        # back to the full vocabulary
+        assert lib.mc_load_shortlist(eng.handle, None, 0) == 0
+        out, off = eng.translate_token_ids(np.array([4, 0], np.int32), np.array([0, 2], np.uint32),
+                                           np.array([4], np.uint32))
+        assert off[-1] >= 1

@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 
 import oracle as O
+from marian_cuda import workloads as W
 
 
 def test_quantization_ties_to_even_and_saturation():
@@ -138,3 +139,55 @@ def test_full_vocabulary_masks_control_tokens():
     assert 0 in c and 63 in c
     # 32000-token vocabulary: everything but 1 and 7..38
     assert len(O.full_vocab_candidates(32000)) == 32000 - 1 - 32
+
+
+# ---- lexical shortlist (marian-model/src/shortlist.rs) ------------------------
+
+def test_shortlist_full_vocabulary_masks_control_tokens():
+    # shortlist.rs:259-266: no file, 64-id vocabulary, sentence [0, 63]
+    c = O.shortlist_candidates(None, 64, 64, [0, 63])
+    assert 1 not in c and not any(i in c for i in range(7, 39))
+    assert 0 in c and 63 in c
+
+
+def test_shortlist_must_supply_eos():
+    # shortlist.rs:268-277: firstNum 0, source id 0 -> target 2 only
+    sl = O.parse_shortlist(W.shortlist_bytes(0, [0, 1], [2]), 1, 64)
+    with pytest.raises(ValueError, match="lexical shortlist does not contain EOS token 0"):
+        O.shortlist_candidates(sl, 1, 64, [0])
+
+
+def test_shortlist_entry_count_is_bounded():
+    # shortlist.rs:279-291: a target count of MAX_TARGET_ENTRIES + 1 is rejected
+    b = bytearray(W.shortlist_bytes(0, [0, 0], []))
+    b[40:48] = (O.SHORTLIST_MAX_TARGET_ENTRIES + 1).to_bytes(8, "little")
+    with pytest.raises(ValueError):
+        O.parse_shortlist(bytes(b), 1, 64)
+
+
+def test_shortlist_candidates_are_padded_to_multiples_of_eight():
+    # shortlist.rs:185-192: 3 candidates {0, 2, 3} gain the first 5 absent ids from 50
+    sl = O.parse_shortlist(W.shortlist_bytes(0, [0, 3], [0, 2, 3]), 1, 64)
+    assert O.shortlist_candidates(sl, 1, 64, [0]).tolist() == [0, 2, 3, 50, 51, 52, 53, 54]
+    # firstNum 10 marks 0..9; 1 and 7..9 are masked, 40 and 60 come from the token
+    sl = O.parse_shortlist(W.shortlist_bytes(10, [0, 0, 2], [40, 60]), 2, 64)
+    assert O.shortlist_candidates(sl, 2, 64, [1, 0]).tolist() == [0, 2, 3, 4, 5, 6, 40, 60]
+
+
+def test_shortlist_parser_rejects_malformed_files():
+    good = W.shortlist_bytes(0, [0, 1, 2], [0, 5])
+    O.parse_shortlist(good, 2, 64)
+    for bad, msg in ((good[:40], "truncated"), (good + b"\0", "expected"),
+                     (W.shortlist_bytes(0, [0, 2, 1], [0, 5]), "offsets are invalid"),
+                     (W.shortlist_bytes(0, [0, 1, 2], [0, 64]), "exceeds vocabulary"),
+                     (W.shortlist_bytes(65, [0, 1, 2], [0, 5]), "unsupported")):
+        with pytest.raises(ValueError, match=msg):
+            O.parse_shortlist(bad, 2, 64)
+
+
+def test_synthetic_shortlist_round_trips():
+    raw = W.synthetic_shortlist(300, 512, seed=4, first_num=16, max_per_token=8)
+    first, offs, tg = O.parse_shortlist(raw, 300, 512)
+    assert first == 16 and offs.size == 301 and tg.size == int(offs[-1])
+    c = O.shortlist_candidates((first, offs, tg), 300, 512, [5, 17, 0])
+    assert c[0] == 0 and c.size % 8 == 0 and np.all(np.diff(c.astype(np.int64)) > 0)
