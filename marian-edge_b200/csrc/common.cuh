@@ -31,11 +31,15 @@ __device__ __forceinline__ void flag_status(uint32_t* status, uint32_t bits) {
 }
 
 // ---- programmatic dependent launch ------------------------------------------
-// Every engine kernel is launched with programmatic stream serialization: it
+// Every engine kernel is written for programmatic stream serialization: it
 // may start while its predecessor on the stream is still running, waits in
 // pdl_wait() until that grid has completed and its writes are visible, and
 // then lets its own successor begin launching.  Nothing touches global memory
-// written or read by other kernels before pdl_wait().
+// written or read by other kernels before pdl_wait().  Whether launches ask
+// for it is kProgrammaticLaunch (below): on the benchmark stream the early
+// CTAs of a waiting kernel hold shared memory and TMEM that the concurrent
+// encoder-stream kernels could use, and end to end it measured 4-5% slower,
+// so it is off; without the attribute griddepcontrol.wait returns at once.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -223,6 +227,8 @@ __device__ __forceinline__ float dequant(int32_t acc, float scale, float bias) {
   return __fadd_rn(__fmul_rn(__int2float_rn(acc), scale), bias);
 }
 
+constexpr bool kProgrammaticLaunch = false;
+
 #ifdef __CUDACC__
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
@@ -234,7 +240,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = kProgrammaticLaunch ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
