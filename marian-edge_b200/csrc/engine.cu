@@ -818,6 +818,8 @@ mc_status allocate_buffers(mc_engine* e) {
 
   const int n_lanes = std::max(1, std::min<int>(e->cfg.lanes ? (int)e->cfg.lanes : 1, std::min(kMaxLanes, R)));
   e->lanes.resize(n_lanes);
+  int prio_low = 0, prio_high = 0;
+  CK(cudaDeviceGetStreamPriorityRange(&prio_low, &prio_high));
   for (int i = 0; i < n_lanes; ++i) {
     Lane& L = e->lanes[i];
     L.id = i;
@@ -825,10 +827,10 @@ mc_status allocate_buffers(mc_engine* e) {
     if (i == 0) {
       L.stream = e->stream;
     } else {
-      CK(cudaStreamCreateWithFlags(&L.stream, cudaStreamNonBlocking));
+      CK(cudaStreamCreateWithPriority(&L.stream, cudaStreamNonBlocking, prio_high));
       L.own_stream = true;
     }
-    CK(cudaStreamCreateWithFlags(&L.enc_stream, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithPriority(&L.enc_stream, cudaStreamNonBlocking, prio_low));
     CK(cudaEventCreateWithFlags(&L.enc_done, cudaEventDisableTiming));
     L.cur = L.stream;
     mc_status st = allocate_lane(e, L);
@@ -1259,7 +1261,11 @@ extern "C" mc_status mc_create(const mc_config* cfg, mc_engine** out) {
   e->cfg = *cfg;
   mc_status st = set_device(e);
   if (st == MC_OK) {
-    cudaError_t r = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+    int lowest = 0, highest = 0;
+    cudaError_t r = cudaDeviceGetStreamPriorityRange(&lowest, &highest);
+    // decode steps are the latency chain: their streams get the highest
+    // priority, encoder passes fill in at the lowest
+    if (r == cudaSuccess) r = cudaStreamCreateWithPriority(&e->stream, cudaStreamNonBlocking, highest);
     if (r != cudaSuccess) st = MC_CUDA;
   }
   if (st != MC_OK) {
