@@ -412,15 +412,44 @@ __global__ void __launch_bounds__(kLnWarps * 32) ssru_warp_kernel(
 // weighted sum of V per output dimension.  The host launches one grid per
 // length bucket so shared memory follows the bucket's longest sequence.
 constexpr int kEncWarps = 8;
-constexpr int kEncQpw = 4;  // queries per warp
+constexpr int kEncQpw = 4;  // queries per warp, advanced in two pairs
+
+// Packed f32x2 arithmetic (sm_100): each half is one IEEE f32 operation
+// rounded to nearest, exactly as the scalar instruction, so pairing two
+// independent sums changes no result while halving the issued instructions.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(unsigned long long v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return make_float2(lo, hi);
+}
+// acc + a * b with two roundings per half (the reference's `acc += a * b`;
+// never a fused multiply-add).  ptxas contracts mul.rn.f32x2 followed by
+// add.rn.f32x2 into one fused f32x2 multiply-add despite the explicit
+// rounding modifiers (and --fmad=false), so the sum is issued as
+// fma(prod, ones, acc): prod * 1 is exact, leaving the single rounding of
+// prod + acc.  `ones` must be a runtime value (a kernel argument) so that
+// the multiply by 1 cannot be folded back into an add.
+__device__ __forceinline__ unsigned long long f2_mul_add(unsigned long long acc, unsigned long long a,
+                                                         unsigned long long b,
+                                                         unsigned long long ones) {
+  unsigned long long prod, r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(prod) : "l"(a), "l"(b));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(prod), "l"(ones), "l"(acc));
+  return r;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
     const float* __restrict__ qkv, const int32_t* __restrict__ cu,
     const int32_t* __restrict__ seq_ids, int d, int max_len, int8_t* __restrict__ out_q,
-    float alpha, uint32_t* status) {
+    float alpha, float one, uint32_t* status) {
   pdl_enter();
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   const int b = seq_ids[blockIdx.x];
   const int h = blockIdx.y;
   const int start = cu[b];
@@ -435,8 +464,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
   constexpr int KLD = HD + 4;
   float* ks = sm;                                          // [max_len][HD + 4]
   float* vs = ks + (size_t)max_len * KLD;                   // [max_len][HD]
-  float* qs = vs + (size_t)max_len * HD;                   // [warps][4][HD]
-  float* ps = qs + kEncWarps * kEncQpw * HD;               // [warps][4][max_len]
+  float* qs = vs + (size_t)max_len * HD;                   // [warps][2 pairs][HD][2]
+  float* ps = qs + kEncWarps * kEncQpw * HD;               // [warps][2 pairs][max_len][2]
   constexpr int kVec = HD / 4;
   for (int idx = threadIdx.x; idx < len * kVec; idx += blockDim.x) {
     const int j = idx / kVec, i = (idx % kVec) * 4;
@@ -447,42 +476,49 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qb = q0 + warp * kEncQpw;                      // this warp's first query
   const int nq = max(0, min(kEncQpw, len - qb));
+  // queries 2p and 2p + 1 interleaved: qw[p][i] = (q_2p[i], q_2p+1[i])
   float* qw = qs + warp * kEncQpw * HD;
   float* pw = ps + warp * kEncQpw * max_len;
   for (int idx = lane; idx < kEncQpw * HD; idx += 32) {
     const int qq = idx / HD, i = idx % HD;
-    qw[idx] = qq < nq ? qkv[(size_t)(start + qb + qq) * ld + h * HD + i] : 0.0f;
+    qw[(qq >> 1) * 2 * HD + 2 * i + (qq & 1)] =
+        qq < nq ? qkv[(size_t)(start + qb + qq) * ld + h * HD + i] : 0.0f;
   }
   __syncthreads();
   if (nq == 0) return;
+  auto pidx = [&](int qq, int j) { return (qq >> 1) * 2 * max_len + 2 * j + (qq & 1); };
   const float scale = 1.0f / sqrtf((float)HD);
+  const unsigned long long ones = f2_pack(one, one);
   float mx[kEncQpw];
 #pragma unroll
   for (int qq = 0; qq < kEncQpw; ++qq) mx[qq] = -INFINITY;
   for (int j = lane; j < len; j += 32) {
     const float* kr = ks + j * KLD;
-    float dot[kEncQpw];
-#pragma unroll
-    for (int qq = 0; qq < kEncQpw; ++qq) dot[qq] = 0.0f;
+    unsigned long long dot[2] = {0ull, 0ull};  // (+0, +0)
 #pragma unroll
     for (int i = 0; i < HD; i += 4) {
       const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
+      const unsigned long long kx = f2_pack(k4.x, k4.x), ky = f2_pack(k4.y, k4.y),
+                               kz = f2_pack(k4.z, k4.z), kw = f2_pack(k4.w, k4.w);
 #pragma unroll
-      for (int qq = 0; qq < kEncQpw; ++qq) {
-        const float4 q4 = *reinterpret_cast<const float4*>(qw + qq * HD + i);
-        float t = dot[qq];
-        t = t + q4.x * k4.x;
-        t = t + q4.y * k4.y;
-        t = t + q4.z * k4.z;
-        t = t + q4.w * k4.w;
-        dot[qq] = t;
+      for (int p = 0; p < 2; ++p) {
+        const float4 qa = *reinterpret_cast<const float4*>(qw + p * 2 * HD + 2 * i);
+        const float4 qc = *reinterpret_cast<const float4*>(qw + p * 2 * HD + 2 * i + 4);
+        unsigned long long t = dot[p];
+        t = f2_mul_add(t, f2_pack(qa.x, qa.y), kx, ones);
+        t = f2_mul_add(t, f2_pack(qa.z, qa.w), ky, ones);
+        t = f2_mul_add(t, f2_pack(qc.x, qc.y), kz, ones);
+        t = f2_mul_add(t, f2_pack(qc.z, qc.w), kw, ones);
+        dot[p] = t;
       }
     }
 #pragma unroll
-    for (int qq = 0; qq < kEncQpw; ++qq) {
-      const float sc = dot[qq] * scale;
-      pw[qq * max_len + j] = sc;
-      mx[qq] = fmaxf(mx[qq], sc);
+    for (int p = 0; p < 2; ++p) {
+      const float2 dd = f2_unpack(dot[p]);
+      const float s0 = dd.x * scale, s1 = dd.y * scale;
+      *reinterpret_cast<float2*>(pw + pidx(2 * p, j)) = make_float2(s0, s1);
+      mx[2 * p] = fmaxf(mx[2 * p], s0);
+      mx[2 * p + 1] = fmaxf(mx[2 * p + 1], s1);
     }
   }
 #pragma unroll
@@ -490,15 +526,14 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
     for (int o = 16; o > 0; o >>= 1) mx[qq] = fmaxf(mx[qq], __shfl_xor_sync(0xffffffffu, mx[qq], o));
   for (int j = lane; j < len; j += 32) {
 #pragma unroll
-    for (int qq = 0; qq < kEncQpw; ++qq) pw[qq * max_len + j] = exp_f32(pw[qq * max_len + j] - mx[qq]);
+    for (int qq = 0; qq < kEncQpw; ++qq) pw[pidx(qq, j)] = exp_f32(pw[pidx(qq, j)] - mx[qq]);
   }
   __syncwarp();
   float inv_mine = 0.0f;
   if (lane < kEncQpw) {  // lane qq sums query qq's exponentials in key order
-    const float* pr = pw + lane * max_len;
     float sum = 0.0f;
 #pragma unroll 8
-    for (int j = 0; j < len; ++j) sum = sum + pr[j];
+    for (int j = 0; j < len; ++j) sum = sum + pw[pidx(lane, j)];
     inv_mine = 1.0f / sum;
   }
   float inv[kEncQpw];
@@ -506,33 +541,39 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
   for (int qq = 0; qq < kEncQpw; ++qq) inv[qq] = __shfl_sync(0xffffffffu, inv_mine, qq);
   for (int j = lane; j < len; j += 32) {
 #pragma unroll
-    for (int qq = 0; qq < kEncQpw; ++qq) pw[qq * max_len + j] = pw[qq * max_len + j] * inv[qq];
+    for (int qq = 0; qq < kEncQpw; ++qq) pw[pidx(qq, j)] = pw[pidx(qq, j)] * inv[qq];
   }
   __syncwarp();
-  // lane owns output dims 2*lane and 2*lane + 1 of each of the 4 queries
+  // lane owns output dims 2*lane and 2*lane + 1 of each of the 4 queries;
+  // acc[p][c] holds dim c of queries 2p and 2p + 1
   const bool active = 2 * lane < HD;
-  float acc[kEncQpw][2];
-#pragma unroll
-  for (int qq = 0; qq < kEncQpw; ++qq) acc[qq][0] = acc[qq][1] = 0.0f;
+  unsigned long long acc[2][2] = {{0ull, 0ull}, {0ull, 0ull}};
 #pragma unroll 4
   for (int j = 0; j < len; ++j) {
     const float2 v2 = active ? *reinterpret_cast<const float2*>(vs + j * HD + 2 * lane)
                              : make_float2(0.f, 0.f);
+    const unsigned long long vx = f2_pack(v2.x, v2.x), vy = f2_pack(v2.y, v2.y);
 #pragma unroll
-    for (int qq = 0; qq < kEncQpw; ++qq) {
-      const float p = pw[qq * max_len + j];
-      acc[qq][0] = acc[qq][0] + v2.x * p;
-      acc[qq][1] = acc[qq][1] + v2.y * p;
+    for (int p = 0; p < 2; ++p) {
+      const unsigned long long pp = *reinterpret_cast<const unsigned long long*>(pw + pidx(2 * p, j));
+      acc[p][0] = f2_mul_add(acc[p][0], pp, vx, ones);
+      acc[p][1] = f2_mul_add(acc[p][1], pp, vy, ones);
     }
   }
   if (active) {
 #pragma unroll
-    for (int qq = 0; qq < kEncQpw; ++qq) {
-      if (qq < nq) {
-        int8_t* o = out_q + (size_t)(start + qb + qq) * d + h * HD + 2 * lane;
-        const uint16_t w2 = (uint16_t)(uint8_t)quantize_one(acc[qq][0], alpha, status) |
-                            ((uint16_t)(uint8_t)quantize_one(acc[qq][1], alpha, status) << 8);
-        *reinterpret_cast<uint16_t*>(o) = w2;
+    for (int p = 0; p < 2; ++p) {
+      const float2 c0 = f2_unpack(acc[p][0]), c1 = f2_unpack(acc[p][1]);
+      const float dims[2][2] = {{c0.x, c1.x}, {c0.y, c1.y}};  // [query in pair][dim]
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int qq = 2 * p + u;
+        if (qq < nq) {
+          int8_t* o = out_q + (size_t)(start + qb + qq) * d + h * HD + 2 * lane;
+          const uint16_t w2 = (uint16_t)(uint8_t)quantize_one(dims[u][0], alpha, status) |
+                              ((uint16_t)(uint8_t)quantize_one(dims[u][1], alpha, status) << 8);
+          *reinterpret_cast<uint16_t*>(o) = w2;
+        }
       }
     }
   }
@@ -999,7 +1040,7 @@ cudaError_t launch_attn_encoder_hd(const float* qkv, const int32_t* cu_seqlens,
   }
   const int chunks = (max_len + 31) / 32;
   launch_pdl(attn_encoder_kernel<HD>, dim3(dim3(n_seqs, heads, chunks)), dim3(kEncWarps * 32), smem, s, qkv, cu_seqlens, seq_ids, d,
-                                                                        max_len, out_q, alpha, status);
+                                                                        max_len, out_q, alpha, 1.0f, status);
   return cudaGetLastError();
 }
 
