@@ -288,12 +288,12 @@ __device__ __forceinline__ float serial_sum(const float* row) {
 
 // x[k] (this lane's chunks, columns 4 * (lane + 32 k)) hold the pre-norm row;
 // row is the warp's shared-memory row buffer.  Writes out and the quantized
-// copies of global row `grow`.
+// copies of global row `grow` when `store` (warp-uniform) is set.
 template <int VPL>
 __device__ __forceinline__ void ln_row(float4 (&x)[VPL], float* row, int grow,
                                        const float* __restrict__ gamma,
                                        const float* __restrict__ beta, float* __restrict__ out,
-                                       const QuantOut& q, uint32_t* status) {
+                                       const QuantOut& q, uint32_t* status, bool store = true) {
   constexpr int d = VPL * 128;
   const int lane = threadIdx.x & 31;
   float4* r4 = reinterpret_cast<float4*>(row);
@@ -330,9 +330,11 @@ __device__ __forceinline__ void ln_row(float4 (&x)[VPL], float* row, int grow,
     v.y = c[k].y * inv * g.y + b.y;
     v.z = c[k].z * inv * g.z + b.z;
     v.w = c[k].w * inv * g.w + b.w;
-    const long long elem = (long long)grow * d + col;
-    *reinterpret_cast<float4*>(out + elem) = v;
-    store_quant4(q, elem, v.x, v.y, v.z, v.w, status);
+    if (store) {
+      const long long elem = (long long)grow * d + col;
+      *reinterpret_cast<float4*>(out + elem) = v;
+      store_quant4(q, elem, v.x, v.y, v.z, v.w, status);
+    }
   }
 }
 
@@ -345,10 +347,13 @@ __global__ void __launch_bounds__(kLnWarps * 32) residual_ln_warp_kernel(
   constexpr int d = VPL * 128;
   __shared__ __align__(16) float rows_s[kLnWarps][d];
   pdl_enter();
-  const int rows = launch_rows(rows_dev, cap);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kLnWarps + warp;
-  if (row >= rows) return;
+  if (row >= cap) return;
+  // The row is loaded together with the device row count, so the two loads'
+  // latencies overlap: a row past the count (inside the buffers' cap rows)
+  // is normalized like the others and not stored.
+  const int rows = launch_rows(rows_dev, cap);
   float4 x[VPL];
 #pragma unroll
   for (int k = 0; k < VPL; ++k) {
@@ -357,7 +362,7 @@ __global__ void __launch_bounds__(kLnWarps * 32) residual_ln_warp_kernel(
     const float4 w = *reinterpret_cast<const float4*>(r + (size_t)row * ldr + col);
     x[k] = make_float4(u.x + w.x, u.y + w.y, u.z + w.z, u.w + w.w);
   }
-  ln_row<VPL>(x, rows_s[warp], row, gamma, beta, out, q, status);
+  ln_row<VPL>(x, rows_s[warp], row, gamma, beta, out, q, status, row < rows);
 }
 
 // SSRU (tensor.rs:184-218) with the warp-per-row LayerNorm above.

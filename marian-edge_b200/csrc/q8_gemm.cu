@@ -290,6 +290,10 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
   const int lane = threadIdx.x & 31;
   const int num_kb = (p.k + kBK - 1) / kBK;
   const int n_tiles = (p.max_n + BN - 1) / BN;
+  pdl_enter();
+  // The device row count is loaded before the set-up and used after it, so
+  // its latency overlaps the barrier initialization and TMEM allocation.
+  const int m_raw = p.m_dev ? *p.m_dev : p.m;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -314,8 +318,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_s;
-  pdl_enter();  // set-up above overlaps the previous kernel's tail
-  const int m = p.m_dev ? max(0, min(*p.m_dev, p.m)) : p.m;
+  const int m = max(0, min(m_raw, p.m));
   const int m_tiles = (m + kBM - 1) / kBM;
   const int total = n_tiles * m_tiles * p.num_groups;
 
@@ -379,20 +382,27 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
       if (!tile_coord<BN>(p, t, n_tiles, m_tiles, &c)) continue;
       const GemmGroup& g = p.g[c.z];
       const int buf = it & 1;
-      // Warp-uniform: tcgen05.ld below is .sync.aligned.
-      const bool ready = __all_sync(0xffffffffu, mbar_wait(&tfull_bar[buf], (it >> 1) & 1, p.status));
-      if (!ready) break;
-      tc_fence_after();
+      constexpr int kShare = BN / (EPI / 4) >= 32 ? BN / (EPI / 4) : 32;
+      // The per-row operands are loaded, and the first chunk's bias line is
+      // prefetched into L1, before the accumulator is ready, so their
+      // latency overlaps the MMAs.
       const int row = c.m0 + quarter * 32 + lane;
       const bool row_ok = row < m;
       const int dest_row = row_ok ? (g.row_map ? g.row_map[row] : row) : 0;
       const float row_scale = (row_ok && g.row_scale) ? g.row_scale[row] : 1.0f;
+      const int c_first = part * kShare;
+      const int nb_first = c.n0 + c_first;
+      if (lane == 0 && g.bias != nullptr && g.mode != kEpiI32 && nb_first < g.n)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(g.bias + nb_first));
+      // Warp-uniform: tcgen05.ld below is .sync.aligned.
+      const bool ready = __all_sync(0xffffffffu, mbar_wait(&tfull_bar[buf], (it >> 1) & 1, p.status));
+      if (!ready) break;
+      tc_fence_after();
       float best = -INFINITY;
       int best_n = -1;
       const uint32_t lane_base = tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
-      constexpr int kShare = BN / (EPI / 4) >= 32 ? BN / (EPI / 4) : 32;
 #pragma unroll 1
-      for (int c0 = part * kShare; c0 < BN && c0 < (part + 1) * kShare; c0 += 32) {
+      for (int c0 = c_first; c0 < BN && c0 < (part + 1) * kShare; c0 += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(lane_base + c0, r);
         tmem_ld_wait();
