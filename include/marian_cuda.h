@@ -235,6 +235,55 @@ mc_status mc_q8_linear_noalloc(const float *x, int32_t m, int32_t k, const int8_
  * current device (non-finite quantizer input, wait timeout); synchronizes. */
 mc_status mc_op_status(uint32_t *status_bits);
 
+/* ---- long-text splitting ----------------------------------------------------
+ * Replaces marian_core::segment_text (crates/marian-core/src/segmenter.rs:
+ * 122-197), which the reference's backends call before tokenizing a request
+ * (crates/marian-cpu/src/backend.rs:132-135).  Host-only; no engine needed. */
+
+/* One range of the input: content[start, end) to translate, followed by
+ * separator[start, end) to copy to the output verbatim (segmenter.rs:26-46).
+ * The ranges of all segments partition the input in order. */
+typedef struct {
+    uint64_t content_start, content_end;
+    uint64_t separator_start, separator_end;
+    uint64_t source_pieces;   /* the counter's value for the content */
+} mc_text_segment;
+
+/* SegmentError (segmenter.rs:48-72) plus the two failures only a C caller
+ * can cause. */
+typedef enum {
+    MC_SEGMENT_OK = 0,
+    MC_SEGMENT_ZERO_PIECE_LIMIT = 1,
+    MC_SEGMENT_INPUT_TOO_LARGE = 2,       /* end: input bytes; maximum: 4 MiB */
+    MC_SEGMENT_ENCODING = 3,              /* start, end: the range the counter failed on */
+    MC_SEGMENT_ENCODING_WORK_LIMIT = 4,   /* maximum: the exceeded limit */
+    MC_SEGMENT_TOO_MANY_SEGMENTS = 5,     /* maximum: 4096 */
+    MC_SEGMENT_UNSPLITABLE_SCALAR = 6,    /* start, end, pieces, maximum */
+    MC_SEGMENT_INVALID_UTF8 = 7,          /* a Rust &str cannot hold such bytes */
+    MC_SEGMENT_INVALID_ARGUMENT = 8       /* null pointers, or capacity too small */
+} mc_segment_error_kind;
+
+typedef struct {
+    int32_t kind;              /* mc_segment_error_kind */
+    uint64_t start, end, pieces, maximum;
+    char message[256];         /* the reference's Display text (segmenter.rs:74-110) */
+} mc_segment_error;
+
+/* The caller's exact source-piece counter for text[0, len) (the closure of
+ * segment_text).  Returns 0 and sets *pieces, or non-zero with a message
+ * (NUL-terminated, at most message_capacity bytes) on a tokenizer failure. */
+typedef int32_t (*mc_piece_count_fn)(void *ctx, const char *text, size_t len, uint64_t *pieces,
+                                     char *message, size_t message_capacity);
+
+/* Splits text (UTF-8, len bytes) into segments whose content fits
+ * max_pieces.  Writes *n_segments (at most 4096) and, when they fit
+ * capacity, the segments.  Every failure returns MC_INVALID_INPUT (the
+ * reference backend's BackendError::InvalidInput) and fills *error when
+ * given; on success error->kind is MC_SEGMENT_OK. */
+mc_status mc_segment_text(const char *text, size_t len, uint64_t max_pieces,
+                          mc_piece_count_fn count_pieces, void *ctx, mc_text_segment *segments,
+                          size_t capacity, size_t *n_segments, mc_segment_error *error);
+
 #ifdef __cplusplus
 }
 #endif

@@ -19,6 +19,7 @@ EXPORTS = [
     "mc_last_error", "mc_is_ready", "mc_translate_token_ids", "mc_submit", "mc_step", "mc_poll",
     "mc_trace_first_step", "mc_stream", "mc_q8_gemm", "mc_op_status", "mc_profile",
     "mc_profile_read", "mc_launch_count", "mc_q8_linear", "mc_q8_linear_noalloc", "mc_load_shortlist",
+    "mc_segment_text",
 ]
 
 # MC_Q8_LINEAR_NOALLOC_MAX_ACTIVATIONS in include/marian_cuda.h
@@ -32,6 +33,22 @@ class Config(C.Structure):
     _fields_ = [("device", C.c_int32), ("max_inflight", C.c_uint32), ("max_encode_tokens", C.c_uint32),
                 ("page_tokens", C.c_uint32), ("kv_pages", C.c_uint32), ("max_length_factor", C.c_uint32),
                 ("lanes", C.c_uint32)]
+
+
+class TextSegment(C.Structure):
+    _fields_ = [("content_start", C.c_uint64), ("content_end", C.c_uint64),
+                ("separator_start", C.c_uint64), ("separator_end", C.c_uint64),
+                ("source_pieces", C.c_uint64)]
+
+
+class SegmentError(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("start", C.c_uint64), ("end", C.c_uint64),
+                ("pieces", C.c_uint64), ("maximum", C.c_uint64), ("message", C.c_char * 256)]
+
+
+# mc_piece_count_fn
+PIECE_COUNT_FN = C.CFUNCTYPE(C.c_int32, C.c_void_p, C.POINTER(C.c_char), C.c_size_t,
+                             C.POINTER(C.c_uint64), C.POINTER(C.c_char), C.c_size_t)
 
 
 class ModelInfo(C.Structure):
@@ -91,6 +108,8 @@ def load(build_if_missing: bool = True):
     lib.mc_profile_read.argtypes = [vp, i32, C.POINTER(u64), C.POINTER(C.c_double),
                                     C.POINTER(C.c_double), C.POINTER(C.c_double)]
     lib.mc_load_shortlist.argtypes = [vp, C.c_char_p, sz]
+    lib.mc_segment_text.argtypes = [C.c_char_p, sz, u64, PIECE_COUNT_FN, vp, C.POINTER(TextSegment), sz,
+                                    C.POINTER(sz), C.POINTER(SegmentError)]
     lib.mc_launch_count.argtypes = [vp]
     lib.mc_launch_count.restype = u64
     _lib = lib

@@ -6,8 +6,12 @@
   ``BatchOutput`` (``engine.rs:82``), plus the streaming calls of the device
   continuous batcher (``submit`` / ``step`` / ``poll``).
 * :class:`CudaBackend` is the ``TranslationBackend`` contract
-  (``crates/marian-core/src/backend.rs:7-38``) for callers that already hold
-  token ids: ``info()``, ``is_ready()``, ``translate_batch``.
+  (``crates/marian-core/src/backend.rs:7-38``): ``info()``, ``is_ready()``,
+  ``translate_batch`` over token ids, and -- given the caller's source and
+  target tokenizers -- ``translate`` over text, which splits long inputs
+  (``segment_text``) and shares each input's output budget across its
+  segments exactly as the reference's CPU backend does
+  (``crates/marian-cpu/src/backend.rs:107-346``, :func:`translate_texts`).
 
 Errors map to the reference's ``BackendError`` kinds
 (``marian-core/src/types.rs:61-70``) through :class:`MarianCudaError.status`.
@@ -21,6 +25,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib as L
+from . import segmenter as _seg
 
 
 def _ptr(a):
@@ -144,11 +149,154 @@ class CudaEngine:
         return {"encoder_output": enc, "cross_key": ck, "cross_value": cv, "decoder_state_step0": st}
 
 
-class CudaBackend:
-    """TranslationBackend over token ids (the tokenizer stays with the caller)."""
+# ---- text translation (crates/marian-cpu/src/backend.rs:107-346) ------------
+MAXIMUM_SOURCE_TOKENS = 256          # marian-cpu/src/limits.rs:3
+MAXIMUM_TRANSLATION_SEGMENTS = 4096  # marian-cpu/src/limits.rs:7
 
-    def __init__(self, model_bytes: bytes, device: int = 0, **kw):
+
+@dataclass
+class TranslationInput:
+    """marian-core/src/types.rs:7-12"""
+    text: str
+    source_lang: str
+    target_lang: str
+    max_output_tokens: int = 512
+
+
+@dataclass
+class TranslationOutput:
+    """marian-core/src/types.rs:41-47"""
+    text: str
+    score: float | None
+    input_tokens: int
+    output_tokens: int
+
+
+class BackendError(Exception):
+    """BackendError (marian-core/src/types.rs:61-70); kind is one of
+    ``invalid_input``, ``unsupported_direction``, ``inference``."""
+
+    def __init__(self, kind: str, message: str):
+        super().__init__(message)
+        self.kind = kind
+
+
+def translate_texts(inputs, engine_fn, source, target, source_lang: str, target_lang: str,
+                    eos_id: int = 0):
+    """translate_with_engine (marian-cpu/src/backend.rs:107-346).
+
+    Each input is split by :func:`segmenter.segment_text` under
+    MAXIMUM_SOURCE_TOKENS - 1 source pieces; its non-empty segments are
+    tokenized, EOS-terminated and translated in order, every segment
+    limited to what the input's max_output_tokens budget has left after the
+    segments before it (an input whose budget is spent gets empty text for
+    its remaining segments); translations are joined with the original
+    separators.  ``source``/``target`` are the tokenizers
+    (``encode(str) -> list[int]``, ``decode(list[int]) -> str``,
+    ``vocabulary_size() -> int``, backend.rs:26-32); ``engine_fn(tokens,
+    offsets, max_output_tokens) -> (tokens, offsets)`` is the token engine.
+    Each round sends the next segment of every input with work left: the
+    engine batches any number of rows of any length, so the CPU engine's
+    batch bounds (backend.rs:222-240) have no counterpart, and the results
+    are the same because each row's greedy decode is independent of its
+    batch.
+    """
+    if not inputs:
+        return []
+    for inp in inputs:
+        if inp.source_lang != source_lang or inp.target_lang != target_lang:
+            raise BackendError("unsupported_direction",
+                               f"{inp.source_lang} -> {inp.target_lang}; loaded model is "
+                               f"{source_lang} -> {target_lang}")
+    vocab = source.vocabulary_size()
+    planned = []   # per input: [translated or None, separator, input_tokens, output_tokens]
+    work = []      # per input: [(planned index, tokens)]
+    total = 0
+    for inp in inputs:
+        try:
+            segments = _seg.segment_text(inp.text, MAXIMUM_SOURCE_TOKENS - 1,
+                                         lambda t: len(source.encode(t)))
+        except _seg.SegmentError as e:
+            raise BackendError("invalid_input", str(e)) from None
+        text = inp.text.encode("utf-8")
+        plan, todo = [], []
+        for sg in segments:
+            content, separator = sg.content(text), sg.separator(text)
+            if not content:
+                plan.append(["", separator, 0, 0])
+                continue
+            if total >= MAXIMUM_TRANSLATION_SEGMENTS:
+                raise BackendError("invalid_input", f"batch requires more than "
+                                                    f"{MAXIMUM_TRANSLATION_SEGMENTS} translated segments")
+            pieces = list(source.encode(content))
+            if len(pieces) != sg.source_pieces:
+                raise BackendError("inference", f"source tokenizer returned {len(pieces)} pieces after "
+                                                f"sizing the segment as {sg.source_pieces}")
+            bad = next((t for t in pieces if t < 0 or t >= vocab), None)
+            if bad is not None:
+                raise BackendError("invalid_input",
+                                   f"tokenizer returned source token {bad} outside vocabulary {vocab}")
+            pieces.append(eos_id)
+            if len(pieces) > MAXIMUM_SOURCE_TOKENS:
+                raise BackendError("inference", f"segmented source has {len(pieces)} tokens including EOS; "
+                                                f"maximum is {MAXIMUM_SOURCE_TOKENS}")
+            todo.append((len(plan), pieces))
+            plan.append([None, separator, len(pieces), 0])
+            total += 1
+        planned.append(plan)
+        work.append(todo)
+
+    positions = [0] * len(inputs)
+    remaining = [int(inp.max_output_tokens) for inp in inputs]
+    while True:
+        for i, todo in enumerate(work):
+            if remaining[i] == 0:  # the budget is spent: the rest translate to nothing
+                while positions[i] < len(todo):
+                    planned[i][todo[positions[i]][0]][0] = ""
+                    positions[i] += 1
+        batch = [(i, todo[positions[i]]) for i, todo in enumerate(work) if positions[i] < len(todo)]
+        if not batch:
+            break
+        offsets = np.zeros(len(batch) + 1, np.uint32)
+        offsets[1:] = np.cumsum([len(t) for _, (_, t) in batch])
+        tokens = np.concatenate([np.asarray(t, np.int32) for _, (_, t) in batch])
+        limits = np.array([remaining[i] for i, _ in batch], np.uint32)
+        out, out_off = engine_fn(tokens, offsets, limits)
+        if len(out_off) != len(batch) + 1:
+            raise BackendError("inference", "engine returned malformed batch offsets")
+        for row, (i, (pi, _)) in enumerate(batch):
+            start, end = int(out_off[row]), int(out_off[row + 1])
+            if end < start or end > len(out):
+                raise BackendError("inference", "engine returned out-of-range token offsets")
+            if end - start > remaining[i]:
+                raise BackendError("inference", "engine exceeded the original max_output_tokens budget")
+            remaining[i] -= end - start
+            ids = [int(t) for t in out[start:end] if t != eos_id]
+            planned[i][pi][0] = target.decode(ids)
+            planned[i][pi][3] = len(ids)
+            positions[i] += 1
+
+    return [TranslationOutput("".join(p[0] + p[1] for p in plan), None, sum(p[2] for p in plan),
+                              sum(p[3] for p in plan)) for plan in planned]
+
+
+class CudaBackend:
+    """TranslationBackend: token ids directly, or text through the caller's
+    tokenizers (translate)."""
+
+    def __init__(self, model_bytes: bytes, device: int = 0, source_tokenizer=None, target_tokenizer=None,
+                 source_lang: str = "", target_lang: str = "", eos_id: int = 0, **kw):
         self.engine = CudaEngine(model_bytes, device=device, **kw)
+        self.source_tokenizer, self.target_tokenizer = source_tokenizer, target_tokenizer
+        self.source_lang, self.target_lang, self.eos_id = source_lang, target_lang, eos_id
+
+    def translate(self, inputs):
+        """TranslationBackend::translate (marian-core/src/backend.rs:17-24) over
+        text: list of TranslationInput -> list of TranslationOutput."""
+        if self.source_tokenizer is None or self.target_tokenizer is None:
+            raise BackendError("invalid_input", "text translation needs source and target tokenizers")
+        return translate_texts(inputs, self.engine.translate_token_ids, self.source_tokenizer,
+                               self.target_tokenizer, self.source_lang, self.target_lang, self.eos_id)
 
     def info(self) -> BackendInfo:
         i = self.engine.info
