@@ -419,6 +419,16 @@ __global__ void __launch_bounds__(kLnWarps * 32) ssru_warp_kernel(
 constexpr int kEncWarps = 8;
 constexpr int kEncQpw = 4;  // queries per warp, advanced in two pairs
 
+// Asynchronous global -> shared copies (cp.async): 16 bytes (both addresses
+// 16-byte aligned) or 4 bytes; cp_async_wait_all waits for this thread's.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Packed f32x2 arithmetic (sm_100): each half is one IEEE f32 operation
 // rounded to nearest, exactly as the scalar instruction, so pairing two
 // independent sums changes no result while halving the issued instructions.
@@ -471,12 +481,14 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
   float* vs = ks + (size_t)max_len * KLD;                   // [max_len][HD]
   float* qs = vs + (size_t)max_len * HD;                   // [warps][2 pairs][HD][2]
   float* ps = qs + kEncWarps * kEncQpw * HD;               // [warps][2 pairs][max_len][2]
+  // K, V and the queries are staged with asynchronous copies (no register
+  // round trip), so every thread has all of its copies in flight at once.
   constexpr int kVec = HD / 4;
   for (int idx = threadIdx.x; idx < len * kVec; idx += blockDim.x) {
     const int j = idx / kVec, i = (idx % kVec) * 4;
     const float* row = qkv + (size_t)(start + j) * ld + h * HD + i;
-    *reinterpret_cast<float4*>(ks + j * KLD + i) = *reinterpret_cast<const float4*>(row + d);
-    *reinterpret_cast<float4*>(vs + j * HD + i) = *reinterpret_cast<const float4*>(row + 2 * d);
+    cp_async16(ks + j * KLD + i, row + d);
+    cp_async16(vs + j * HD + i, row + 2 * d);
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qb = q0 + warp * kEncQpw;                      // this warp's first query
@@ -486,9 +498,13 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
   float* pw = ps + warp * kEncQpw * max_len;
   for (int idx = lane; idx < kEncQpw * HD; idx += 32) {
     const int qq = idx / HD, i = idx % HD;
-    qw[(qq >> 1) * 2 * HD + 2 * i + (qq & 1)] =
-        qq < nq ? qkv[(size_t)(start + qb + qq) * ld + h * HD + i] : 0.0f;
+    float* dst = qw + (qq >> 1) * 2 * HD + 2 * i + (qq & 1);
+    if (qq < nq)
+      cp_async4(dst, qkv + (size_t)(start + qb + qq) * ld + h * HD + i);
+    else
+      *dst = 0.0f;
   }
+  cp_async_wait_all();
   __syncthreads();
   if (nq == 0) return;
   auto pidx = [&](int qq, int j) { return (qq >> 1) * 2 * max_len + 2 * j + (qq & 1); };
