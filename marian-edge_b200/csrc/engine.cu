@@ -1487,14 +1487,23 @@ extern "C" mc_status mc_translate_token_ids(mc_engine* e, const int32_t* tokens,
   if (st) return st;
   if (!max_out || !out_offsets || (!out_tokens && out_capacity))
     return fail(e, MC_INVALID_INPUT, "null output or limit buffers");
+  std::vector<Request*> reqs(batch);
   for (uint32_t b = 0; b < batch; ++b) {
     Request* r = new Request();
     r->id = b;
     r->tokens.assign(tokens + offsets[b], tokens + offsets[b + 1]);
     r->max_out = max_out[b];
     r->force = force_len ? force_len[b] : 0;
-    e->queue.push_back(r);
+    reqs[b] = r;
   }
+  // Longest first: the rows of a batch are independent (results come back
+  // by request id), so admitting those with the most decode steps first
+  // keeps the slots full to the end instead of leaving a tail of steps with
+  // few active rows; equal step bounds keep the submission order.
+  std::stable_sort(reqs.begin(), reqs.end(), [e](const Request* a, const Request* b) {
+    return request_limit(e, a) > request_limit(e, b);
+  });
+  for (Request* r : reqs) e->queue.push_back(r);
   const uint64_t step_bound = (uint64_t)batch * (kMaxSeq + 2) + 16;
   for (uint64_t i = 0; i < step_bound && (!e->queue.empty() || total_active(e) != 0); ++i) {
     if ((st = engine_step(e))) {

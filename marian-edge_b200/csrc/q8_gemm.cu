@@ -383,17 +383,17 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
       const GemmGroup& g = p.g[c.z];
       const int buf = it & 1;
       constexpr int kShare = BN / (EPI / 4) >= 32 ? BN / (EPI / 4) : 32;
-      // The per-row operands are loaded, and the first chunk's bias line is
-      // prefetched into L1, before the accumulator is ready, so their
-      // latency overlaps the MMAs.
+      // The per-row operands are loaded, and the bias lines of this warp's
+      // columns are prefetched into L1, before the accumulator is ready, so
+      // their latency overlaps the MMAs.
       const int row = c.m0 + quarter * 32 + lane;
       const bool row_ok = row < m;
       const int dest_row = row_ok ? (g.row_map ? g.row_map[row] : row) : 0;
       const float row_scale = (row_ok && g.row_scale) ? g.row_scale[row] : 1.0f;
       const int c_first = part * kShare;
       const int nb_first = c.n0 + c_first;
-      if (lane == 0 && g.bias != nullptr && g.mode != kEpiI32 && nb_first < g.n)
-        asm volatile("prefetch.global.L1 [%0];" ::"l"(g.bias + nb_first));
+      if (lane < kShare / 32 && g.bias != nullptr && g.mode != kEpiI32 && nb_first + 32 * lane < g.n)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(g.bias + nb_first + 32 * lane));
       // Warp-uniform: tcgen05.ld below is .sync.aligned.
       const bool ready = __all_sync(0xffffffffu, mbar_wait(&tfull_bar[buf], (it >> 1) & 1, p.status));
       if (!ready) break;
