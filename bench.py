@@ -13,6 +13,13 @@ data path).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
 
+`--workload longtext` runs the request-sharded long-text stream instead: per
+step, --docs documents per GPU of 200..2,000 Zipf(1.1) tokens with a
+pseudo-sentence end every 8..64 tokens, split by the library's segment_text
+(marian-core's splitter) into segments of at most 128 tokens with EOS,
+sorted by length and dealt round-robin over the replicas; the same output
+length rule.  The step's batch is built once, before timing.
+
 The reference arm times the CPU restatement of marian-edge's Q8 engine (the
 Rust reference cannot be built on this image) on the host cores.
 """
@@ -51,6 +58,8 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-latency", action="store_true")
+    p.add_argument("--workload", default="stream", choices=["stream", "longtext"])
+    p.add_argument("--docs", type=int, default=500, help="longtext: documents per GPU per step")
     return p.parse_args()
 
 
@@ -62,16 +71,27 @@ def dist_env():
 
 
 def config_dict(args, world):
-    return {"workload": "continuous-batching stream: %d requests/GPU/step, lognormal(ln24,0.8) src "
-                        "4..256 tok, Zipf(1.1) ids, out=round(1.2*src) EOS-masked" % args.requests,
+    if args.workload == "longtext":
+        workload = ("long-text stream: %d documents/GPU/step of 200..2000 Zipf(1.1) tokens, pseudo-sentence "
+                    "every 8..64 tokens, split by segment_text into segments <= 128 tokens, dealt round-robin "
+                    "by length over %d replica(s), out=round(1.2*src) EOS-masked" % (args.docs, world))
+    else:
+        workload = ("continuous-batching stream: %d requests/GPU/step, lognormal(ln24,0.8) src "
+                    "4..256 tok, Zipf(1.1) ids, out=round(1.2*src) EOS-masked" % args.requests)
+    return {"workload": workload,
             "model_shape": args.model, "d_model": W.SHAPES[args.model].dim,
             "decoder": W.SHAPES[args.model].decoder_kind, "max_inflight": args.max_inflight,
             "page_tokens": 16, "parallelism": "replica x%d (request-sharded)" % world,
             "l2": "no flush: each step streams > 1 GB of KV-cache pages and activations (L2 is 126 MB)"}
 
 
-def step_batches(args, rank, count, base_seed):
+def step_batches(args, rank, count, base_seed, world=1):
     vocab = W.SHAPES[args.model].vocab
+    if args.workload == "longtext":
+        # one global document set per call, dealt over the replicas; every
+        # step repeats it (the engine keeps nothing between steps)
+        b = W.longtext_batch(args.docs * world, vocab=vocab, seed=base_seed, rank=rank, world=world)
+        return [b] * count
     return [W.stream_batch(n=args.requests, vocab=vocab, seed=base_seed + 7919 * rank + s) for s in range(count)]
 
 
@@ -256,8 +276,8 @@ def run_cuda(args):
                      lanes=args.lanes)
     lib = L.load()
     stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
-    warm = step_batches(args, rank, max(1, args.warmup), 100)
-    timed = step_batches(args, rank, args.steps, 1000)
+    warm = step_batches(args, rank, max(1, args.warmup), 100, world)
+    timed = step_batches(args, rank, args.steps, 1000, world)
 
     def run(batch):
         out, off = eng.translate_token_ids(batch.tokens, batch.offsets, batch.max_out, batch.force_len)
@@ -302,7 +322,7 @@ def run_cuda(args):
     all_tokens, max_ms, max_wall = reduce_job(tokens, dev_ms, wall, world, "cuda")
 
     latency = None
-    if not args.no_latency and rank == 0:
+    if not args.no_latency and rank == 0 and args.workload == "stream":
         latency = poisson_latency(eng, args)
 
     if rank == 0:

@@ -1186,8 +1186,24 @@ mc_status engine_step(mc_engine* e) {
   for (Lane& L : e->lanes) {
     if ((st = complete_lane(e, L))) return st;
     // a finished encoder pass joins now; with nothing to decode, wait for it
-    if ((st = join_pending(e, L, L.active.empty())) || (st = admit(e, L, L.cap)) ||
-        (L.active.empty() && (st = join_pending(e, L, true))) || (st = launch_decode(e, L, true))) {
+    if ((st = join_pending(e, L, L.active.empty()))) {
+      abort_all(e);
+      return st;
+    }
+    if (L.active.empty()) {
+      // idle lane: admit, wait for the encoder pass, then decode its rows
+      st = admit(e, L, L.cap);
+      if (!st && L.active.empty()) st = join_pending(e, L, true);
+      if (!st) st = launch_decode(e, L, true);
+    } else {
+      // The step is launched before the admission: the admission's host
+      // work (packing the sources, enqueueing the encoder pass on the
+      // encoder stream) then overlaps the step on the GPU.  Its rows join
+      // at a later step either way, once the encoder pass has completed.
+      st = launch_decode(e, L, true);
+      if (!st) st = admit(e, L, L.cap);
+    }
+    if (st) {
       abort_all(e);
       return st;
     }

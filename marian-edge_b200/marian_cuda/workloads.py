@@ -204,6 +204,55 @@ def stream_batch(n=256, vocab=32000, seed=0) -> Batch:
     return pack([zipf_ids(rng, int(l) - 1, vocab) for l in lens])
 
 
+class WordIds:
+    """Tokenizer of the synthetic documents: the word "w<id>" (a trailing
+    '.' marks a pseudo-sentence end) is the piece <id>."""
+
+    def __init__(self, vocab=32000):
+        self.vocab = vocab
+
+    def vocabulary_size(self):
+        return self.vocab
+
+    def encode(self, text):
+        return [int(w.rstrip(".")[1:]) for w in text.split()]
+
+    def decode(self, ids):
+        return " ".join(f"w{i}" for i in ids)
+
+
+def longtext_document(rng, vocab=32000, lo=200, hi=2000, s_lo=8, s_hi=64) -> str:
+    """One long-text document: lo..hi Zipf ids as words, with a pseudo-sentence
+    end ('.') every s_lo..s_hi tokens."""
+    n = int(rng.integers(lo, hi + 1))
+    ids = zipf_ids(rng, n, vocab)
+    parts, k = [], 0
+    while k < n:
+        m = min(int(rng.integers(s_lo, s_hi + 1)), n - k)
+        parts.append(" ".join(f"w{i}" for i in ids[k:k + m]) + ".")
+        k += m
+    return " ".join(parts)
+
+
+def longtext_batch(n_docs, vocab=32000, seed=0, rank=0, world=1, max_tokens=128) -> Batch:
+    """The long-text stream: n_docs documents split by the library's
+    segment_text into segments of at most max_tokens tokens with EOS, sorted
+    by length and dealt round-robin over `world` replicas (this one takes
+    every world-th from `rank`); output length rule as the other workloads."""
+    from . import segmenter
+    rng = np.random.Generator(np.random.PCG64(seed))
+    tok = WordIds(vocab)
+    sources = []
+    for _ in range(n_docs):
+        doc = longtext_document(rng, vocab)
+        for sg in segmenter.segment_text(doc, max_tokens - 1, lambda t: len(t.split())):
+            ids = tok.encode(sg.content(doc))
+            if ids:
+                sources.append(ids)
+    order = sorted(range(len(sources)), key=lambda i: (len(sources[i]), i))
+    return pack([sources[i] for i in order[rank::world]])
+
+
 def poisson_arrivals(n, rate, seed=0):
     rng = np.random.Generator(np.random.PCG64(seed + 7919))
     return np.cumsum(rng.exponential(1.0 / rate, size=n))

@@ -226,3 +226,18 @@ def test_library_matches_the_oracle_on_random_texts():
         assert all(p <= limit for _, _, p in got)
         checked += 1
     assert checked > 200
+
+
+def test_longtext_workload_segments_fit_and_partition_over_replicas():
+    # The long-text benchmark stream: documents split by the library into
+    # segments of at most 128 tokens (EOS included), dealt over replicas.
+    import numpy as np
+    from marian_cuda import workloads as W
+    full = W.longtext_batch(40, seed=3)
+    lens = np.diff(full.offsets.astype(np.int64))
+    assert lens.max() <= 128 and lens.min() >= 2
+    assert all(full.tokens[o - 1] == W.EOS for o in full.offsets[1:])
+    parts = [W.longtext_batch(40, seed=3, rank=r, world=3) for r in range(3)]
+    assert sum(p.size for p in parts) == full.size
+    assert sorted(np.concatenate([np.diff(p.offsets.astype(np.int64)) for p in parts])) == sorted(lens)
+    assert np.array_equal(full.force_len, W.force_lengths(lens - 1))
