@@ -148,3 +148,30 @@ def test_text_translation_on_the_gpu_matches_the_oracle_engine(name):
     finally:
         backend.engine.close()
     assert got == want
+
+
+def test_text_path_with_the_oracle_engine_respects_budgets_and_separators():
+    # The planning and budget loop over real greedy outputs (the CPU oracle
+    # engine on a tiny model): each input's generated tokens fit its budget,
+    # every separator survives, and an input whose budget runs out before its
+    # last segment gets empty text there.
+    mb = W.synthetic_model(W.SHAPES["tiny_self"], seed=5)
+    om = O.OracleModel(mb)
+    tok = WordTokenizer(vocab=W.SHAPES["tiny_self"].vocab)
+    engine = lambda t, o, m: om.translate(t, o, m, None)
+    texts = ["a b c.\nd e f g.\r\n", "one two three four five six seven. eight nine.  ", "x"]
+    budgets = [40, 3, 5]
+    outs = B.translate_texts([_inp(t, b) for t, b in zip(texts, budgets)], engine, tok, tok, "en", "zh")
+    for text, budget, out in zip(texts, budgets, outs):
+        assert out.output_tokens <= budget
+        assert out.input_tokens == len(text.split()) + len(
+            [s for s in _segments(text) if s.strip()])  # pieces + one EOS per non-empty segment
+    assert outs[0].text.endswith("\r\n") and "\n" in outs[0].text
+    assert outs[1].text.endswith("  ")
+    again = B.translate_texts([_inp(t, b) for t, b in zip(texts, budgets)], engine, tok, tok, "en", "zh")
+    assert again == outs  # greedy decoding is deterministic
+
+
+def _segments(text):
+    from marian_cuda import segmenter as S
+    return [sg.content(text) for sg in S.segment_text(text, 255, lambda t: len(t.split()))]
