@@ -7,10 +7,11 @@
   continuous batcher (``submit`` / ``step`` / ``poll``).
 * :class:`CudaBackend` is the ``TranslationBackend`` contract
   (``crates/marian-core/src/backend.rs:7-38``): ``info()``, ``is_ready()``,
-  ``translate_batch`` over token ids, and -- given the caller's source and
-  target tokenizers -- ``translate`` over text, which splits long inputs
-  (``segment_text``) and shares each input's output budget across its
-  segments exactly as the reference's CPU backend does
+  ``translate_batch`` / ``translate_batch_with_repetitions`` over text
+  through the caller's source and target tokenizers (``translate`` is the
+  same call; ``translate_token_batch`` serves token-id callers).  The text
+  calls split long inputs (``segment_text``) and share each input's output
+  budget across its segments exactly as the reference's CPU backend does
   (``crates/marian-cpu/src/backend.rs:107-346``, :func:`translate_texts`).
 
 Errors map to the reference's ``BackendError`` kinds
@@ -290,13 +291,24 @@ class CudaBackend:
         self.source_tokenizer, self.target_tokenizer = source_tokenizer, target_tokenizer
         self.source_lang, self.target_lang, self.eos_id = source_lang, target_lang, eos_id
 
-    def translate(self, inputs):
-        """TranslationBackend::translate (marian-core/src/backend.rs:17-24) over
-        text: list of TranslationInput -> list of TranslationOutput."""
+    def translate_batch(self, inputs):
+        """TranslationBackend::translate_batch (marian-core/src/backend.rs:20-23):
+        list of TranslationInput (text) -> list of TranslationOutput, through the
+        caller's tokenizers, long-text splitting and the shared output budget."""
         if self.source_tokenizer is None or self.target_tokenizer is None:
             raise BackendError("invalid_input", "text translation needs source and target tokenizers")
         return translate_texts(inputs, self.engine.translate_token_ids, self.source_tokenizer,
                                self.target_tokenizer, self.source_lang, self.target_lang, self.eos_id)
+
+    translate = translate_batch
+
+    def translate_batch_with_repetitions(self, inputs, repetitions):
+        """marian-core/src/backend.rs:25-37: one output per logical input.  The
+        repetition counts (admitted requests per row) are not needed to fill
+        the GPU, so the rows are translated once, as the trait's default does."""
+        if len(inputs) != len(repetitions):
+            raise BackendError("invalid_input", f"{len(inputs)} inputs but {len(repetitions)} repetition counts")
+        return self.translate_batch(inputs)
 
     def info(self) -> BackendInfo:
         i = self.engine.info
@@ -308,15 +320,11 @@ class CudaBackend:
     def is_ready(self) -> bool:
         return self.engine.is_ready()
 
-    def translate_batch(self, sources, max_output_tokens=512):
-        """sources: list of token-id sequences each ending in EOS."""
+    def translate_token_batch(self, sources, max_output_tokens=512):
+        """Token-id callers: list of token-id sequences each ending in EOS -> the
+        generated ids per sequence (EOS included when generated)."""
         offsets = np.zeros(len(sources) + 1, np.uint32)
         offsets[1:] = np.cumsum([len(s) for s in sources])
         toks = np.concatenate([np.asarray(s, np.int32) for s in sources]) if sources else np.zeros(0, np.int32)
         out, off = self.engine.translate_token_ids(toks, offsets, np.full(len(sources), max_output_tokens, np.uint32))
         return [out[off[i]:off[i + 1]] for i in range(len(sources))]
-
-    def translate_batch_with_repetitions(self, sources, repetitions, max_output_tokens=512):
-        # one output per logical input (marian-core/src/backend.rs:26-37)
-        assert len(sources) == len(repetitions)
-        return self.translate_batch(sources, max_output_tokens)

@@ -175,3 +175,33 @@ def test_text_path_with_the_oracle_engine_respects_budgets_and_separators():
 def _segments(text):
     from marian_cuda import segmenter as S
     return [sg.content(text) for sg in S.segment_text(text, 255, lambda t: len(t.split()))]
+
+
+def test_backend_entry_points_follow_the_trait():
+    # TranslationBackend's batch calls (marian-core/src/backend.rs:7-38) on a
+    # CudaBackend whose engine is the CPU oracle, so the test needs no GPU.
+    class OracleEngine:
+        def __init__(self, mb):
+            self.om = O.OracleModel(mb)
+
+        def translate_token_ids(self, t, o, m, force_len=None):
+            return self.om.translate(t, o, m, None)
+
+    mb = W.synthetic_model(W.SHAPES["tiny_self"], seed=5)
+    tok = WordTokenizer(vocab=W.SHAPES["tiny_self"].vocab)
+    be = object.__new__(B.CudaBackend)
+    be.engine = OracleEngine(mb)
+    be.source_tokenizer = be.target_tokenizer = tok
+    be.source_lang, be.target_lang, be.eos_id = "en", "zh", 0
+    inputs = [_inp("a b c. d e.", 30), _inp("f g", 4)]
+    outs = be.translate_batch(inputs)
+    assert be.translate(inputs) == outs
+    assert be.translate_batch_with_repetitions(inputs, [3, 1]) == outs  # one output per logical input
+    with pytest.raises(B.BackendError) as e:
+        be.translate_batch_with_repetitions(inputs, [1])
+    assert e.value.kind == "invalid_input"
+    ids = be.translate_token_batch([tok.encode("f g") + [0]], max_output_tokens=4)
+    assert tok.decode([int(t) for t in ids[0] if t != 0]) == outs[1].text
+    be.source_tokenizer = None
+    with pytest.raises(B.BackendError):
+        be.translate_batch(inputs)
