@@ -15,9 +15,11 @@
 // device code is loaded holds the array until the process exits.  Its device
 // address is looked up once per device (cudaGetSymbolAddress, on the first
 // call made with that device current); host code never passes the array's
-// host-side name to a kernel.  All calls on a device share the array: calls
-// whose kernels overlap on the GPU (different streams without ordering) race
-// on it.
+// host-side name to a kernel.  The cached address belongs to the device
+// context the first call ran in: a cudaDeviceReset after that call is not
+// supported (the array is reloaded elsewhere with the module).  All calls on
+// a device share the array: calls whose kernels overlap on the GPU
+// (different streams without ordering) race on it.
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -72,14 +74,17 @@ extern "C" mc_status mc_q8_linear_noalloc(const float* x, int32_t m, int32_t k, 
   int8_t* q = reinterpret_cast<int8_t*>(base + kStatusBytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (m > 0) {
-    mc::launch_quantize(x, (long long)m * k, activation_mult, q, status, s);
     mc::GemmParams p;
     std::memset(&p, 0, sizeof(p));
     const int bn = mc::pick_bn(m, n);
     mc::GemmGroup& g = p.g[0];
+    // Both tensor maps are encoded (and w's alignment checked) before any
+    // launch, so an invalid weight pointer returns without touching the
+    // scratch or its status word.
     if (!mc::encode_tmap_i8(&g.tmap_a, q, (uint64_t)m, (uint64_t)k, 128) ||
         !mc::encode_tmap_i8(&g.tmap_b, w, (uint64_t)n, (uint64_t)k, (uint32_t)bn))
       return MC_INVALID_INPUT;
+    mc::launch_quantize(x, (long long)m * k, activation_mult, q, status, s);
     g.uniform_scale = inverse_scale;
     g.bias = bias;
     g.out = y;
