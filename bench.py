@@ -297,6 +297,16 @@ def run_cuda(args):
             prof[name] = {"launches": n.value, "ms": ms.value, "flops": fl.value, "bytes": by.value}
     lib.mc_profile(eng.handle, 0)
 
+    # decode-stream timeline on one more (untimed) step: each decode step's
+    # device time and the stream's idle time between steps
+    lib.mc_timeline(eng.handle, 1)
+    run(warm[0])
+    tl_n, tl_busy, tl_idle = C.c_uint64(), C.c_double(), C.c_double()
+    lib.mc_timeline_read(eng.handle, C.byref(tl_n), C.byref(tl_busy), C.byref(tl_idle))
+    lib.mc_timeline(eng.handle, 0)
+    timeline = {"decode_steps": tl_n.value, "busy_ms": tl_busy.value, "idle_ms": tl_idle.value,
+                "idle_frac": tl_idle.value / max(1e-9, tl_busy.value + tl_idle.value)}
+
     torch.cuda.synchronize()
     barrier()
     launches0 = lib.mc_launch_count(eng.handle)
@@ -366,7 +376,8 @@ def run_cuda(args):
                         "d2h_bytes_per_step": d2h // args.steps,
                         "path": "mc_translate_token_ids from host numpy buffers, host wall clock"},
                 "gpu_launches": int(launches), "roofline": roofline, "cpu_baseline": cpu,
-                "clocks": clocks.summary(), "kernel_profile": prof, "target_tokens": int(all_tokens)}
+                "clocks": clocks.summary(), "kernel_profile": prof, "decode_stream": timeline,
+                "target_tokens": int(all_tokens)}
         if latency:
             line["latency_ms"] = latency
         print(json.dumps(line), flush=True)

@@ -86,6 +86,37 @@ mc_status mc_load_marian_bin(mc_engine *e, const uint8_t *bytes, size_t len);
 
 mc_status mc_model_info_get(const mc_engine *e, mc_model_info *info);
 
+/* What mc_inspect_marian_bin found in a model file. */
+typedef struct {
+    uint64_t tensors;
+    uint64_t dense_linears;       /* intgemm8 weights with an activation scale */
+    uint64_t embeddings;          /* intgemm8 *_Wemb tables */
+    uint64_t activation_scales;   /* *_QuantMultA scalars */
+    uint64_t row_scaled_linears;  /* dense weights with *_QuantMultRows (extension below) */
+    float decoder_output_alpha;   /* decoder_Wemb_QuantMultA, normalised; 0 if absent */
+    int32_t engine_graph;         /* 1: the tensor set is a graph this engine runs */
+    int32_t decoder_kind, dim, heads, encoder_layers, decoder_layers;  /* when engine_graph */
+} mc_model_report;
+
+/* Host-only check of a Marian binary v1 file, no device or engine needed:
+ * MarianBinaryModel::parse and ::validate_q8 (crates/marian-cpu/src/
+ * legacy_q8.rs:179-422, 497-542) -- header, names, shapes, 256-byte
+ * alignment and zero padding, record lengths, trailing bytes, finite
+ * positive multipliers, no -128, every activation scale a positive scalar
+ * of an intgemm8 weight, every dense weight with its scale -- then the
+ * engine's schema check (q8_engine.rs:1007-1101).  A format or Q8 error
+ * returns MC_MODEL with the reason in message; a valid file the engine
+ * cannot run returns MC_OK with engine_graph = 0 and the reason.
+ *
+ * Per-row extension (no counterpart in the reference, whose weights have one
+ * multiplier per tensor): a dense weight W may come with a float32 tensor
+ * W_QuantMultRows of shape [1, out], one multiplier per output row; the
+ * weight's row n is then values[n, :] / W_QuantMultRows[n] and its outputs
+ * dequantize with 1 / (alpha * W_QuantMultRows[n]).  mc_load_marian_bin
+ * accepts such files. */
+mc_status mc_inspect_marian_bin(const uint8_t *bytes, size_t len, mc_model_report *report,
+                                char *message, size_t message_capacity);
+
 /* Loads a Marian lexical shortlist (LexicalShortlist::from_bytes and
  * ::candidates, marian-model/src/shortlist.rs:59-198; the engine's
  * prepare_candidates, marian-cpu/src/q8_engine.rs:576-584): each sentence's
@@ -182,6 +213,15 @@ mc_status mc_profile_read(const mc_engine *e, int32_t kind, uint64_t *launches, 
 /* Number of kernels the engine has launched since creation. */
 uint64_t mc_launch_count(const mc_engine *e);
 
+/* Decode-stream timeline (measurement only; the reference has no
+ * counterpart).  mc_timeline(e, 1) clears the counters and records a pair
+ * of events around every decode step; mc_timeline_read returns the steps
+ * completed since, their summed device duration, and the summed idle time
+ * of the decode streams between the end of one step and the start of the
+ * next (host round trips, waits for admissions).  Off by default. */
+mc_status mc_timeline(mc_engine *e, int32_t enable);
+mc_status mc_timeline_read(const mc_engine *e, uint64_t *steps, double *busy_ms, double *idle_ms);
+
 /* Device-level Q8 GEMM (benchmark / operator API), Q8Linear::run_into's
  * integer GEMM and epilogue.  a: device int8 [m, k] (centred activations,
  * i.e. the reference's u8 minus 127), w: device int8 [n, k] (canonical
@@ -222,8 +262,9 @@ mc_status mc_q8_linear(const float *x, int32_t m, int32_t k, const int8_t *w, in
  * GPU using the library holds until the process exits.  m * k beyond that
  * size returns MC_INVALID_INPUT without launching anything.  The first call
  * on a device looks up the array's device address (make it before any
- * stream capture).  All calls share the array: calls whose kernels overlap
- * on the GPU race.  status_bits (host pointer, nullable): when given, the
+ * stream capture) and keeps it for the process: cudaDeviceReset after that
+ * call is not supported.  All calls share the array: calls whose kernels
+ * overlap on the GPU race.  status_bits (host pointer, nullable): when given, the
  * call synchronizes the stream and returns the status bits recorded since
  * the last report (bit 0: non-finite activation), clearing them; when null
  * the call stays asynchronous and the bits accumulate. */

@@ -47,6 +47,7 @@ struct DevLinear {
   int in = 0, out = 0;
   float alpha = 1.0f;          // this linear's own activation alpha
   float scale = 1.0f;          // 1 / (alpha * weight quant_mult)
+  bool per_row = false;        // col_scale holds 1 / (alpha * row multiplier[n])
   CUtensorMap tmap_b[3];       // W tensor maps for BN = 64, 128, 256
 };
 
@@ -92,8 +93,26 @@ struct ProfRec {
   cudaEvent_t a, b;
 };
 
+// One decode step enqueued on a lane and not yet applied on the host.
+struct StepInFlight {
+  std::vector<int32_t> joins;  // admitted slots the step's row table appends
+  int parity = 0;              // which result buffers (and graph) the step uses
+  int rows_bound = 0;          // its rows: exact once the step before it is applied
+  cudaEvent_t tl_start = nullptr, tl_end = nullptr;  // mc_timeline
+};
+
 // One lane: a stream, the activation buffers of an encoder pass and of a
-// decode step, and the rows (slots) whose step runs on it.
+// decode step, and the rows (slots) whose steps run on it.
+//
+// The row table a step runs over lives on the device: the step's first
+// kernel (launch_step_rows) drops the rows the previous step finished and
+// appends the slots admitted since, so a lane keeps up to kStepDepth steps
+// enqueued and the host applies a step's tokens while the next one runs.
+// The host mirrors the table: `active` is the previous applied step's rows
+// minus the ones it finished; an enqueued step's rows are `active` (as it
+// will be when the steps before it are applied) followed by its joins.
+constexpr int kStepDepth = 2;
+
 struct Lane {
   int id = 0;
   int cap = 0;                       // scheduling limit on active rows
@@ -103,7 +122,6 @@ struct Lane {
   cudaEvent_t enc_done = nullptr;    // the last admission's encoder pass is complete
   cudaStream_t cur = nullptr;        // stream the launch helpers use
   uint32_t* d_status = nullptr;      // error bits of this lane's kernels
-  uint32_t* h_status = nullptr;      // pinned
 
   // encoder pass (capacity tmax packed tokens)
   float *enc_x = nullptr, *enc_x1 = nullptr, *enc_qkv = nullptr, *enc_proj = nullptr;
@@ -124,26 +142,35 @@ struct Lane {
   float *dec_a = nullptr, *dec_b = nullptr, *dec_qkv = nullptr, *dec_proj = nullptr;
   QBuf dec_q[kMaxQuantOut];
   QBuf dec_o, dec_h;
-  // rows block [4 + 3 * rmax]: row count, pad, then row slots, self-attention
-  // row order and cross-attention row order (longest first), rmax each
-  int32_t* rows_h = nullptr;  // pinned
+  // device row table [4 + 3 * rmax]: row count, 3 unused, then row slots,
+  // self-attention row order and cross-attention row order (most keys
+  // first), rmax each -- written by each step's launch_step_rows
   int32_t* rows_d = nullptr;
+  int32_t* rows_scratch = nullptr;   // [rmax]
+  int32_t* join_d = nullptr;         // [1 + rmax]: count, then the appended slots
   int32_t *self_row_map = nullptr, *step_tokens = nullptr;
   uint8_t *eos_mask = nullptr, *done = nullptr;
   unsigned long long* best = nullptr;
-  int32_t* h_step_tokens = nullptr;  // pinned
-  uint8_t* h_done = nullptr;         // pinned
+  // per parity (two steps in flight): pinned join block and read-backs
+  int32_t* join_h[kStepDepth] = {};
+  int32_t* h_step_tokens[kStepDepth] = {};
+  uint8_t* h_done[kStepDepth] = {};
+  uint32_t* h_status[kStepDepth] = {};
+  cudaEvent_t step_done[kStepDepth] = {};  // recorded after the step's read-backs
 
-  std::vector<int32_t> active;   // slots in row order
+  std::vector<int32_t> active;   // rows surviving the last applied step, in table order
+  std::vector<int32_t> ready;    // admitted slots whose encoder pass is done; next step appends them
   std::vector<int32_t> pending;  // admitted slots whose encoder pass is in flight
+  std::deque<StepInFlight> inflight;
+  int next_parity = 0;
   bool enc_in_flight = false;
-  int launched = 0;              // rows of the step in flight (0: none)
   float* last_state = nullptr;  // final decoder state of the last step
   int eager_steps = 0;
-  cudaGraphExec_t graph = nullptr;  // decode step for up to `cap` rows
-  bool graph_tried = false;
+  cudaGraphExec_t graph[kStepDepth] = {};  // decode step for up to `cap` rows, per parity
+  bool graph_tried[kStepDepth] = {};
   uint64_t graph_kernels = 0;
   std::vector<ProfRec> prof_pending;
+  cudaEvent_t tl_prev_end = nullptr;  // mc_timeline: end of the last applied step
 
   int32_t* row_slot() const { return rows_d + 4; }
 };
@@ -209,6 +236,9 @@ struct mc_engine {
 
   bool profiling = false;
   std::vector<cudaEvent_t> event_pool;
+  bool timeline = false;
+  uint64_t tl_steps = 0;
+  double tl_busy_ms = 0.0, tl_gap_ms = 0.0;
   double prof_ms[MC_KERNEL_KINDS] = {}, prof_flops[MC_KERNEL_KINDS] = {}, prof_bytes[MC_KERNEL_KINDS] = {};
   uint64_t prof_n[MC_KERNEL_KINDS] = {};
 
@@ -234,19 +264,21 @@ mc_status fail_cuda(mc_engine* e, const char* what, cudaError_t err) {
   return MC_CUDA;
 }
 
+// A timing event from the engine's pool.
+cudaEvent_t pooled_event(mc_engine* e) {
+  cudaEvent_t x = nullptr;
+  if (!e->event_pool.empty()) {
+    x = e->event_pool.back();
+    e->event_pool.pop_back();
+  } else {
+    cudaEventCreate(&x);
+  }
+  return x;
+}
+
 int prof_begin(mc_engine* e, Lane& L, int kind, double flops, double bytes) {
   if (!e->profiling) return -1;
-  auto ev = [&]() {
-    cudaEvent_t x;
-    if (!e->event_pool.empty()) {
-      x = e->event_pool.back();
-      e->event_pool.pop_back();
-    } else {
-      cudaEventCreate(&x);
-    }
-    return x;
-  };
-  ProfRec r{kind, flops, bytes, ev(), ev()};
+  ProfRec r{kind, flops, bytes, pooled_event(e), pooled_event(e)};
   cudaEventRecord(r.a, L.cur);
   L.prof_pending.push_back(r);
   return (int)L.prof_pending.size() - 1;
@@ -270,6 +302,35 @@ void prof_harvest(mc_engine* e, Lane& L) {
     e->event_pool.push_back(r.b);
   }
   L.prof_pending.clear();
+}
+
+// Timeline of lane L's decode stream (call once step F is complete): the
+// step's duration between the events recorded before and after its work,
+// and the stream's idle time since the previous step ended.
+void timeline_harvest(mc_engine* e, Lane& L, StepInFlight& F) {
+  if (!F.tl_start) return;
+  float busy = 0.0f, gap = 0.0f;
+  if (cudaEventElapsedTime(&busy, F.tl_start, F.tl_end) == cudaSuccess) {
+    e->tl_busy_ms += busy;
+    ++e->tl_steps;
+  }
+  if (L.tl_prev_end && cudaEventElapsedTime(&gap, L.tl_prev_end, F.tl_start) == cudaSuccess)
+    e->tl_gap_ms += gap;
+  if (L.tl_prev_end) e->event_pool.push_back(L.tl_prev_end);
+  e->event_pool.push_back(F.tl_start);
+  L.tl_prev_end = F.tl_end;
+  F.tl_start = F.tl_end = nullptr;
+}
+
+void timeline_drop(mc_engine* e, Lane& L) {
+  for (StepInFlight& F : L.inflight)
+    for (cudaEvent_t* ev : {&F.tl_start, &F.tl_end})
+      if (*ev) {
+        e->event_pool.push_back(*ev);
+        *ev = nullptr;
+      }
+  if (L.tl_prev_end) e->event_pool.push_back(L.tl_prev_end);
+  L.tl_prev_end = nullptr;
 }
 
 #define PROFILED(kind, flops, bytes, stmt)                        \
@@ -329,6 +390,18 @@ mc_status upload_linear(mc_engine* e, const std::string& wname, const char* bnam
     return fail(e, MC_MODEL, wname + ": 1 / (activation scale * quantization multiplier) is not finite");
   L->scale = inv;
   std::vector<float> cs(L->out, inv);
+  // per-output-row multipliers (the loader's _QuantMultRows extension):
+  // column n of the GEMM output dequantizes with 1 / (alpha * mult[n])
+  const std::vector<float> rows = weight_row_mults(e->host, wname);
+  if (!rows.empty()) {
+    if ((int)rows.size() != L->out) return fail(e, MC_MODEL, wname + ": row multiplier count mismatch");
+    for (int n = 0; n < L->out; ++n) {
+      cs[n] = 1.0f / (L->alpha * rows[n]);
+      if (!std::isfinite(cs[n]) || cs[n] <= 0.0f)
+        return fail(e, MC_MODEL, wname + ": 1 / (activation scale * row multiplier) is not finite");
+    }
+    L->per_row = true;
+  }
   CK(dalloc(e, &L->col_scale, cs.size()));
   CK(cudaMemcpyAsync(L->col_scale, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, e->stream));
   if (bname) {
@@ -407,7 +480,8 @@ mc_status gemm(mc_engine* e, Lane& L, int kind, int m, const int32_t* m_dev, dou
     GemmGroup& g = p.g[i];
     g.tmap_a = s.a->tmap;
     g.tmap_b = s.w->tmap_b[bn_index(bn)];
-    g.col_scale = nullptr;  // per-tensor weight scale (q8_gemm.rs:438)
+    // per-tensor weight scale (q8_gemm.rs:438), or the per-row extension's
+    g.col_scale = s.w->per_row ? s.w->col_scale : nullptr;
     g.uniform_scale = s.w->scale;
     g.bias = s.w->bias;
     g.out = s.out;
@@ -575,7 +649,9 @@ mc_status run_encoder(mc_engine* e, Lane& L, const AdmLayout& A, double sum_len_
 // Grids cover `cap` rows; the kernels read the step's row count from the
 // lane's rows block (rows_d[0]), so the same launches serve any row count up
 // to cap and can be replayed from a CUDA graph.
-mc_status run_decode_step(mc_engine* e, Lane& L, int cap) {
+// `rows` (the step's slots, known exactly when profiling) only feeds the
+// profile's algorithmic byte and flop counts.
+mc_status run_decode_step(mc_engine* e, Lane& L, int cap, const std::vector<int32_t>& rows) {
   const int d = e->d;
   float* x = L.dec_a;   // layer input
   float* y = L.dec_b;   // next
@@ -586,14 +662,14 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap) {
   // key counts for the attention roofline: self = step + 1, cross = source
   double self_keys = 0, cross_keys = 0;
   if (e->profiling) {
-    for (int s : L.active) {
+    for (int s : rows) {
       const Request* q = e->slot_req[s];
       if (!q) continue;
       self_keys += (double)q->output.size() + 1;
       cross_keys += (double)q->tokens.size();
     }
   }
-  const double R = (double)L.active.size();
+  const double R = (double)rows.size();
   const double rows_d = R * d;
   PROFILED(MC_K_EMBED, 0.0, rows_d * (1 + 4 + 4 + 3),
            launch_embed_decoder(cap, nrows, row_slot, e->slot_prev, e->slot_step, e->slot_force,
@@ -689,12 +765,19 @@ mc_engine::~mc_engine() {
       cudaEventDestroy(r.a);
       cudaEventDestroy(r.b);
     }
-    if (L.graph) cudaGraphExecDestroy(L.graph);
-    if (L.h_status) cudaFreeHost(L.h_status);
+    for (StepInFlight& F : L.inflight)
+      for (cudaEvent_t ev : {F.tl_start, F.tl_end})
+        if (ev) cudaEventDestroy(ev);
+    if (L.tl_prev_end) cudaEventDestroy(L.tl_prev_end);
+    for (int i = 0; i < kStepDepth; ++i) {
+      if (L.graph[i]) cudaGraphExecDestroy(L.graph[i]);
+      if (L.h_status[i]) cudaFreeHost(L.h_status[i]);
+      if (L.join_h[i]) cudaFreeHost(L.join_h[i]);
+      if (L.h_step_tokens[i]) cudaFreeHost(L.h_step_tokens[i]);
+      if (L.h_done[i]) cudaFreeHost(L.h_done[i]);
+      if (L.step_done[i]) cudaEventDestroy(L.step_done[i]);
+    }
     if (L.adm_h) cudaFreeHost(L.adm_h);
-    if (L.rows_h) cudaFreeHost(L.rows_h);
-    if (L.h_step_tokens) cudaFreeHost(L.h_step_tokens);
-    if (L.h_done) cudaFreeHost(L.h_done);
     if (L.own_stream && L.stream) cudaStreamDestroy(L.stream);
     if (L.enc_stream) cudaStreamDestroy(L.enc_stream);
     if (L.enc_done) cudaEventDestroy(L.enc_done);
@@ -717,8 +800,6 @@ mc_status allocate_lane(mc_engine* e, Lane& L) {
   const int d = e->d, F = e->ffn;
   const int T = e->tmax, R = e->rmax;
   CK(dalloc(e, &L.d_status, 1));
-  CK(cudaHostAlloc(&L.h_status, sizeof(uint32_t), cudaHostAllocDefault));
-  *L.h_status = 0;
   CK(dalloc(e, &L.enc_x, (size_t)T * d));
   CK(dalloc(e, &L.enc_x1, (size_t)T * d));
   CK(dalloc(e, &L.enc_qkv, (size_t)T * 3 * d));
@@ -753,16 +834,23 @@ mc_status allocate_lane(mc_engine* e, Lane& L) {
   }
   if ((st = make_qbuf(e, &L.dec_o, R, d))) return st;
   if ((st = make_qbuf(e, &L.dec_h, R, F))) return st;
-  CK(dalloc(e, &L.rows_d, (size_t)4 + 3 * R));
-  CK(cudaHostAlloc(&L.rows_h, ((size_t)4 + 3 * R) * sizeof(int32_t), cudaHostAllocDefault));
-  std::memset(L.rows_h, 0, ((size_t)4 + 3 * R) * sizeof(int32_t));
+  CK(dalloc(e, &L.rows_d, (size_t)4 + 3 * R));  // zeroed: an empty table
+  CK(dalloc(e, &L.rows_scratch, R));
+  CK(dalloc(e, &L.join_d, (size_t)1 + R));
   CK(dalloc(e, &L.self_row_map, R));
   CK(dalloc(e, &L.step_tokens, R));
   CK(dalloc(e, &L.eos_mask, R));
   CK(dalloc(e, &L.done, R));
   CK(dalloc(e, &L.best, R));
-  CK(cudaHostAlloc(&L.h_step_tokens, (size_t)R * sizeof(int32_t), cudaHostAllocDefault));
-  CK(cudaHostAlloc(&L.h_done, (size_t)R, cudaHostAllocDefault));
+  for (int i = 0; i < kStepDepth; ++i) {
+    CK(cudaHostAlloc(&L.join_h[i], ((size_t)1 + R) * sizeof(int32_t), cudaHostAllocDefault));
+    std::memset(L.join_h[i], 0, ((size_t)1 + R) * sizeof(int32_t));
+    CK(cudaHostAlloc(&L.h_step_tokens[i], (size_t)R * sizeof(int32_t), cudaHostAllocDefault));
+    CK(cudaHostAlloc(&L.h_done[i], (size_t)R, cudaHostAllocDefault));
+    CK(cudaHostAlloc(&L.h_status[i], sizeof(uint32_t), cudaHostAllocDefault));
+    *L.h_status[i] = 0;
+    CK(cudaEventCreateWithFlags(&L.step_done[i], cudaEventDisableTiming));
+  }
   return MC_OK;
 }
 
@@ -870,7 +958,7 @@ void finish_request(mc_engine* e, Request* r) {
 
 // Drops every queued and in-flight request (after a failed step).  Waits for
 // every lane's work first: their kernels may still read the slots and pages
-// released here.
+// released here.  The lanes' device row tables are emptied.
 void abort_all(mc_engine* e) {
   for (Lane& L : e->lanes) {
     cudaStreamSynchronize(L.stream);
@@ -882,28 +970,39 @@ void abort_all(mc_engine* e) {
       e->event_pool.push_back(r.b);
     }
     L.prof_pending.clear();
-    L.launched = 0;
+    timeline_drop(e, L);
+    if (L.rows_d) {
+      cudaMemsetAsync(L.rows_d, 0, sizeof(int32_t), L.stream);
+      cudaStreamSynchronize(L.stream);
+    }
   }
   for (Request* r : e->queue) delete r;
   e->queue.clear();
-  for (Lane& L : e->lanes) {
-    for (auto* list : {&L.active, &L.pending}) {
-      for (int s : *list) {
-        Request* r = e->slot_req[s];
-        if (r) {
-          release_slot(e, r);
-          delete r;
-        }
+  auto drop = [e](std::vector<int32_t>& list) {
+    for (int s : list) {
+      Request* r = e->slot_req[s];
+      if (r) {
+        release_slot(e, r);
+        delete r;
       }
-      list->clear();
     }
+    list.clear();
+  };
+  for (Lane& L : e->lanes) {
+    drop(L.active);
+    drop(L.ready);
+    drop(L.pending);
+    for (StepInFlight& F : L.inflight) drop(F.joins);
+    L.inflight.clear();
   }
 }
 
-mc_status check_status(mc_engine* e, Lane& L) {
-  const uint32_t bits = *L.h_status;
+// The status bits one completed step read back (its own kernels' and,
+// since the word is only cleared here, any earlier ones').
+mc_status check_status(mc_engine* e, Lane& L, int parity) {
+  const uint32_t bits = *L.h_status[parity];
   if (!bits) return MC_OK;
-  *L.h_status = 0;
+  for (int i = 0; i < kStepDepth; ++i) *L.h_status[i] = 0;
   CK(cudaMemsetAsync(L.d_status, 0, sizeof(uint32_t), L.stream));
   CK(cudaStreamSynchronize(L.stream));
   abort_all(e);
@@ -918,6 +1017,14 @@ mc_status check_status(mc_engine* e, Lane& L) {
   return fail(e, MC_INFERENCE, "activation contains a non-finite value");
 }
 
+// Rows of lane L occupying slots: applied, joined or waiting to join, in
+// enqueued steps, or waiting for their encoder pass.
+size_t lane_rows(const Lane& L) {
+  size_t n = L.active.size() + L.ready.size() + L.pending.size();
+  for (const StepInFlight& F : L.inflight) n += F.joins.size();
+  return n;
+}
+
 // Admits queued requests into free slots of lane L and enqueues one packed
 // encoder pass for them on the lane's encoder stream, which runs alongside
 // the lane's decode steps; the admitted slots wait in L.pending until the
@@ -930,7 +1037,7 @@ mc_status admit(mc_engine* e, Lane& L, int cap) {
   int T = 0;
   const int pt = e->page_tokens;
   const int pps = e->pages_per_slot;
-  const int used = (int)(L.active.size() + L.pending.size());
+  const int used = (int)lane_rows(L);
   const size_t room = cap > used ? (size_t)(cap - used) : 0;
   const size_t avail = std::min(room, e->free_slots.size());
   // Admission granularity: an encoder pass over a handful of sources costs
@@ -938,8 +1045,8 @@ mc_status admit(mc_engine* e, Lane& L, int cap) {
   // eighth of the lane is free -- unless the lane is idle or the whole
   // queue fits (which keeps latency low under light load).
   if (avail == 0 || e->queue.empty()) return MC_OK;
-  if (!L.active.empty() && avail < (size_t)std::max(1, cap / 8) && e->queue.size() > avail)
-    return MC_OK;
+  const bool decoding = !L.active.empty() || !L.ready.empty() || !L.inflight.empty();
+  if (decoding && avail < (size_t)std::max(1, cap / 8) && e->queue.size() > avail) return MC_OK;
   std::vector<Request*> admitted;
   while (!e->queue.empty() && admitted.size() < avail) {
     Request* r = e->queue.front();
@@ -1036,9 +1143,10 @@ mc_status admit(mc_engine* e, Lane& L, int cap) {
   return MC_OK;
 }
 
-// Moves the slots of lane L's completed admission into its active rows and
-// orders the lane's decode stream after the encoder pass.  With wait =
-// false an encoder pass still running is left pending.
+// Moves the slots of lane L's completed admission to its ready list (the
+// next step's row table appends them) and orders the lane's decode stream
+// after the encoder pass.  With wait = false an encoder pass still running
+// is left pending.
 mc_status join_pending(mc_engine* e, Lane& L, bool wait) {
   if (!L.enc_in_flight) return MC_OK;
   if (wait) {
@@ -1049,68 +1157,50 @@ mc_status join_pending(mc_engine* e, Lane& L, bool wait) {
     CK(q);
   }
   CK(cudaStreamWaitEvent(L.stream, L.enc_done, 0));
-  L.active.insert(L.active.end(), L.pending.begin(), L.pending.end());
+  L.ready.insert(L.ready.end(), L.pending.begin(), L.pending.end());
   L.pending.clear();
   L.enc_in_flight = false;
   return MC_OK;
 }
 
-// Row orders for the decode attention launches: rows with the most keys
-// first (counting sort; self keys = step + 1, cross keys = source length).
-void build_row_orders(mc_engine* e, const Lane& L, int32_t* order_self, int32_t* order_cross) {
-  const int R = (int)L.active.size();
-  int count_s[kMaxSeq + 2] = {0}, count_c[kMaxSeq + 2] = {0};
-  std::vector<int> ks(R), kc(R);
-  for (int r = 0; r < R; ++r) {
-    const Request* q = e->slot_req[L.active[r]];
-    ks[r] = std::min<int>(kMaxSeq + 1, (int)q->output.size() + 1);
-    kc[r] = std::min<int>(kMaxSeq + 1, (int)q->tokens.size());
-    ++count_s[kMaxSeq + 1 - ks[r]];
-    ++count_c[kMaxSeq + 1 - kc[r]];
-  }
-  for (int i = 1; i < kMaxSeq + 2; ++i) {
-    count_s[i] += count_s[i - 1];
-    count_c[i] += count_c[i - 1];
-  }
-  for (int r = R - 1; r >= 0; --r) {
-    order_self[--count_s[kMaxSeq + 1 - ks[r]]] = r;
-    order_cross[--count_c[kMaxSeq + 1 - kc[r]]] = r;
-  }
-}
-
 // The device work of one decode step of lane L, grids sized for `cap` rows:
-// the rows block upload, the step's kernels, and the read-back of `cap`
-// tokens, finished flags and the status word.
-mc_status enqueue_step(mc_engine* e, Lane& L, int cap) {
+// the join block upload, the row table (launch_step_rows), the step's
+// kernels, and the read-back of `cap` tokens, finished flags and the status
+// word into the parity's pinned buffers.
+mc_status enqueue_step(mc_engine* e, Lane& L, int cap, int parity, const std::vector<int32_t>& rows) {
   cudaStream_t s = L.stream;
-  CK(cudaMemcpyAsync(L.rows_d, L.rows_h, ((size_t)4 + 3 * e->rmax) * sizeof(int32_t),
+  CK(cudaMemcpyAsync(L.join_d, L.join_h[parity], ((size_t)1 + cap) * sizeof(int32_t),
                      cudaMemcpyHostToDevice, s));
-  mc_status st = run_decode_step(e, L, cap);
+  launch_step_rows(L.rows_d, e->rmax, L.done, L.join_d, e->slot_step, e->slot_src, L.rows_scratch,
+                   L.d_status, s);
+  ++e->launches;
+  mc_status st = run_decode_step(e, L, cap, rows);
   if (st) return st;
-  CK(cudaMemcpyAsync(L.h_step_tokens, L.step_tokens, (size_t)cap * 4, cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(L.h_done, L.done, (size_t)cap, cudaMemcpyDeviceToHost, s));
-  CK(cudaMemcpyAsync(L.h_status, L.d_status, 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(L.h_step_tokens[parity], L.step_tokens, (size_t)cap * 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(L.h_done[parity], L.done, (size_t)cap, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(L.h_status[parity], L.d_status, 4, cudaMemcpyDeviceToHost, s));
   return MC_OK;
 }
 
-// Captures lane L's decode step for L.cap rows as a CUDA graph.  A failed
-// capture is not an error: the lane keeps launching eagerly.
-void capture_step(mc_engine* e, Lane& L) {
-  L.graph_tried = true;
+// Captures lane L's decode step for L.cap rows as a CUDA graph (one per
+// parity: they differ in the pinned buffers).  A failed capture is not an
+// error: the lane keeps launching eagerly.
+void capture_step(mc_engine* e, Lane& L, int parity) {
+  L.graph_tried[parity] = true;
   const std::string saved_error = e->error;
   const bool saved_ready = e->ready;
   const uint64_t launches0 = e->launches;
   cudaGraph_t g = nullptr;
   bool ok = cudaStreamBeginCapture(L.stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
   if (ok) {
-    const mc_status st = enqueue_step(e, L, L.cap);
+    const mc_status st = enqueue_step(e, L, L.cap, parity, {});
     ok = cudaStreamEndCapture(L.stream, &g) == cudaSuccess && st == MC_OK && g != nullptr;
   }
-  if (ok) ok = cudaGraphInstantiate(&L.graph, g, 0) == cudaSuccess;
+  if (ok) ok = cudaGraphInstantiate(&L.graph[parity], g, 0) == cudaSuccess;
   if (g) cudaGraphDestroy(g);
   if (!ok) {
-    if (L.graph) cudaGraphExecDestroy(L.graph);
-    L.graph = nullptr;
+    if (L.graph[parity]) cudaGraphExecDestroy(L.graph[parity]);
+    L.graph[parity] = nullptr;
     cudaGetLastError();
     e->error = saved_error;
     e->ready = saved_ready;
@@ -1119,105 +1209,145 @@ void capture_step(mc_engine* e, Lane& L) {
   e->launches = launches0;
 }
 
-// Launches one decode step over lane L's active rows (asynchronous).
+// Rows the next step of lane L can have at most: those of its newest
+// enqueued step (some may finish in it), or the applied survivors, plus the
+// slots ready to join.
+size_t next_step_bound(const Lane& L) {
+  const size_t base = L.inflight.empty() ? L.active.size() : (size_t)L.inflight.back().rows_bound;
+  return base + L.ready.size();
+}
+
+// Enqueues one decode step of lane L (asynchronous): its row table appends
+// the ready slots.  Grids cover the lane's capacity when the step replays
+// the parity's graph, else the step's row bound.
 mc_status launch_decode(mc_engine* e, Lane& L, bool allow_graph) {
-  const int R = (int)L.active.size();
-  if (R == 0) return MC_OK;
-  int32_t* rs = L.rows_h + 4;
-  L.rows_h[0] = R;
-  std::memcpy(rs, L.active.data(), R * 4);
-  build_row_orders(e, L, rs + e->rmax, rs + 2 * e->rmax);
-  const bool graph_ok = allow_graph && e->use_graphs && !e->profiling && R <= L.cap &&
+  const size_t bound = next_step_bound(L);
+  if (bound == 0) return MC_OK;
+  StepInFlight F;
+  F.parity = L.next_parity;
+  F.rows_bound = (int)bound;
+  F.joins.swap(L.ready);
+  int32_t* jb = L.join_h[F.parity];
+  jb[0] = (int32_t)F.joins.size();
+  if (!F.joins.empty()) std::memcpy(jb + 1, F.joins.data(), F.joins.size() * 4);
+  const bool graph_ok = allow_graph && e->use_graphs && !e->profiling && (int)bound <= L.cap &&
                         L.eager_steps > 0;
-  if (graph_ok && !L.graph_tried) capture_step(e, L);
-  if (graph_ok && L.graph) {
-    CK(cudaGraphLaunch(L.graph, L.stream));
+  if (graph_ok && !L.graph_tried[F.parity]) capture_step(e, L, F.parity);
+  if (e->timeline) {
+    F.tl_start = pooled_event(e);
+    F.tl_end = pooled_event(e);
+    CK(cudaEventRecord(F.tl_start, L.stream));
+  }
+  if (graph_ok && L.graph[F.parity]) {
+    CK(cudaGraphLaunch(L.graph[F.parity], L.stream));
     e->launches += L.graph_kernels;
   } else {
-    mc_status st = enqueue_step(e, L, R);
+    std::vector<int32_t> rows;
+    if (e->profiling && L.inflight.empty()) {  // exact rows for the profile's counts
+      rows = L.active;
+      rows.insert(rows.end(), F.joins.begin(), F.joins.end());
+    }
+    mc_status st = enqueue_step(e, L, (int)bound, F.parity, rows);
     if (st) return st;
     ++L.eager_steps;
   }
-  L.launched = R;
+  if (e->timeline) CK(cudaEventRecord(F.tl_end, L.stream));
+  CK(cudaEventRecord(L.step_done[F.parity], L.stream));
+  L.next_parity = (F.parity + 1) % kStepDepth;
+  L.inflight.push_back(std::move(F));
   return MC_OK;
 }
 
-// Waits for lane L's step in flight and applies its tokens: each row appends
-// its token; finished rows retire and release their slot and pages.
-mc_status complete_lane(mc_engine* e, Lane& L) {
-  if (!L.launched) return MC_OK;
-  const int R = L.launched;
-  L.launched = 0;
-  CK(cudaStreamSynchronize(L.stream));
+// Waits for lane L's oldest enqueued step and applies its tokens: its rows
+// are the applied survivors followed by its joins (the order its row table
+// has on the device); each appends its token, and finished rows retire and
+// release their slot and pages.
+mc_status apply_step(mc_engine* e, Lane& L) {
+  if (L.inflight.empty()) return MC_OK;
+  StepInFlight& F = L.inflight.front();
+  CK(cudaEventSynchronize(L.step_done[F.parity]));
   prof_harvest(e, L);
+  timeline_harvest(e, L, F);
   ++e->steps;
-  mc_status st = check_status(e, L);
+  mc_status st = check_status(e, L, F.parity);
   if (st) return st;
+  const int32_t* tok = L.h_step_tokens[F.parity];
+  const uint8_t* fin = L.h_done[F.parity];
   std::vector<int32_t> keep;
-  keep.reserve(R);
-  for (int r = 0; r < R; ++r) {
-    const int slot = L.active[r];
-    Request* q = e->slot_req[slot];
-    q->output.push_back(L.h_step_tokens[r]);
-    if (L.h_done[r]) finish_request(e, q);
-    else keep.push_back(slot);
-  }
+  keep.reserve(L.active.size() + F.joins.size());
+  int r = 0;
+  for (const std::vector<int32_t>* part : {&L.active, &F.joins})
+    for (int slot : *part) {
+      Request* q = e->slot_req[slot];
+      q->output.push_back(tok[r]);
+      if (fin[r]) finish_request(e, q);
+      else keep.push_back(slot);
+      ++r;
+    }
   L.active.swap(keep);
+  L.inflight.pop_front();
+  if (!L.inflight.empty())  // the next step's rows are now known exactly
+    L.inflight.front().rows_bound = (int)(L.active.size() + L.inflight.front().joins.size());
   return MC_OK;
 }
 
 // Rows admitted to any lane: decoding, or waiting for their encoder pass.
 size_t total_active(const mc_engine* e) {
   size_t n = 0;
-  for (const Lane& L : e->lanes) n += L.active.size() + L.pending.size();
+  for (const Lane& L : e->lanes) n += lane_rows(L);
   return n;
 }
 
-// One scheduler step: each lane in turn completes its step in flight (if
-// any), admits queued requests, and launches its next step.  Lane i's new
-// step runs on the GPU while the host completes lane i+1, so the GPU stays
-// busy across the host's bookkeeping.  With profiling on, lanes run one at a
-// time so the per-kernel times are not shared with another lane.
+// One scheduler step.  Each lane in turn: applies its oldest step once
+// kStepDepth are enqueued (so the next step, already on the GPU, runs while
+// the host applies tokens and retires rows), joins a completed admission,
+// enqueues its next step, then admits queued requests (that host work and
+// the encoder pass overlap the decode steps).  An idle lane admits first and
+// waits for the encoder pass.  With profiling on, each step is applied as
+// soon as it is enqueued, so the per-kernel times are not shared with
+// another step or lane.
 mc_status engine_step(mc_engine* e) {
   if (!e->loaded) return fail(e, MC_MODEL, "no model loaded");
   if (!e->ready) return fail(e, MC_INFERENCE, "engine is not ready after a device failure");
   mc_status st = set_device(e);
   if (st) return st;
+  const size_t depth = e->profiling ? 1 : kStepDepth;
   for (Lane& L : e->lanes) {
-    if ((st = complete_lane(e, L))) return st;
-    // a finished encoder pass joins now; with nothing to decode, wait for it
-    if ((st = join_pending(e, L, L.active.empty()))) {
+    while (L.inflight.size() >= depth)
+      if ((st = apply_step(e, L))) return st;
+    if ((st = join_pending(e, L, false))) {
       abort_all(e);
       return st;
     }
-    if (L.active.empty()) {
+    bool admitted = false;
+    if (next_step_bound(L) == 0 && L.inflight.empty()) {
       // idle lane: admit, wait for the encoder pass, then decode its rows
       st = admit(e, L, L.cap);
-      if (!st && L.active.empty()) st = join_pending(e, L, true);
-      if (!st) st = launch_decode(e, L, true);
-    } else {
-      // The step is launched before the admission: the admission's host
-      // work (packing the sources, enqueueing the encoder pass on the
-      // encoder stream) then overlaps the step on the GPU.  Its rows join
-      // at a later step either way, once the encoder pass has completed.
-      st = launch_decode(e, L, true);
-      if (!st) st = admit(e, L, L.cap);
+      if (!st) st = join_pending(e, L, true);
+      admitted = true;
     }
+    if (!st) {
+      if (next_step_bound(L) > 0) st = launch_decode(e, L, true);
+      else st = apply_step(e, L);  // nothing to enqueue behind the last step
+    }
+    if (!st && !admitted) st = admit(e, L, L.cap);
     if (st) {
       abort_all(e);
       return st;
     }
-    if (e->profiling && (st = complete_lane(e, L))) return st;
+    while (e->profiling && !L.inflight.empty())
+      if ((st = apply_step(e, L))) return st;
   }
   return MC_OK;
 }
 
-// Completes every lane's step in flight (used before returning results that
+// Applies every lane's enqueued steps (used before returning results that
 // must be whole).
 mc_status drain_lanes(mc_engine* e) {
   mc_status st;
   for (Lane& L : e->lanes)
-    if ((st = complete_lane(e, L))) return st;
+    while (!L.inflight.empty())
+      if ((st = apply_step(e, L))) return st;
   return MC_OK;
 }
 
@@ -1582,7 +1712,7 @@ extern "C" mc_status mc_trace_first_step(mc_engine* e, const int32_t* tokens, si
     abort_all(e);
     return st;
   }
-  if (L.active.size() != batch) {
+  if (L.ready.size() != batch) {
     abort_all(e);
     return fail(e, MC_INVALID_INPUT, "trace batch does not fit the free slots or pages");
   }
@@ -1597,7 +1727,7 @@ extern "C" mc_status mc_trace_first_step(mc_engine* e, const int32_t* tokens, si
   }
   for (int l = 0; l < e->dec_layers && (cross_key || cross_value); ++l)
     for (uint32_t b = 0; b < batch; ++b) {
-      const Request* r = e->slot_req[L.active[b]];
+      const Request* r = e->slot_req[L.ready[b]];
       for (uint32_t i = 0; i < offsets[b + 1] - offsets[b]; ++i) {
         const size_t row = (size_t)r->cross_pages[i / e->page_tokens] * e->page_tokens + i % e->page_tokens;
         const size_t dst = (((size_t)l * batch + b) * lmax + i) * d;
@@ -1611,10 +1741,9 @@ extern "C" mc_status mc_trace_first_step(mc_engine* e, const int32_t* tokens, si
     abort_all(e);
     return st;
   }
-  L.launched = 0;
   CK(cudaStreamSynchronize(L.stream));
   prof_harvest(e, L);
-  if ((st = check_status(e, L))) return st;
+  if ((st = check_status(e, L, L.inflight.front().parity))) return st;
   if (decoder_state)
     CK(cudaMemcpy(decoder_state, L.last_state, (size_t)batch * row_bytes, cudaMemcpyDeviceToHost));
   abort_all(e);
@@ -1678,6 +1807,7 @@ extern "C" mc_status mc_load_shortlist(mc_engine* e, const uint8_t* bytes, size_
     return fail(e, MC_INVALID_INPUT, "engine has requests in flight");
   mc_status st = set_device(e);
   if (st) return st;
+  if ((st = drain_lanes(e))) return st;  // no step may run with the graphs replaced below
   if (!bytes) {  // back to the full vocabulary
     e->has_shortlist = false;
   } else {
@@ -1706,9 +1836,11 @@ extern "C" mc_status mc_load_shortlist(mc_engine* e, const uint8_t* bytes, size_
   }
   // the decode graphs captured so far bake the vocabulary launch's arguments
   for (Lane& L : e->lanes) {
-    if (L.graph) cudaGraphExecDestroy(L.graph);
-    L.graph = nullptr;
-    L.graph_tried = false;
+    for (int i = 0; i < kStepDepth; ++i) {
+      if (L.graph[i]) cudaGraphExecDestroy(L.graph[i]);
+      L.graph[i] = nullptr;
+      L.graph_tried[i] = false;
+    }
     L.eager_steps = 0;
   }
   return MC_OK;
@@ -1739,3 +1871,24 @@ extern "C" mc_status mc_profile_read(const mc_engine* e, int32_t kind, uint64_t*
 }
 
 extern "C" uint64_t mc_launch_count(const mc_engine* e) { return e ? e->launches : 0; }
+
+extern "C" mc_status mc_timeline(mc_engine* e, int32_t enable) {
+  if (!e) return MC_INVALID_INPUT;
+  for (Lane& L : e->lanes) {
+    cudaStreamSynchronize(L.stream);
+    timeline_drop(e, L);
+  }
+  e->timeline = enable != 0;
+  e->tl_steps = 0;
+  e->tl_busy_ms = e->tl_gap_ms = 0.0;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_timeline_read(const mc_engine* e, uint64_t* steps, double* busy_ms,
+                                      double* idle_ms) {
+  if (!e) return MC_INVALID_INPUT;
+  if (steps) *steps = e->tl_steps;
+  if (busy_ms) *busy_ms = e->tl_busy_ms;
+  if (idle_ms) *idle_ms = e->tl_gap_ms;
+  return MC_OK;
+}

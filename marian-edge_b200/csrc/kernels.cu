@@ -842,6 +842,133 @@ __global__ void finalize_kernel(int cap, const int32_t* __restrict__ rows_dev,
   done[r] = (token == 0 || t + 1 >= slot_limit[slot]) ? 1 : 0;
 }
 
+// ---- decode-step row table (the batcher's per-step retire and admit) ------------
+// One CTA builds the table a decode step runs over, on the device, so the
+// host can enqueue the next step before it has read the previous one's
+// tokens.  The table (see launch_step_rows) holds the previous step's rows;
+// their finished flags are that step's `done`.  The survivors keep their
+// order (a stable compaction: block-wide scan over chunks of 1,024 rows,
+// staged in `scratch`), the admitted slots listed in the join block are
+// appended, and the two attention orders -- most keys first, self keys =
+// step + 1, cross keys = source length -- are rebuilt by counting sort.
+// The host mirrors the same compaction, so row r of the table is its row r.
+constexpr int kRowsThreads = 1024;
+
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = warp_sums[lane];
+    int s = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    warp_sums[lane] = s - w;
+    if (lane == 31) *total = s;
+  }
+  __syncthreads();
+  return warp_sums[warp] + x - v;
+}
+
+__device__ __forceinline__ void row_keys(const int32_t* slot_step, const int32_t* slot_src, int s, int* bs,
+                                         int* bc) {
+  const int ks = min(kMaxSeq + 1, max(0, slot_step[s] + 1));
+  const int kc = min(kMaxSeq + 1, max(0, slot_src[s]));
+  *bs = kMaxSeq + 1 - ks;  // bin 0 = most keys
+  *bc = kMaxSeq + 1 - kc;
+}
+
+__global__ void __launch_bounds__(kRowsThreads) step_rows_kernel(
+    int32_t* __restrict__ table, int rmax, const uint8_t* __restrict__ done,
+    const int32_t* __restrict__ join, const int32_t* __restrict__ slot_step,
+    const int32_t* __restrict__ slot_src, int32_t* __restrict__ scratch, uint32_t* status) {
+  constexpr int kBins = kMaxSeq + 2;
+  __shared__ int warp_sums[32];
+  __shared__ int s_total;
+  __shared__ int hist[2][kBins];
+  pdl_enter();
+  const int tid = threadIdx.x;
+  int32_t* row_slot = table + 4;
+  int32_t* ord_self = row_slot + rmax;
+  int32_t* ord_cross = ord_self + rmax;
+  const int r0 = min(max(table[0], 0), rmax);
+  for (int i = tid; i < 2 * kBins; i += kRowsThreads) (&hist[0][0])[i] = 0;
+  int base = 0;
+  for (int c0 = 0; c0 < r0; c0 += kRowsThreads) {
+    const int r = c0 + tid;
+    const int keep = (r < r0 && done[r] == 0) ? 1 : 0;
+    const int slot = keep ? row_slot[r] : 0;
+    const int pos = base + block_exclusive_scan(keep, warp_sums, &s_total);
+    if (keep) scratch[pos] = slot;
+    base += s_total;
+    __syncthreads();  // warp_sums and s_total are reused by the next chunk
+  }
+  int nj = join[0];
+  if (nj < 0 || nj > rmax - base) {
+    if (tid == 0) flag_status(status, kStatusBadIndex);
+    nj = max(0, min(nj, rmax - base));
+  }
+  for (int i = tid; i < nj; i += kRowsThreads) scratch[base + i] = join[1 + i];
+  const int r1 = base + nj;
+  __syncthreads();
+  for (int r = tid; r < r1; r += kRowsThreads) {
+    int s = scratch[r];
+    if (s < 0 || s >= rmax) {
+      flag_status(status, kStatusBadIndex);
+      s = 0;
+      scratch[r] = 0;
+    }
+    int bs, bc;
+    row_keys(slot_step, slot_src, s, &bs, &bc);
+    atomicAdd(&hist[0][bs], 1);
+    atomicAdd(&hist[1][bc], 1);
+  }
+  __syncthreads();
+  if (tid < 64) {  // warp 0 scans the self histogram, warp 1 the cross one
+    int* h = hist[tid >> 5];
+    const int lane = tid & 31;
+    constexpr int kPer = (kBins + 31) / 32;
+    int local[kPer];
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int b = lane * kPer + i;
+      local[i] = sum;
+      sum += b < kBins ? h[b] : 0;
+    }
+    int x = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int b = lane * kPer + i;
+      if (b < kBins) h[b] = x - sum + local[i];
+    }
+  }
+  __syncthreads();
+  for (int r = tid; r < r1; r += kRowsThreads) {
+    const int s = scratch[r];
+    int bs, bc;
+    row_keys(slot_step, slot_src, s, &bs, &bc);
+    ord_self[atomicAdd(&hist[0][bs], 1)] = r;
+    ord_cross[atomicAdd(&hist[1][bc], 1)] = r;
+    row_slot[r] = s;
+  }
+  if (tid == 0) table[0] = r1;
+}
+
 __global__ void init_slots_kernel(int n, const int32_t* slots, const int32_t* limits,
                                   const int32_t* force, const int32_t* src_len, int32_t* slot_prev,
                                   int32_t* slot_step, int32_t* slot_limit, int32_t* slot_force,
@@ -1164,6 +1291,13 @@ void launch_shortlist_masks(int n, const int32_t* slots, const int32_t* tokens, 
   const int words = (vocab + 31) / 32;
   launch_pdl(shortlist_mask_kernel, dim3(n), dim3(256), (size_t)words * 4, s, n, slots, tokens, cu,
              offsets, targets, first_num, vocab, words, masks);
+}
+
+void launch_step_rows(int32_t* table, int rmax, const uint8_t* done, const int32_t* join,
+                      const int32_t* slot_step, const int32_t* slot_src, int32_t* scratch,
+                      uint32_t* status, cudaStream_t s) {
+  launch_pdl(step_rows_kernel, dim3(1), dim3(kRowsThreads), 0, s, table, rmax, done, join, slot_step,
+             slot_src, scratch, status);
 }
 
 void launch_init_slots(int n, const int32_t* slots, const int32_t* limits, const int32_t* force,

@@ -104,6 +104,17 @@ void launch_shortlist_masks(int n, const int32_t* slots, const int32_t* tokens, 
                             const int32_t* offsets, const int32_t* targets, int first_num, int vocab,
                             uint32_t* masks, cudaStream_t s);
 
+// The row table of one decode step, built on the device (one CTA):
+// table = [count, 3 unused, row_slot[rmax], order_self[rmax],
+// order_cross[rmax]] holds the previous step's rows on entry; rows whose
+// `done` flag that step set are dropped (the others keep their order), the
+// slots of join = [n, slot...] are appended, and the orders list the rows
+// with the most self keys (step + 1) and cross keys (source length) first.
+// scratch is [rmax] int32.  A bad slot or join count sets kStatusBadIndex.
+void launch_step_rows(int32_t* table, int rmax, const uint8_t* done, const int32_t* join,
+                      const int32_t* slot_step, const int32_t* slot_src, int32_t* scratch,
+                      uint32_t* status, cudaStream_t s);
+
 // Initializes newly admitted slots: prev = -1, step = 0, limit, force_len,
 // source length, SSRU states zeroed (state pools [layers][slots][d]), and
 // copies each slot's page-table rows from page_rows ([n][pages_per_slot]

@@ -1,9 +1,12 @@
 // model_loader.cpp -- Marian binary v1 reader and Q8 schema check (host C++).
 #include "model_loader.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <set>
+
+#include "marian_cuda.h"
 
 namespace mc {
 
@@ -153,6 +156,71 @@ std::string activation_scale(const HostModel& m, const std::string& weight, floa
 
 namespace {
 
+constexpr char kAlphaSuffix[] = "_QuantMultA";
+constexpr char kRowSuffix[] = "_QuantMultRows";
+
+bool ends_with(const std::string& s, const char* suffix) {
+  const size_t n = std::strlen(suffix);
+  return s.size() >= n && s.compare(s.size() - n, n, suffix) == 0;
+}
+
+}  // namespace
+
+std::string validate_q8(const HostModel& m, Q8Inventory* inv) {
+  *inv = Q8Inventory();
+  for (const std::string& name : m.order) {
+    const HostTensor& t = m.tensors.at(name);
+    if (ends_with(name, kAlphaSuffix)) {
+      const std::string weight = name.substr(0, name.size() - std::strlen(kAlphaSuffix));
+      float a;
+      std::string err = activation_scale(m, weight, &a);
+      if (!err.empty()) return err;
+      auto w = m.tensors.find(weight);
+      if (w == m.tensors.end()) return "missing tensor " + weight;
+      if (w->second.type != TensorType::Intgemm8)
+        return name + ": activation scale refers to non-Q8 tensor " + weight;
+      ++inv->activation_scales;
+      continue;
+    }
+    if (ends_with(name, kRowSuffix)) {
+      const std::string weight = name.substr(0, name.size() - std::strlen(kRowSuffix));
+      auto w = m.tensors.find(weight);
+      if (w == m.tensors.end()) return "missing tensor " + weight;
+      if (w->second.type != TensorType::Intgemm8 || ends_with(weight, "_Wemb") || w->second.shape.size() != 2)
+        return name + ": row multipliers refer to a tensor that is not a dense Q8 weight";
+      const int64_t out = w->second.shape[1];
+      const bool shape_ok = (t.shape.size() == 2 && t.shape[0] == 1 && t.shape[1] == out) ||
+                            (t.shape.size() == 1 && t.shape[0] == out);
+      if (t.type != TensorType::Float32 || !shape_ok)
+        return name + ": row multipliers must be float32 [1, " + std::to_string(out) + "]";
+      for (float v : t.f32)
+        if (!std::isfinite(v) || v <= 0.0f) return name + ": row multipliers must be finite and positive";
+      ++inv->row_scaled;
+      continue;
+    }
+    if (t.type != TensorType::Intgemm8) continue;
+    if (t.shape.size() != 2) return name + ": Q8 weight must have rank 2";
+    if (ends_with(name, "_Wemb")) {
+      ++inv->embeddings;
+    } else {
+      float a;
+      std::string err = activation_scale(m, name, &a);
+      if (!err.empty()) return err;
+      ++inv->dense_linears;
+    }
+  }
+  if (inv->dense_linears + inv->embeddings == 0) return "model contains no intgemm8 weight tensors";
+  return "";
+}
+
+std::vector<float> weight_row_mults(const HostModel& m, const std::string& weight) {
+  auto it = m.tensors.find(weight + kRowSuffix);
+  if (it == m.tensors.end()) return {};
+  return it->second.f32;
+}
+
+namespace {
+
 std::string expect_shape(const HostModel& m, const std::string& name, std::vector<int64_t> shape,
                          TensorType type) {
   auto it = m.tensors.find(name);
@@ -222,6 +290,10 @@ std::string validate_schema(HostModel* m) {
   auto dense = [&](const std::string& n, int in, int out, const char* bias) -> std::string {
     add_dense(&expected, n);
     std::string err = expect_shape(*m, n, {in, out}, I8);
+    if (err.empty() && T.count(n + kRowSuffix)) {  // optional per-row multipliers
+      expected.insert(n + kRowSuffix);
+      err = expect_shape(*m, n + kRowSuffix, {1, out}, F32);
+    }
     if (err.empty() && bias) {
       expected.insert(bias);
       err = expect_shape(*m, bias, {1, out}, F32);
@@ -275,7 +347,53 @@ std::string validate_schema(HostModel* m) {
   for (const auto& kv : T)
     if (!expected.count(kv.first)) return "unexpected tensor " + kv.first;
   if (expected.size() != T.size()) return "tensor schema mismatch";
-  return "";
+  Q8Inventory inv;
+  return validate_q8(*m, &inv);
 }
 
 }  // namespace mc
+
+// Host-only inspection of a model file: MarianBinaryModel::parse and
+// validate_q8 (legacy_q8.rs:179-422, 497-542), then the engine's schema
+// check.  No device is touched.
+extern "C" mc_status mc_inspect_marian_bin(const uint8_t* bytes, size_t len, mc_model_report* report,
+                                           char* message, size_t message_capacity) {
+  auto say = [&](const std::string& text) {
+    if (message && message_capacity) {
+      const size_t n = std::min(message_capacity - 1, text.size());
+      std::memcpy(message, text.data(), n);
+      message[n] = 0;
+    }
+  };
+  say("");
+  if (!bytes || !report) return MC_INVALID_INPUT;
+  *report = mc_model_report();
+  mc::HostModel m;
+  std::string err = mc::parse_marian_v1(bytes, len, &m);
+  mc::Q8Inventory inv;
+  if (err.empty()) err = mc::validate_q8(m, &inv);
+  if (!err.empty()) {
+    say(err);
+    return MC_MODEL;
+  }
+  report->tensors = m.order.size();
+  report->dense_linears = inv.dense_linears;
+  report->embeddings = inv.embeddings;
+  report->activation_scales = inv.activation_scales;
+  report->row_scaled_linears = inv.row_scaled;
+  float alpha = 0.0f;
+  if (m.tensors.count("decoder_Wemb_QuantMultA") && mc::activation_scale(m, "decoder_Wemb", &alpha).empty())
+    report->decoder_output_alpha = alpha;
+  const std::string schema = mc::validate_schema(&m);
+  if (schema.empty()) {
+    report->engine_graph = 1;
+    report->decoder_kind = m.decoder_kind;
+    report->dim = m.dim;
+    report->heads = m.heads;
+    report->encoder_layers = m.enc_layers;
+    report->decoder_layers = m.dec_layers;
+  } else {
+    say(schema);  // a valid Q8 file the engine cannot run: why
+  }
+  return MC_OK;
+}

@@ -44,6 +44,22 @@ std::string parse_marian_v1(const uint8_t* data, size_t len, HostModel* out);
 // Resolves the static activation alpha of a Q8 weight (<name>_QuantMultA).
 std::string activation_scale(const HostModel& m, const std::string& weight, float* alpha);
 
+// Q8 inventory of a parsed file (MarianBinaryModel::validate_q8,
+// legacy_q8.rs:497-542): every *_QuantMultA is a valid scalar scale of an
+// intgemm8 weight, every intgemm8 tensor is rank 2, every dense one (not
+// *_Wemb) has its activation scale, and at least one intgemm8 tensor
+// exists.  Also checks the per-row extension: <weight>_QuantMultRows must
+// be a finite, positive float32 [1, out] (or [out]) vector of an intgemm8
+// dense weight whose header shape is [in, out].
+struct Q8Inventory {
+  uint64_t dense_linears = 0, embeddings = 0, activation_scales = 0, row_scaled = 0;
+};
+std::string validate_q8(const HostModel& m, Q8Inventory* inv);
+
+// Per-output-row weight multipliers of a dense Q8 weight (the extension
+// above), or an empty vector when the weight has one multiplier per tensor.
+std::vector<float> weight_row_mults(const HostModel& m, const std::string& weight);
+
 // Infers the graph (dims, layer counts, decoder kind, heads from
 // special:model.yml "transformer-heads") and checks that the tensor set is
 // exactly the schema of that graph (q8_engine.rs:1007-1101) with the expected

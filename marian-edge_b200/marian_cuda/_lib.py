@@ -19,7 +19,7 @@ EXPORTS = [
     "mc_last_error", "mc_is_ready", "mc_translate_token_ids", "mc_submit", "mc_step", "mc_poll",
     "mc_trace_first_step", "mc_stream", "mc_q8_gemm", "mc_op_status", "mc_profile",
     "mc_profile_read", "mc_launch_count", "mc_q8_linear", "mc_q8_linear_noalloc", "mc_load_shortlist",
-    "mc_segment_text",
+    "mc_segment_text", "mc_timeline", "mc_timeline_read", "mc_inspect_marian_bin",
 ]
 
 # MC_Q8_LINEAR_NOALLOC_MAX_ACTIVATIONS in include/marian_cuda.h
@@ -56,6 +56,14 @@ class ModelInfo(C.Structure):
                 ("encoder_layers", C.c_int32), ("decoder_layers", C.c_int32),
                 ("decoder_kind", C.c_int32), ("source_vocab", C.c_int32),
                 ("target_vocab", C.c_int32), ("weight_bytes", C.c_uint64)]
+
+
+class ModelReport(C.Structure):
+    _fields_ = [("tensors", C.c_uint64), ("dense_linears", C.c_uint64), ("embeddings", C.c_uint64),
+                ("activation_scales", C.c_uint64), ("row_scaled_linears", C.c_uint64),
+                ("decoder_output_alpha", C.c_float), ("engine_graph", C.c_int32),
+                ("decoder_kind", C.c_int32), ("dim", C.c_int32), ("heads", C.c_int32),
+                ("encoder_layers", C.c_int32), ("decoder_layers", C.c_int32)]
 
 
 class MarianCudaError(RuntimeError):
@@ -110,6 +118,9 @@ def load(build_if_missing: bool = True):
     lib.mc_load_shortlist.argtypes = [vp, C.c_char_p, sz]
     lib.mc_segment_text.argtypes = [C.c_char_p, sz, u64, PIECE_COUNT_FN, vp, C.POINTER(TextSegment), sz,
                                     C.POINTER(sz), C.POINTER(SegmentError)]
+    lib.mc_timeline.argtypes = [vp, i32]
+    lib.mc_timeline_read.argtypes = [vp, C.POINTER(u64), C.POINTER(C.c_double), C.POINTER(C.c_double)]
+    lib.mc_inspect_marian_bin.argtypes = [C.c_char_p, sz, C.POINTER(ModelReport), C.c_char_p, sz]
     lib.mc_launch_count.argtypes = [vp]
     lib.mc_launch_count.restype = u64
     _lib = lib

@@ -81,13 +81,18 @@ def _zero_sum_rows(values):
     return np.clip(v, -127, 127).astype(np.int8)
 
 
-def _dense(tensors, rng, name, in_dim, out_dim, bias_name=None):
+def _dense(tensors, rng, name, in_dim, out_dim, bias_name=None, per_row=False):
     gain = _BRANCH_GAIN if name.endswith(("_Wo", "_W2")) else 1.0
     w, qm = _q8_weight(rng, out_dim, in_dim, gain)
     if _ZERO_SUM and name.endswith("_W2"):
         w = _zero_sum_rows(w)
     tensors.append(mb.q8(name, w, qm, (in_dim, out_dim)))
     tensors.append(mb.f32(name + "_QuantMultA", [_alpha(rng)], (1, 1)))
+    if per_row:
+        # per-output-row multipliers (the loader's _QuantMultRows extension):
+        # row n's real weights are w[n] / mult[n]
+        mult = (qm * rng.uniform(0.5, 2.0, out_dim)).astype(np.float32)
+        tensors.append(mb.f32(name + "_QuantMultRows", mult, (1, out_dim)))
     if bias_name:
         tensors.append(mb.f32(bias_name, rng.uniform(-0.1, 0.1, out_dim), (1, out_dim)))
 
@@ -97,20 +102,24 @@ def _ln(tensors, rng, prefix, dim):
     tensors.append(mb.f32(prefix + "_bias", rng.uniform(-0.1, 0.1, dim), (1, dim)))
 
 
-def _attention(tensors, rng, prefix, d):
+def _attention(tensors, rng, prefix, d, per_row=False):
     for w, b in (("Wq", "bq"), ("Wk", "bk"), ("Wv", "bv"), ("Wo", "bo")):
-        _dense(tensors, rng, f"{prefix}_{w}", d, d, f"{prefix}_{b}")
+        _dense(tensors, rng, f"{prefix}_{w}", d, d, f"{prefix}_{b}", per_row)
     _ln(tensors, rng, f"{prefix}_Wo_ln", d)
 
 
-def _ffn(tensors, rng, prefix, d, f):
-    _dense(tensors, rng, f"{prefix}_W1", d, f, f"{prefix}_b1")
-    _dense(tensors, rng, f"{prefix}_W2", f, d, f"{prefix}_b2")
+def _ffn(tensors, rng, prefix, d, f, per_row=False):
+    _dense(tensors, rng, f"{prefix}_W1", d, f, f"{prefix}_b1", per_row)
+    _dense(tensors, rng, f"{prefix}_W2", f, d, f"{prefix}_b2", per_row)
     _ln(tensors, rng, f"{prefix}_ffn_ln", d)
 
 
-def synthetic_model(shape: ModelShape, seed: int = 0) -> bytes:
-    """Random-init Q8 model of the given shape, as Marian binary v1 bytes."""
+def synthetic_model(shape: ModelShape, seed: int = 0, per_row: bool = False) -> bytes:
+    """Random-init Q8 model of the given shape, as Marian binary v1 bytes.
+
+    per_row: every dense linear also carries per-output-row weight
+    multipliers (``<W>_QuantMultRows``, the per-row scale extension);
+    embeddings keep their per-tensor multiplier."""
     rng = np.random.Generator(np.random.PCG64(seed))
     d, f, v = shape.dim, shape.ffn, shape.vocab
     t: list = []
@@ -125,18 +134,18 @@ def synthetic_model(shape: ModelShape, seed: int = 0) -> bytes:
            f"max-length-factor: {shape.max_length_factor}\n").encode()
     t.append(mb.raw_int8("special:model.yml", yml))
     for layer in range(1, shape.encoder_layers + 1):
-        _attention(t, rng, f"encoder_l{layer}_self", d)
-        _ffn(t, rng, f"encoder_l{layer}_ffn", d, f)
+        _attention(t, rng, f"encoder_l{layer}_self", d, per_row)
+        _ffn(t, rng, f"encoder_l{layer}_ffn", d, f, per_row)
     for layer in range(1, shape.decoder_layers + 1):
         if shape.decoder_kind == "ssru":
             p = f"decoder_l{layer}_rnn"
-            _dense(t, rng, p + "_W", d, d, None)
-            _dense(t, rng, p + "_Wf", d, d, p + "_bf")
+            _dense(t, rng, p + "_W", d, d, None, per_row)
+            _dense(t, rng, p + "_Wf", d, d, p + "_bf", per_row)
             _ln(t, rng, p + "_ffn_ln", d)
         else:
-            _attention(t, rng, f"decoder_l{layer}_self", d)
-        _attention(t, rng, f"decoder_l{layer}_context", d)
-        _ffn(t, rng, f"decoder_l{layer}_ffn", d, f)
+            _attention(t, rng, f"decoder_l{layer}_self", d, per_row)
+        _attention(t, rng, f"decoder_l{layer}_context", d, per_row)
+        _ffn(t, rng, f"decoder_l{layer}_ffn", d, f, per_row)
     return mb.write(t)
 
 

@@ -33,7 +33,7 @@ def build(force=False):
 class Linear(C.Structure):
     _fields_ = [("weights", C.c_void_p), ("activation_mult", C.c_float),
                 ("weight_mult", C.c_float), ("bias", C.c_void_p),
-                ("in_dim", C.c_int32), ("out_dim", C.c_int32)]
+                ("in_dim", C.c_int32), ("out_dim", C.c_int32), ("weight_row_mults", C.c_void_p)]
 
 
 class AttentionBlock(C.Structure):
@@ -145,11 +145,13 @@ def epilogue(acc, col_scale, bias=None, row_scale=None, relu=False, residual=Non
     return out
 
 
-def make_linear(weights, activation_mult, weight_mult, bias=None):
+def make_linear(weights, activation_mult, weight_mult, bias=None, row_mults=None):
     w = np.ascontiguousarray(weights, dtype=np.int8)
     b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
-    lin = Linear(w.ctypes.data, float(activation_mult), float(weight_mult), _p(b), w.shape[1], w.shape[0])
-    lin._keep = (w, b)
+    rm = None if row_mults is None else np.ascontiguousarray(row_mults, dtype=np.float32)
+    lin = Linear(w.ctypes.data, float(activation_mult), float(weight_mult), _p(b), w.shape[1], w.shape[0],
+                 _p(rm))
+    lin._keep = (w, b, rm)
     return lin
 
 
@@ -351,7 +353,9 @@ class OracleModel:
         in_dim, out_dim = t[wname].shape
         alpha = mb.activation_scale(t, wname)
         b = self._hold(t[bname].data) if bname else None
-        return Linear(self._hold(w), float(alpha), float(qm), b, in_dim, out_dim)
+        rows = t.get(wname + "_QuantMultRows")  # per-row extension
+        rm = self._hold(np.asarray(rows.data, np.float32).reshape(-1)) if rows is not None else None
+        return Linear(self._hold(w), float(alpha), float(qm), b, in_dim, out_dim, rm)
 
     def _attn(self, blk, prefix):
         blk.wq = self._linear(prefix + "_Wq", prefix + "_bq")

@@ -96,7 +96,11 @@ int oq_linear_run(const oq_linear *L, const float *input, size_t rows, float *ou
     for (size_t r = 0; r < rows; ++r)
         for (size_t c = 0; c < n; ++c) {
             float bias = L->bias ? L->bias[c] : 0.0f;
-            output[r * n + c] = (float)acc[r * n + c] * inverse_scale + bias;
+            /* per-row extension: the same formula with row c's multiplier */
+            float scale = L->weight_row_mults
+                              ? 1.0f / (L->activation_mult * L->weight_row_mults[c])
+                              : inverse_scale;
+            output[r * n + c] = (float)acc[r * n + c] * scale + bias;
         }
     free(q);
     free(acc);

@@ -45,6 +45,9 @@ typedef struct {
     const float *bias;          /* [out_dim] or NULL */
     int32_t in_dim;
     int32_t out_dim;
+    /* Per-row extension (not in the reference): one weight multiplier per
+     * output row, replacing weight_mult for row n; NULL = per tensor. */
+    const float *weight_row_mults;
 } oq_linear;
 
 typedef struct {
