@@ -2,23 +2,33 @@
 """Throughput benchmark of the Q8 greedy translation path on B200.
 
 Metric: target tokens/s (greedy, EOS masked until round(1.2 x src) so the work
-is fixed), whole job over all GPUs.  Workload per step: 20,000 requests with
-lognormal(ln 24, 0.8) source lengths clipped to 4..256 tokens (EOS included),
-Zipf(1.1) ids, all queued at once and served by the continuous batcher
-(1024 decode slots, 16-token KV pages) on the benchmark model shape
-(d=512, 8 heads, 6 encoder layers, 2 self+cross-attention decoder layers,
-FFN 2048, vocabulary 32000, random init, seed 0).  Each rank owns a full model
-replica and its own request stream (request-sharded; no collective on the
-data path).
+is fixed), whole job over all GPUs.  Workload per step (BASELINE config 4 as
+a capacity measurement): 20,000 requests with lognormal(ln 24, 0.8) source
+lengths clipped to 4..256 tokens (EOS included), Zipf(1.1) ids, all queued at
+once and served by the continuous batcher (1024 decode slots, 16-token KV
+pages) on the benchmark model shape (d=512, 8 heads, 6 encoder layers, 2
+self+cross-attention decoder layers, FFN 2048, vocabulary 32000, random
+init, seed 0).  Each rank owns a full model replica and its own request
+stream (request-sharded; no collective on the data path).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
 
-`--workload longtext` runs the request-sharded long-text stream instead: per
-step, --docs documents per GPU of 200..2,000 Zipf(1.1) tokens with a
-pseudo-sentence end every 8..64 tokens, split by the library's segment_text
-(marian-core's splitter) into segments of at most 128 tokens with EOS,
-sorted by length and dealt round-robin over the replicas; the same output
-length rule.  The step's batch is built once, before timing.
+The same JSON line also carries, unless --no-configs:
+  * config3_encoder -- config 3: packed encoder passes over 256 lognormal
+    sentences each (mc_encode_token_ids): source tokens/s, encoder attention
+    GB/s and GEMM TOP/s against the measured peaks, and the CPU port's
+    encoder rate;
+  * config5_longtext -- config 5 as strong scaling: one fixed global set of
+    --longtext-docs documents of 200..2,000 Zipf(1.1) tokens with a
+    pseudo-sentence end every 8..64 tokens, split by the library's
+    segment_text into segments of at most 128 tokens with EOS, sorted by
+    length and dealt round-robin over the N replicas;
+  * latency_ms -- config 4's latency: 20,000 requests replayed with Poisson
+    arrivals at 2,000 req/s, and again near capacity, by the library's own
+    arrival loop (mc_replay), p50/p99 from arrival to last token.
+
+`--workload longtext` makes the long-text stream the step workload instead
+(weak scaling: --docs documents per GPU).
 
 The reference arm times the CPU restatement of marian-edge's Q8 engine (the
 Rust reference cannot be built on this image) on the host cores.
@@ -58,8 +68,12 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-latency", action="store_true")
+    p.add_argument("--no-configs", action="store_true", help="skip the config 3 and config 5 lines")
     p.add_argument("--workload", default="stream", choices=["stream", "longtext"])
-    p.add_argument("--docs", type=int, default=500, help="longtext: documents per GPU per step")
+    p.add_argument("--docs", type=int, default=500, help="longtext workload: documents per GPU per step")
+    p.add_argument("--longtext-docs", type=int, default=400, help="config 5: global documents")
+    p.add_argument("--encoder-batches", type=int, default=16, help="config 3: timed 256-sentence passes")
+    p.add_argument("--capacity-rate", type=float, default=40000.0, help="near-capacity arrival rate")
     return p.parse_args()
 
 
@@ -77,7 +91,9 @@ def config_dict(args, world):
                     "by length over %d replica(s), out=round(1.2*src) EOS-masked" % (args.docs, world))
     else:
         workload = ("continuous-batching stream: %d requests/GPU/step, lognormal(ln24,0.8) src "
-                    "4..256 tok, Zipf(1.1) ids, out=round(1.2*src) EOS-masked" % args.requests)
+                    "4..256 tok, Zipf(1.1) ids, out=round(1.2*src) EOS-masked; value is capacity with "
+                    "every request queued at the step's start (config 4's Poisson arrivals are replayed "
+                    "separately in latency_ms)" % args.requests)
     return {"workload": workload,
             "model_shape": args.model, "d_model": W.SHAPES[args.model].dim,
             "decoder": W.SHAPES[args.model].decoder_kind, "max_inflight": args.max_inflight,
@@ -88,8 +104,8 @@ def config_dict(args, world):
 def step_batches(args, rank, count, base_seed, world=1):
     vocab = W.SHAPES[args.model].vocab
     if args.workload == "longtext":
-        # one global document set per call, dealt over the replicas; every
-        # step repeats it (the engine keeps nothing between steps)
+        # one document set per call, dealt over the replicas; every step
+        # repeats it (the engine keeps nothing between steps)
         b = W.longtext_batch(args.docs * world, vocab=vocab, seed=base_seed, rank=rank, world=world)
         return [b] * count
     return [W.stream_batch(n=args.requests, vocab=vocab, seed=base_seed + 7919 * rank + s) for s in range(count)]
@@ -135,21 +151,51 @@ class Clocks:
 
 
 # ---- CPU side (oracle) ---------------------------------------------------------
-def cpu_translate_sample(model_bytes, batches, seconds, threads):
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def host_cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def _oracle():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    return O
+
+
+def cpu_sample(model_bytes, batches, seconds, threads, encoder_only=False):
     """Time the CPU restatement of the reference's Q8 engine on host threads.
 
     Each thread is one engine worker (the reference's worker pool,
     marian-core/src/scheduler.rs:179-226) translating reference-legal batches
-    (B <= 256, B*Lmax^2 <= 65536, marian-cpu/src/backend.rs:223-243) of the
-    same request distribution until the time budget is spent.
+    (B <= 256, B*Lmax^2 <= 65536, first fit, marian-cpu/src/backend.rs:223-243)
+    of the same request distribution until the time budget is spent.  With
+    encoder_only, every row stops after one token (the encoder pass and one
+    decode step); the rate counted is then source tokens.
+    Returns (rate, requests, counted tokens, seconds).
     """
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
+    O = _oracle()
     om = O.OracleModel(model_bytes)
     work = []
     for b in batches:
-        for g in W.legal_cpu_batches(b, max_batch=16):
-            work.append(W.subset(b, g))
+        for g in W.legal_cpu_batches(b):
+            sb = W.subset(b, g)
+            if encoder_only:
+                sb.max_out[:] = 1
+                sb.force_len[:] = 1
+            work.append(sb)
     lock = threading.Lock()
     state = {"next": 0, "tokens": 0, "requests": 0}
     deadline = time.perf_counter() + seconds
@@ -163,8 +209,9 @@ def cpu_translate_sample(model_bytes, batches, seconds, threads):
                 return
             sb = work[i]
             toks, offs = om.translate(sb.tokens, sb.offsets, sb.max_out, sb.force_len)
+            n = int(sb.offsets[-1]) if encoder_only else int(offs[-1])
             with lock:
-                state["tokens"] += int(offs[-1])
+                state["tokens"] += n
                 state["requests"] += sb.size
     t0 = time.perf_counter()
     ts = [threading.Thread(target=worker) for _ in range(threads)]
@@ -176,11 +223,10 @@ def cpu_translate_sample(model_bytes, batches, seconds, threads):
     return state["tokens"] / el, state["requests"], state["tokens"], el
 
 
-def host_threads():
-    try:
-        return len(os.sched_getaffinity(0))
-    except AttributeError:
-        return os.cpu_count() or 1
+def cpu_baseline_obj(rate, reqs, toks, secs, threads, what, unit=UNIT):
+    return {"value": rate, "unit": unit, "cores": threads, "cpu_model": host_cpu_model(), "kind": "port",
+            "sample": f"{reqs} requests ({toks} {what}) in {secs:.1f} s, reference-legal CPU batches "
+                      f"(B<=256, B*Lmax^2<=65536), {threads} worker threads, AVX2 integer GEMM"}
 
 
 # ---- reference arm ---------------------------------------------------------------
@@ -193,11 +239,10 @@ def run_reference(args):
     per_step = max(2.0, args.cpu_seconds / max(1, args.steps))
     batches = step_batches(args, 0, 1, 1000)
     for _ in range(args.warmup):
-        cpu_translate_sample(model_bytes, batches, 0.5, threads)
-    vals, reqs, toks, secs = [], 0, 0, 0.0
+        cpu_sample(model_bytes, batches, 0.5, threads)
+    reqs, toks, secs = 0, 0, 0.0
     for _ in range(args.steps):
-        v, r, t, s = cpu_translate_sample(model_bytes, batches, per_step, threads)
-        vals.append(v)
+        _, r, t, s = cpu_sample(model_bytes, batches, per_step, threads)
         reqs += r
         toks += t
         secs += s
@@ -207,9 +252,7 @@ def run_reference(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "s8xs8->s32, f32",
             "data": "synthetic (seeded random-init model and token streams)",
             "config": config_dict(args, 1),
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"{reqs} requests ({toks} target tokens) of the same stream over "
-                                       f"{secs:.1f} s, reference-legal CPU batches, {threads} worker threads"},
+            "cpu_baseline": cpu_baseline_obj(value, reqs, toks, secs, threads, "target tokens"),
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -227,7 +270,6 @@ def reduce_job(tokens, dev_ms, wall_s, world, device):
     m = torch.tensor([float(dev_ms), float(wall_s)], dtype=torch.float64, device=device)
     dist.all_reduce(m, op=dist.ReduceOp.MAX)
     return float(t.item()), float(m[0].item()), float(m[1].item())
-
 
 
 # DRAM traffic per algorithmic byte, from one ncu --set full capture of each
@@ -253,6 +295,125 @@ def load_peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
+def read_profile(lib, eng, L):
+    prof = {}
+    for k, name in enumerate(L.KERNEL_KINDS):
+        n, ms, fl, by = C.c_uint64(), C.c_double(), C.c_double(), C.c_double()
+        lib.mc_profile_read(eng.handle, k, C.byref(n), C.byref(ms), C.byref(fl), C.byref(by))
+        if n.value:
+            prof[name] = {"launches": n.value, "ms": ms.value, "flops": fl.value, "bytes": by.value}
+    return prof
+
+
+def class_roofline(name, r, peaks, peak_kind):
+    """Roofline object of one kernel class from its profile record."""
+    per_launch_s = r["ms"] / 1000.0 / r["launches"]
+    if name.startswith("gemm"):
+        peak = 2.0 * peaks["bf16_tflops"]  # dense int8 tensor rate = 2 x bf16
+        achieved = r["flops"] / r["launches"] / per_launch_s / 1e12
+        out = {"kernel": name, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
+               "frac": achieved / peak, "peak_source": f"2 x {peak_kind} bf16 dense TFLOP/s (int8 rate is twice bf16)"}
+    else:
+        peak = peaks["hbm_gbs"]
+        achieved = r["bytes"] / r["launches"] / per_launch_s / 1e9
+        out = {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+               "frac": achieved / peak, "peak_source": f"{peak_kind} HBM copy GB/s"}
+    ratio = DRAM_PER_ALGO_BYTE.get(name)
+    out["traffic"] = (ratio * r["bytes"] / r["launches"]) if ratio else None
+    out["traffic_unit"] = "bytes per launch (ncu DRAM bytes per algorithmic byte x algorithmic bytes)"
+    out["algorithmic_bytes_per_launch"] = r["bytes"] / r["launches"]
+    out["avg_launch_us"] = per_launch_s * 1e6
+    return out
+
+
+def measure_encoder(args, eng, lib, L, model_bytes, peaks, peak_kind, rank, world):
+    """Config 3: packed encoder passes over 256 lognormal sentences."""
+    vocab = W.SHAPES[args.model].vocab
+    batches = [W.stream_batch(n=256, vocab=vocab, seed=31000 + 101 * rank + i)
+               for i in range(args.encoder_batches + 3)]
+    for b in batches[:3]:
+        eng.encode_token_ids(b.tokens, b.offsets)
+    lib.mc_profile(eng.handle, 1)
+    eng.encode_token_ids(batches[0].tokens, batches[0].offsets)
+    prof = read_profile(lib, eng, L)
+    lib.mc_profile(eng.handle, 0)
+    timed = batches[3:]
+    src = sum(int(b.offsets[-1]) for b in timed)
+    t0 = time.perf_counter()
+    for b in timed:
+        eng.encode_token_ids(b.tokens, b.offsets)
+    wall = time.perf_counter() - t0
+    out = {"workload": "config 3: %d packed encoder passes of 256 sentences, lognormal(ln24,0.8) src 4..256 "
+                       "tok, Zipf(1.1) ids (mc_encode_token_ids, host buffers in, cross K/V written)"
+                       % len(timed),
+           "value": src / wall, "unit": "source tokens/s", "ms_per_pass": 1000.0 * wall / len(timed),
+           "mean_source_tokens_per_pass": src / len(timed),
+           "device_ms_per_pass_profiled": sum(v["ms"] for v in prof.values()),
+           "kernel_profile": prof}
+    if prof:
+        dom = max(prof.items(), key=lambda kv: kv[1]["ms"])
+        out["roofline"] = class_roofline(dom[0], dom[1], peaks, peak_kind)
+        if "attn_enc" in prof:
+            out["attn_enc"] = class_roofline("attn_enc", prof["attn_enc"], peaks, peak_kind)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = host_threads()
+        v, reqs, toks, secs = cpu_sample(model_bytes, timed[:2], 6.0, threads, encoder_only=True)
+        out["cpu_baseline"] = cpu_baseline_obj(v, reqs, toks, secs, threads,
+                                               "source tokens, encoder + one decode step",
+                                               unit="source tokens/s")
+    return out
+
+
+def measure_longtext(args, eng, stream, model_bytes, rank, world, barrier):
+    """Config 5 as strong scaling: a fixed global document set dealt over
+    the replicas by length bucket."""
+    import torch
+    vocab = W.SHAPES[args.model].vocab
+    batch = W.longtext_batch(args.longtext_docs, vocab=vocab, seed=555, rank=rank, world=world)
+    eng.translate_token_ids(batch.tokens, batch.offsets, batch.max_out, batch.force_len)  # warm
+    torch.cuda.synchronize()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    t0 = time.perf_counter()
+    out, off = eng.translate_token_ids(batch.tokens, batch.offsets, batch.max_out, batch.force_len)
+    end.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    barrier()
+    tokens, max_ms, max_wall = reduce_job(int(off[-1]), start.elapsed_time(end), wall, world, "cuda")
+    res = {"workload": "config 5: %d documents of 200..2000 Zipf(1.1) tokens split by segment_text into "
+                       "segments <= 128 tokens, sorted by length and dealt round-robin over %d replica(s)"
+                       % (args.longtext_docs, world),
+           "scaling": "strong", "value": tokens / (max_ms / 1000.0), "unit": UNIT,
+           "e2e_value": tokens / max_wall, "target_tokens": int(tokens),
+           "segments_this_rank": int(batch.size), "ms": max_ms}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = host_threads()
+        v, reqs, toks, secs = cpu_sample(model_bytes, [batch], 6.0, threads)
+        res["cpu_baseline"] = cpu_baseline_obj(v, reqs, toks, secs, threads, "target tokens")
+    return res
+
+
+def measure_latency(args, eng, n=20000):
+    """Config 4's latency: Poisson arrivals replayed by mc_replay."""
+    vocab = W.SHAPES[args.model].vocab
+    batch = W.stream_batch(n=n, vocab=vocab, seed=4242)
+    out = []
+    for rate in (2000.0, args.capacity_rate):
+        arrivals = W.poisson_arrivals(n, rate, seed=4242)
+        t0 = time.perf_counter()
+        lat = eng.replay(batch.tokens, batch.offsets, batch.max_out, batch.force_len, arrivals) * 1000.0
+        wall = time.perf_counter() - t0
+        lens = np.diff(batch.offsets.astype(np.int64))
+        tokens = int(np.minimum(np.minimum(np.minimum(batch.force_len, batch.max_out), 3 * lens), 256).sum())
+        out.append({"arrival_rate_per_s": rate, "requests": n, "p50": float(np.percentile(lat, 50)),
+                    "p99": float(np.percentile(lat, 99)), "mean": float(lat.mean()),
+                    "served_tokens_per_s": tokens / wall, "wall_s": wall,
+                    "loop": "mc_replay (C++ arrival loop, host clock)"})
+    return out
+
+
 def run_cuda(args):
     import torch
     import torch.distributed as dist
@@ -269,7 +430,6 @@ def run_cuda(args):
     def barrier():
         if world > 1:
             dist.barrier()
-
 
     model_bytes = W.synthetic_model(W.SHAPES[args.model], seed=0)
     eng = CudaEngine(model_bytes, device=local, max_inflight=args.max_inflight, max_encode_tokens=65536,
@@ -289,12 +449,7 @@ def run_cuda(args):
     # kernel-class profile on one extra (untimed) step of the same stream
     lib.mc_profile(eng.handle, 1)
     run(warm[0])
-    prof = {}
-    for k, name in enumerate(L.KERNEL_KINDS):
-        n, ms, fl, by = C.c_uint64(), C.c_double(), C.c_double(), C.c_double()
-        lib.mc_profile_read(eng.handle, k, C.byref(n), C.byref(ms), C.byref(fl), C.byref(by))
-        if n.value:
-            prof[name] = {"launches": n.value, "ms": ms.value, "flops": fl.value, "bytes": by.value}
+    prof = read_profile(lib, eng, L)
     lib.mc_profile(eng.handle, 0)
 
     # decode-stream timeline on one more (untimed) step: each decode step's
@@ -330,42 +485,33 @@ def run_cuda(args):
     launches = lib.mc_launch_count(eng.handle) - launches0
     dev_ms = start.elapsed_time(end)
     all_tokens, max_ms, max_wall = reduce_job(tokens, dev_ms, wall, world, "cuda")
+    peaks, peak_kind = load_peaks()
 
-    latency = None
+    extra = {}
+    if not args.no_configs and args.workload == "stream":
+        # every rank takes part (config 5 is a whole-job measurement)
+        extra["config5_longtext"] = measure_longtext(args, eng, stream, model_bytes, rank, world, barrier)
+        extra["config3_encoder"] = measure_encoder(args, eng, lib, L, model_bytes, peaks, peak_kind, rank,
+                                                   world)
     if not args.no_latency and rank == 0 and args.workload == "stream":
-        latency = poisson_latency(eng, args)
+        extra["latency_ms"] = measure_latency(args, eng)
 
     if rank == 0:
-        peaks, peak_kind = load_peaks()
-        dominant = max(prof.items(), key=lambda kv: kv[1]["ms"]) if prof else None
         roofline = None
-        if dominant:
-            name, r = dominant
-            per_launch_s = r["ms"] / 1000.0 / r["launches"]
-            if name.startswith("gemm"):
-                peak = 2.0 * peaks["bf16_tflops"]  # dense int8 tensor rate = 2 x bf16
-                achieved = r["flops"] / r["launches"] / per_launch_s / 1e12
-                roofline = {"kernel": name, "bound": "tensor", "achieved": achieved, "peak": peak,
-                            "unit": "TOP/s", "frac": achieved / peak,
-                            "peak_source": f"2 x {peak_kind} bf16 dense TFLOP/s (int8 rate is twice bf16)"}
-            else:
-                peak = peaks["hbm_gbs"]
-                achieved = r["bytes"] / r["launches"] / per_launch_s / 1e9
-                roofline = {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": peak,
-                            "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} HBM copy GB/s"}
-            ratio = DRAM_PER_ALGO_BYTE.get(name)
-            roofline["traffic"] = (ratio * r["bytes"] / r["launches"]) if ratio else None
-            roofline["traffic_unit"] = "bytes per launch (ncu DRAM bytes per algorithmic byte x algorithmic bytes)"
-            roofline["algorithmic_bytes_per_launch"] = r["bytes"] / r["launches"]
-            roofline["avg_launch_us"] = per_launch_s * 1e6
+        if prof:
+            name, r = max(prof.items(), key=lambda kv: kv[1]["ms"])
+            roofline = class_roofline(name, r, peaks, peak_kind)
             roofline["share_of_profiled_time"] = r["ms"] / sum(v["ms"] for v in prof.values())
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             threads = host_threads()
-            v, reqs, toks, secs = cpu_translate_sample(model_bytes, timed[:1], args.cpu_seconds, threads)
-            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                   "sample": f"{reqs} requests ({toks} target tokens) of step 0's stream in {secs:.1f} s, "
-                             f"reference-legal CPU batches, {threads} worker threads"}
+            v, reqs, toks, secs = cpu_sample(model_bytes, timed[:1], args.cpu_seconds, threads)
+            cpu = cpu_baseline_obj(v, reqs, toks, secs, threads, "target tokens of step 0's stream")
+        whole = None
+        if prof:  # whole-step fraction: all algorithmic bytes of the profiled step over the timed step time
+            step_bytes = sum(v["bytes"] for v in prof.values())
+            whole = {"algorithmic_bytes_per_step": step_bytes,
+                     "hbm_frac_of_timed_step": step_bytes / (max_ms / args.steps / 1000.0) / 1e9 / peaks["hbm_gbs"]}
         line = {"metric": METRIC, "value": all_tokens / (max_ms / 1000.0), "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -375,39 +521,14 @@ def run_cuda(args):
                 "e2e": {"value": all_tokens / max_wall, "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
                         "d2h_bytes_per_step": d2h // args.steps,
                         "path": "mc_translate_token_ids from host numpy buffers, host wall clock"},
-                "gpu_launches": int(launches), "roofline": roofline, "cpu_baseline": cpu,
+                "gpu_launches": int(launches), "roofline": roofline, "whole_step": whole, "cpu_baseline": cpu,
                 "clocks": clocks.summary(), "kernel_profile": prof, "decode_stream": timeline,
                 "target_tokens": int(all_tokens)}
-        if latency:
-            line["latency_ms"] = latency
+        line.update(extra)
         print(json.dumps(line), flush=True)
     eng.close()
     if world > 1:
         dist.destroy_process_group()
-
-
-def poisson_latency(eng, args, n=4000, rate=2000.0):
-    """p50/p99 request latency (arrival -> last token) for Poisson arrivals."""
-    batch = W.stream_batch(n=n, vocab=W.SHAPES[args.model].vocab, seed=4242)
-    arrivals = W.poisson_arrivals(n, rate, seed=4242)
-    lat = {}
-    t0 = time.perf_counter()
-    nxt = 0
-    while len(lat) < n:
-        now = time.perf_counter() - t0
-        while nxt < n and arrivals[nxt] <= now:
-            s, e = batch.offsets[nxt], batch.offsets[nxt + 1]
-            eng.submit(nxt, batch.tokens[s:e], int(batch.max_out[nxt]), int(batch.force_len[nxt]))
-            nxt += 1
-        active, queued = eng.step()
-        now = time.perf_counter() - t0
-        for rid, _ in eng.poll():
-            lat[rid] = now - arrivals[rid]
-        if active == 0 and queued == 0 and nxt < n:
-            time.sleep(max(0.0, min(0.001, arrivals[nxt] - now)))
-    v = np.array(list(lat.values())) * 1000.0
-    return {"p50": float(np.percentile(v, 50)), "p99": float(np.percentile(v, 99)), "requests": n,
-            "arrival_rate_per_s": rate}
 
 
 def main():

@@ -178,6 +178,28 @@ mc_status mc_trace_first_step(mc_engine *e, const int32_t *tokens, size_t n_toke
                               const uint32_t *offsets, uint32_t batch, float *encoder_output,
                               float *cross_key, float *cross_value, float *decoder_state);
 
+/* Encoder pass only (Q8CpuEngine::encode with the cross-cache fill,
+ * crates/marian-cpu/src/q8_engine.rs:511-574): one packed varlen encoder
+ * pass over a static batch (same input rules as mc_translate_token_ids;
+ * at most max_inflight sentences and max_encode_tokens tokens), its cross
+ * keys/values written into cache pages, then every slot released.
+ * encoder_output (nullable host buffer, packed [n_tokens, dim]) receives
+ * the final encoder states in input order. */
+mc_status mc_encode_token_ids(mc_engine *e, const int32_t *tokens, size_t n_tokens,
+                              const uint32_t *offsets, uint32_t batch, float *encoder_output);
+
+/* Replays an arrival schedule on the calling thread (measurement; the
+ * scheduler worker loop's shape, crates/marian-core/src/scheduler.rs:494-659,
+ * with the host clock as the arrival process): row b of the packed batch is
+ * submitted once arrival_s[b] seconds (ascending) have passed since the
+ * call began, steps run while anything is queued or decoding, and
+ * latency_s[b] receives the seconds from its arrival to the step that
+ * returned its last token.  Generated tokens are dropped.  Requires an idle
+ * engine. */
+mc_status mc_replay(mc_engine *e, const int32_t *tokens, size_t n_tokens, const uint32_t *offsets,
+                    uint32_t batch, const uint32_t *max_output_tokens, const uint32_t *force_len,
+                    const double *arrival_s, double *latency_s);
+
 /* The engine's stream (a cudaStream_t), for callers that time or order work. */
 void *mc_stream(const mc_engine *e);
 

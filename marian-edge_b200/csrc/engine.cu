@@ -17,6 +17,7 @@
 //     kernels of several steps overlap on the GPU.  Weights, slots, page
 //     pools and page tables are shared; lanes use disjoint slots and pages.
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -1684,6 +1685,97 @@ extern "C" mc_status mc_translate_token_ids(mc_engine* e, const int32_t* tokens,
     out_offsets[b + 1] = (uint32_t)used;
   }
   e->finished.clear();
+  return MC_OK;
+}
+
+// Encoder pass only (Q8CpuEngine::encode and the cross-cache fill,
+// q8_engine.rs:511-574): the batch is admitted as one packed encoder pass
+// on lane 0's stream, its cross keys/values are written into cache pages,
+// and every slot is released again without a decode step.
+extern "C" mc_status mc_encode_token_ids(mc_engine* e, const int32_t* tokens, size_t n_tokens,
+                                         const uint32_t* offsets, uint32_t batch,
+                                         float* encoder_output) {
+  if (!e) return MC_INVALID_INPUT;
+  mc_status st = validate_batch(e, tokens, n_tokens, offsets, batch);
+  if (st) return st;
+  if (batch > (uint32_t)e->rmax || n_tokens > (size_t)e->tmax)
+    return fail(e, MC_INVALID_INPUT, "batch exceeds one encoder pass (max_inflight, max_encode_tokens)");
+  if ((st = set_device(e))) return st;
+  Lane& L = e->lanes[0];
+  for (uint32_t b = 0; b < batch; ++b) {
+    Request* r = new Request();
+    r->id = b;
+    r->tokens.assign(tokens + offsets[b], tokens + offsets[b + 1]);
+    r->max_out = kMaxSeq;
+    r->force = 0;
+    e->queue.push_back(r);
+  }
+  if ((st = admit(e, L, e->rmax)) || (st = join_pending(e, L, true))) {
+    abort_all(e);
+    return st;
+  }
+  if (L.ready.size() != batch) {
+    abort_all(e);
+    return fail(e, MC_INVALID_INPUT, "batch does not fit the free slots or pages");
+  }
+  CK(cudaStreamSynchronize(L.stream));
+  prof_harvest(e, L);
+  if (encoder_output)
+    CK(cudaMemcpy(encoder_output, L.enc_x, n_tokens * (size_t)e->d * 4, cudaMemcpyDeviceToHost));
+  abort_all(e);
+  return MC_OK;
+}
+
+// Arrival-schedule replay on the calling thread: request b (the packed
+// batch's row b) is submitted once arrival_s[b] seconds have passed since
+// the call began (arrival_s ascending), mc_step runs while anything is
+// queued or decoding, and latency_s[b] receives the time from its arrival to
+// the step that returned its last token.  The tokens themselves are
+// dropped.  This is the scheduler worker loop's shape
+// (marian-core/src/scheduler.rs:494-659) with the host clock as the
+// arrival process.
+extern "C" mc_status mc_replay(mc_engine* e, const int32_t* tokens, size_t n_tokens,
+                               const uint32_t* offsets, uint32_t batch, const uint32_t* max_out,
+                               const uint32_t* force_len, const double* arrival_s, double* latency_s) {
+  if (!e) return MC_INVALID_INPUT;
+  mc_status st = validate_batch(e, tokens, n_tokens, offsets, batch);
+  if (st) return st;
+  if (!max_out || !arrival_s || !latency_s) return fail(e, MC_INVALID_INPUT, "null replay buffers");
+  for (uint32_t b = 1; b < batch; ++b)
+    if (!(arrival_s[b] >= arrival_s[b - 1])) return fail(e, MC_INVALID_INPUT, "arrivals are not ascending");
+  using clock = std::chrono::steady_clock;
+  const auto t0 = clock::now();
+  auto now = [&]() { return std::chrono::duration<double>(clock::now() - t0).count(); };
+  e->finished.clear();
+  uint32_t next = 0, done = 0;
+  while (done < batch) {
+    double t = now();
+    for (; next < batch && arrival_s[next] <= t; ++next) {
+      Request* r = new Request();
+      r->id = next;
+      r->tokens.assign(tokens + offsets[next], tokens + offsets[next + 1]);
+      r->max_out = max_out[next];
+      r->force = force_len ? force_len[next] : 0;
+      e->queue.push_back(r);
+    }
+    if (e->queue.empty() && total_active(e) == 0) {
+      if (next >= batch) break;
+      while (now() < arrival_s[next]) {
+      }  // idle until the next arrival
+      continue;
+    }
+    if ((st = engine_step(e))) {
+      abort_all(e);
+      e->finished.clear();
+      return st;
+    }
+    t = now();
+    for (const Finished& f : e->finished) {
+      if (f.id < batch) latency_s[f.id] = t - arrival_s[f.id];
+      ++done;
+    }
+    e->finished.clear();
+  }
   return MC_OK;
 }
 

@@ -20,6 +20,7 @@ EXPORTS = [
     "mc_trace_first_step", "mc_stream", "mc_q8_gemm", "mc_op_status", "mc_profile",
     "mc_profile_read", "mc_launch_count", "mc_q8_linear", "mc_q8_linear_noalloc", "mc_load_shortlist",
     "mc_segment_text", "mc_timeline", "mc_timeline_read", "mc_inspect_marian_bin",
+    "mc_encode_token_ids", "mc_replay",
 ]
 
 # MC_Q8_LINEAR_NOALLOC_MAX_ACTIVATIONS in include/marian_cuda.h
@@ -120,6 +121,8 @@ def load(build_if_missing: bool = True):
                                     C.POINTER(sz), C.POINTER(SegmentError)]
     lib.mc_timeline.argtypes = [vp, i32]
     lib.mc_timeline_read.argtypes = [vp, C.POINTER(u64), C.POINTER(C.c_double), C.POINTER(C.c_double)]
+    lib.mc_encode_token_ids.argtypes = [vp, vp, sz, vp, u32, vp]
+    lib.mc_replay.argtypes = [vp, vp, sz, vp, u32, vp, vp, vp, vp]
     lib.mc_inspect_marian_bin.argtypes = [C.c_char_p, sz, C.POINTER(ModelReport), C.c_char_p, sz]
     lib.mc_launch_count.argtypes = [vp]
     lib.mc_launch_count.restype = u64

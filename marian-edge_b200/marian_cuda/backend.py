@@ -134,6 +134,32 @@ class CudaEngine:
             pos += int(lens[i])
         return out
 
+    # -- encoder pass only (Q8CpuEngine::encode, q8_engine.rs:511-574) ----------
+    def encode_token_ids(self, tokens, offsets, want_output: bool = False):
+        """One packed encoder pass over a static batch (cross keys/values
+        written, slots released); returns the packed [tokens, dim] encoder
+        output when want_output."""
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        offsets = np.ascontiguousarray(offsets, dtype=np.uint32)
+        out = np.empty((tokens.size, self.info.dim), np.float32) if want_output else None
+        L.check(self._lib.mc_encode_token_ids(self._h, _ptr(tokens), tokens.size, _ptr(offsets),
+                                              len(offsets) - 1, _ptr(out)), self._h)
+        return out
+
+    # -- arrival-schedule replay (measurement) -----------------------------------
+    def replay(self, tokens, offsets, max_output_tokens, force_len, arrival_s):
+        """Submits row b at arrival_s[b] seconds (host clock) and steps until
+        every request is done; returns each request's latency in seconds."""
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        offsets = np.ascontiguousarray(offsets, dtype=np.uint32)
+        mo = np.ascontiguousarray(max_output_tokens, dtype=np.uint32)
+        fl = None if force_len is None else np.ascontiguousarray(force_len, dtype=np.uint32)
+        arr = np.ascontiguousarray(arrival_s, dtype=np.float64)
+        lat = np.full(len(offsets) - 1, np.nan, np.float64)
+        L.check(self._lib.mc_replay(self._h, _ptr(tokens), tokens.size, _ptr(offsets), len(offsets) - 1,
+                                    _ptr(mo), _ptr(fl), _ptr(arr), _ptr(lat)), self._h)
+        return lat
+
     # -- per-layer capture for parity tests ------------------------------------
     def trace_first_step(self, tokens, offsets):
         tokens = np.ascontiguousarray(tokens, dtype=np.int32)

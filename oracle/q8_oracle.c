@@ -15,6 +15,9 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#ifdef __AVX2__
+#include <immintrin.h>
+#endif
 
 #define ACTIVATION_ZERO_POINT 127
 #define LAYER_NORM_EPSILON 1.0e-6f
@@ -45,9 +48,27 @@ int64_t oq_quantize_u8(const float *input, size_t n, float mult, uint8_t *out) {
 /* Centred activations (q - 127 in [-127, 127]) times int8 weights; rows are
  * blocked by 4 so each weight row is streamed once per block (the integer
  * result is independent of blocking). */
+#ifdef __AVX2__
+static inline int32_t hsum_epi32(__m256i v) {
+    __m128i x = _mm_add_epi32(_mm256_castsi256_si128(v), _mm256_extracti128_si256(v, 1));
+    x = _mm_add_epi32(x, _mm_shuffle_epi32(x, 0x4E));
+    x = _mm_add_epi32(x, _mm_shuffle_epi32(x, 0xB1));
+    return _mm_cvtsi128_si32(x);
+}
+#endif
+
 static int32_t dot_i8(const int16_t *a, const int8_t *w, size_t k) {
     int32_t s = 0;
-    for (size_t i = 0; i < k; ++i) s += (int32_t)a[i] * (int32_t)w[i];
+    size_t i = 0;
+#ifdef __AVX2__
+    __m256i v = _mm256_setzero_si256();
+    for (; i + 16 <= k; i += 16) {
+        const __m256i w16 = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i *)(w + i)));
+        v = _mm256_add_epi32(v, _mm256_madd_epi16(_mm256_loadu_si256((const __m256i *)(a + i)), w16));
+    }
+    s = hsum_epi32(v);
+#endif
+    for (; i < k; ++i) s += (int32_t)a[i] * (int32_t)w[i];
     return s;
 }
 
@@ -57,6 +78,37 @@ void oq_gemm_u8_i8(const uint8_t *a, const int8_t *w, size_t rows, size_t k,
     int16_t *centred = (int16_t *)malloc(((rows * k) > 0 ? rows * k : 1) * sizeof(int16_t));
     for (size_t i = 0; i < rows * k; ++i) centred[i] = (int16_t)((int)a[i] - ACTIVATION_ZERO_POINT);
     size_t r = 0;
+#ifdef __AVX2__
+    /* The exact AVX2 widening scheme of q8_avx2.rs:125-229: 16 weights
+     * widened to i16, vpmaddwd forms exact i32 pair sums of centred
+     * activations times weights (|a| <= 128, |w| <= 127, so no pair sum can
+     * saturate), accumulated in i32 lanes.  Integer addition is associative,
+     * so the result equals the scalar loop's bit for bit. */
+    const size_t k16 = k & ~(size_t)15;
+    for (; r + 4 <= rows; r += 4) {
+        const int16_t *a0 = centred + r * k, *a1 = a0 + k, *a2 = a1 + k, *a3 = a2 + k;
+        for (size_t c = 0; c < n; ++c) {
+            const int8_t *wc = w + c * k;
+            __m256i v0 = _mm256_setzero_si256(), v1 = v0, v2 = v0, v3 = v0;
+            for (size_t i = 0; i < k16; i += 16) {
+                const __m256i w16 = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i *)(wc + i)));
+                v0 = _mm256_add_epi32(v0, _mm256_madd_epi16(_mm256_loadu_si256((const __m256i *)(a0 + i)), w16));
+                v1 = _mm256_add_epi32(v1, _mm256_madd_epi16(_mm256_loadu_si256((const __m256i *)(a1 + i)), w16));
+                v2 = _mm256_add_epi32(v2, _mm256_madd_epi16(_mm256_loadu_si256((const __m256i *)(a2 + i)), w16));
+                v3 = _mm256_add_epi32(v3, _mm256_madd_epi16(_mm256_loadu_si256((const __m256i *)(a3 + i)), w16));
+            }
+            int32_t s[4] = {hsum_epi32(v0), hsum_epi32(v1), hsum_epi32(v2), hsum_epi32(v3)};
+            for (size_t i = k16; i < k; ++i) {
+                const int32_t wv = wc[i];
+                s[0] += (int32_t)a0[i] * wv;
+                s[1] += (int32_t)a1[i] * wv;
+                s[2] += (int32_t)a2[i] * wv;
+                s[3] += (int32_t)a3[i] * wv;
+            }
+            for (int j = 0; j < 4; ++j) acc[(r + j) * n + c] = s[j];
+        }
+    }
+#else
     for (; r + 4 <= rows; r += 4) {
         const int16_t *a0 = centred + r * k, *a1 = a0 + k, *a2 = a1 + k, *a3 = a2 + k;
         for (size_t c = 0; c < n; ++c) {
@@ -75,6 +127,7 @@ void oq_gemm_u8_i8(const uint8_t *a, const int8_t *w, size_t rows, size_t k,
             acc[(r + 3) * n + c] = s3;
         }
     }
+#endif
     for (; r < rows; ++r)
         for (size_t c = 0; c < n; ++c) acc[r * n + c] = dot_i8(centred + r * k, w + c * k, k);
     free(centred);

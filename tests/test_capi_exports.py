@@ -59,3 +59,19 @@ def test_config_validation_rejects_bad_values():
         setattr(c2, field, bad)
         assert lib.mc_create(C.byref(c2), C.byref(h)) == L.MC_INVALID_INPUT, field
         assert not h.value
+
+
+def test_rust_binding_declares_every_header_symbol():
+    # The Rust crate's raw declarations (crates/marian-cuda/src/ffi.rs) cover
+    # the whole C ABI, and nothing the header lacks.
+    ffi = os.path.join(build.ROOT, "crates", "marian-cuda", "src", "ffi.rs")
+    text = open(ffi).read()
+    rust = sorted(set(re.findall(r"pub fn (mc_[a-z0-9_]+)\s*\(", text)))
+    assert rust == declared()
+    # struct layouts: every mc_* struct field of the header appears in the mirror
+    header = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    for name in ("mc_config", "mc_model_info", "mc_model_report", "mc_text_segment"):
+        body = re.search(r"typedef struct \{([^{}]*)\}\s*" + name + ";", header).group(1)
+        fields = re.findall(r"(\w+)\s*(?:,|;)", body)
+        block = re.search(r"pub struct " + name + r" \{(.*?)\}", text, re.S).group(1)
+        assert re.findall(r"pub (\w+):", block) == fields, name

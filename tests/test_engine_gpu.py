@@ -364,3 +364,64 @@ def test_lexical_shortlist_errors_follow_the_reference():
         out, off = eng.translate_token_ids(np.array([4, 0], np.int32), np.array([0, 2], np.uint32),
                                            np.array([4], np.uint32))
         assert off[-1] >= 1
+
+
+@pytest.mark.parametrize("name", ["tiny_self", "tiny_ssru", "graph_b"])
+def test_per_row_weight_multipliers_match_oracle(name):
+    # The per-row extension (<W>_QuantMultRows: one weight multiplier per
+    # output row of every dense linear): the GEMM epilogue takes a
+    # per-column scale 1 / (alpha * mult[n]); tokens, encoder output and
+    # cross keys/values must still equal the oracle's exactly.
+    shape = W.SHAPES[name]
+    mb = W.synthetic_model(shape, seed=5, per_row=True)
+    om = O.OracleModel(mb)
+    full = W.short_batch(n=16, vocab=shape.vocab, seed=4, lo=4, hi=48)
+    with CudaEngine(mb, max_inflight=64, max_encode_tokens=4096) as eng:
+        for g in W.legal_cpu_batches(full):
+            b = W.subset(full, g)
+            ref, ref_off, tr = om.translate(b.tokens, b.offsets, b.max_out, b.force_len, trace=True)
+            got, got_off = eng.translate_token_ids(b.tokens, b.offsets, b.max_out, b.force_len)
+            np.testing.assert_array_equal(got_off, ref_off)
+            np.testing.assert_array_equal(got, ref)
+            gtr = eng.trace_first_step(b.tokens, b.offsets)
+            lens = np.diff(b.offsets.astype(np.int64))
+            valid = np.concatenate([np.arange(l) + j * lens.max() for j, l in enumerate(lens)])
+            np.testing.assert_array_equal(gtr["encoder_output"][valid], tr["encoder_output"][valid])
+            np.testing.assert_array_equal(gtr["cross_key"][:, valid], tr["cross_key"][:, valid])
+
+
+def test_encode_token_ids_matches_oracle_encoder_output():
+    # mc_encode_token_ids: one packed encoder pass (q8_engine.rs:511-574);
+    # the packed output is the oracle's encoder output row for row.
+    name = "graph_r"
+    om = O.OracleModel(model(name))
+    batch = W.stream_batch(n=24, vocab=32000, seed=61)
+    with CudaEngine(model(name), max_inflight=64, max_encode_tokens=8192) as eng:
+        enc = eng.encode_token_ids(batch.tokens, batch.offsets, want_output=True)
+        enc2 = eng.encode_token_ids(batch.tokens, batch.offsets, want_output=True)  # slots were released
+        assert eng.is_ready()
+    np.testing.assert_array_equal(enc, enc2)
+    lens = np.diff(batch.offsets.astype(np.int64))
+    for grp in W.legal_cpu_batches(batch):
+        sb = W.subset(batch, grp)
+        sb.max_out[:] = 1
+        sb.force_len[:] = 1
+        _, _, tr = om.translate(sb.tokens, sb.offsets, sb.max_out, sb.force_len, trace=True)
+        sl = int(max(lens[r] for r in grp))
+        for j, row in enumerate(grp):
+            s, n = int(batch.offsets[row]), int(lens[row])
+            np.testing.assert_array_equal(enc[s:s + n], tr["encoder_output"][j * sl:j * sl + n])
+
+
+def test_replay_serves_every_arrival():
+    # mc_replay: requests arrive on a Poisson clock; every one finishes with
+    # a latency no shorter than its own decode steps need.
+    name = "tiny_self"
+    batch = W.stream_batch(n=200, vocab=512, seed=3)
+    arrivals = W.poisson_arrivals(batch.size, 5000.0, seed=1)
+    with CudaEngine(model(name), max_inflight=32, max_encode_tokens=2048) as eng:
+        lat = eng.replay(batch.tokens, batch.offsets, batch.max_out, batch.force_len, arrivals)
+        assert eng.is_ready()
+        out, off = eng.translate_token_ids(batch.tokens, batch.offsets, batch.max_out, batch.force_len)
+    assert np.isfinite(lat).all() and (lat > 0).all()
+    assert off[-1] > 0
