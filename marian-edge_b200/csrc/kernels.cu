@@ -47,7 +47,7 @@ __global__ void embed_encoder_kernel(const int32_t* __restrict__ tokens,
                                      const int8_t* __restrict__ emb, float emb_mult,
                                      float emb_scale, const float* __restrict__ positions, int d,
                                      float* __restrict__ x, const __grid_constant__ QuantOut q, uint32_t* status) {
-  pdl_enter();
+  pdl_enter_release();
   const int vec_per_row = d >> 2;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)n_tokens * vec_per_row) return;
@@ -77,7 +77,7 @@ __global__ void embed_decoder_kernel(int cap, const int32_t* __restrict__ rows_d
                                      float* __restrict__ x, const __grid_constant__ QuantOut q, uint8_t* eos_mask,
                                      const int32_t* __restrict__ self_pages, int pages_per_slot,
                                      int page_tokens, int32_t* self_row_map, uint32_t* status) {
-  pdl_enter();
+  pdl_enter_release();
   const int rows = launch_rows(rows_dev, cap);
   const int vec_per_row = d >> 2;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kLnThreads) residual_ln_kernel(
   constexpr int d = VPL * 128;
   constexpr int ld = d + 4, kVec = d / 4;
   extern __shared__ __align__(16) float tile[];  // [RPC][d + 4]
-  pdl_enter();
+  pdl_enter_release();
   const int rows = launch_rows(rows_dev, cap);
   const int row0 = blockIdx.x * RPC;
   const int nrows = min(RPC, rows - row0);
@@ -224,7 +224,7 @@ __global__ void __launch_bounds__(kLnThreads) ssru_kernel(
   constexpr int d = VPL * 128;
   constexpr int ld = d + 4, kVec = d / 4;
   extern __shared__ __align__(16) float tile[];
-  pdl_enter();
+  pdl_enter_release();
   const int rows = launch_rows(rows_dev, cap);
   const int row0 = blockIdx.x * RPC;
   const int nrows = min(RPC, rows - row0);
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(kLnWarps * 32) residual_ln_warp_kernel(
     uint32_t* status) {
   constexpr int d = VPL * 128;
   __shared__ __align__(16) float rows_s[kLnWarps][d];
-  pdl_enter();
+  pdl_enter_release();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kLnWarps + warp;
   if (row >= cap) return;
@@ -375,7 +375,7 @@ __global__ void __launch_bounds__(kLnWarps * 32) ssru_warp_kernel(
     uint32_t* status) {
   constexpr int d = VPL * 128;
   __shared__ __align__(16) float rows_s[kLnWarps][d];
-  pdl_enter();
+  pdl_enter_release();
   const int rows = launch_rows(rows_dev, cap);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kLnWarps + warp;
@@ -602,7 +602,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
 
 // Decode: a persistent kernel over work items (active row, group of 4
 // heads), taken in row_order (longest rows first) round-robin by the CTAs.
-// Lane 0 of warp 4 is the producer: for every item it streams the group's
+// Warp 4 is the producer: for every item it streams the group's
 // slices of the cached keys, then of the values, into a 3-slot shared-memory
 // ring, one chunk of 32 keys per slot, with one 3-D TMA copy per 8 cache
 // rows (8 rows x 4 * HD floats of one page, through the pool's tensor map;
@@ -635,19 +635,10 @@ __device__ __forceinline__ void mbar_arrive_cta(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Item -> (row, head group, key count); false for a row whose length fails
-// its bounds check (both roles skip it alike).
-__device__ __forceinline__ bool decode_item(int item, int groups,
-                                            const int32_t* __restrict__ row_order,
-                                            const int32_t* __restrict__ row_slot,
-                                            const int32_t* __restrict__ slot_len, int len_add,
-                                            int limit, int* r, int* g, int* slot, int* len) {
+// Row of work item `item` (items are (row in row_order, head group)).
+__device__ __forceinline__ int item_row(int item, int groups, const int32_t* __restrict__ row_order) {
   const int ro = item / groups;
-  *g = item - ro * groups;
-  *r = row_order ? row_order[ro] : ro;
-  *slot = row_slot[*r];
-  *len = slot_len[*slot] + len_add;
-  return *len > 0 && *len <= limit;
+  return row_order ? row_order[ro] : ro;
 }
 
 // Shared-memory float offset of float f (0 <= f < W) of key t of a chunk
@@ -689,43 +680,60 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
   const int items = launch_rows(rows_dev, cap) * groups;
   const int limit = min(kMaxSeq, pages_per_slot * PT);
   if (warp == kDecGroup) {
-    // ---- producer ---------------------------------------------------------
-    if (lane == 0) {
-      int k = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
-        int r, g, slot, len;
-        if (!decode_item(item, groups, row_order, row_slot, slot_len, len_add, limit, &r, &g, &slot,
-                         &len)) {
-          flag_status(status, kStatusBadIndex);
-          continue;
-        }
-        const int32_t* pages = page_table + (size_t)slot * pages_per_slot;
-        for (int pass = 0; pass < 2 && ok; ++pass) {
-          const CUtensorMap* map = pass == 0 ? &k_map : &v_map;
-          for (int c0 = 0; c0 < len; c0 += kDecChunk, ++k) {
-            const int nb = (min(kDecChunk, len - c0) + 7) / 8;  // 8-row boxes
-            const int sl = k % kDecSlots;
-            if (!(ok = mbar_wait(&empty_bar[sl], ((k / kDecSlots) & 1) ^ 1, status))) break;
+    // ---- producer warp ------------------------------------------------------
+    // All 32 lanes walk the items: an item's page-table row (at most 32
+    // pages: 256 keys of 8-token pages) is fetched by one lane-parallel load,
+    // and the next item's row index is loaded one item ahead, so an item
+    // costs two dependent global round trips (slot, then its length and
+    // pages) instead of one per copied box.  Lane 0 issues the copies.
+    int k = 0;
+    bool ok = true;
+    int item = blockIdx.x;
+    int r_next = item < items ? item_row(item, groups, row_order) : 0;
+    for (; item < items && ok; item += gridDim.x) {
+      const int r = r_next;
+      const int g = item % groups;
+      if (item + (int)gridDim.x < items) r_next = item_row(item + gridDim.x, groups, row_order);
+      const int slot = row_slot[r];
+      const int len = slot_len[slot] + len_add;
+      const int page = lane < pages_per_slot ? page_table[(size_t)slot * pages_per_slot + lane] : 0;
+      if (len <= 0 || len > limit) {
+        if (lane == 0) flag_status(status, kStatusBadIndex);
+        continue;
+      }
+      for (int pass = 0; pass < 2 && ok; ++pass) {
+        const CUtensorMap* map = pass == 0 ? &k_map : &v_map;
+        for (int c0 = 0; c0 < len; c0 += kDecChunk, ++k) {
+          const int nb = (min(kDecChunk, len - c0) + 7) / 8;  // 8-row boxes
+          const int sl = k % kDecSlots;
+          bool free_slot = true;
+          if (lane == 0) free_slot = mbar_wait(&empty_bar[sl], ((k / kDecSlots) & 1) ^ 1, status);
+          if (!(ok = __shfl_sync(0xffffffffu, free_slot, 0))) break;
+          int rows[kDecChunk / 8];  // first cache row of each box (boxes never straddle pages)
+#pragma unroll
+          for (int b = 0; b < kDecChunk / 8; ++b) {
+            const int j = c0 + 8 * b;
+            rows[b] = __shfl_sync(0xffffffffu, page, min(j / PT, 31)) * PT + j % PT;
+          }
+          if (lane == 0) {
             float* dst = dsm + sl * kSlotFloats;
             const uint32_t box_bytes = kBoxFloats * 4, q_bytes = W * 4;
             mbar_arrive_expect_tx(&full_bar[sl], nb * box_bytes + (pass == 0 ? q_bytes : 0));
             if (pass == 0)
               bulk_copy_g2s(dst + (kDecChunk / 8) * kBoxFloats, q + (size_t)r * ldq + g * W, q_bytes,
                             &full_bar[sl]);
-            for (int b = 0; b < nb; ++b) {
-              const int j = c0 + 8 * b;  // first key of the box (boxes never straddle pages)
-              tma_load_3d(dst + b * kBoxFloats, map, 0, pages[j / PT] * PT + j % PT, g * (W / 32),
-                          &full_bar[sl]);
-            }
+            for (int b = 0; b < nb; ++b)
+              tma_load_3d(dst + b * kBoxFloats, map, 0, rows[b], g * (W / 32), &full_bar[sl]);
           }
         }
       }
-      // every issued copy lands before the CTA can exit: wait (bounded) for
-      // the last fill of each slot
+    }
+    if (lane == 0) pdl_trigger();  // every copy of this CTA is issued
+    // every issued copy lands before the CTA can exit: wait (bounded) for
+    // the last fill of each slot
+    if (lane == 0)
       for (int kk = max(0, k - kDecSlots); kk < k; ++kk)
         mbar_wait(&full_bar[kk % kDecSlots], (kk / kDecSlots) & 1, status);
-    }
     return;
   }
   // ---- consumers: warp h = head h of the item's group -------------------------
@@ -734,10 +742,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
   const float scale = 1.0f / sqrtf((float)HD);
   const bool active = 2 * lane < HD;
   int k = 0;
+  int r_next = (int)blockIdx.x < items ? item_row(blockIdx.x, groups, row_order) : 0;
   for (int item = blockIdx.x; item < items; item += gridDim.x) {
-    int r, g, slot, len;
-    if (!decode_item(item, groups, row_order, row_slot, slot_len, len_add, limit, &r, &g, &slot, &len))
-      continue;
+    const int r = r_next;
+    const int g = item % groups;
+    if (item + (int)gridDim.x < items) r_next = item_row(item + gridDim.x, groups, row_order);
+    const int len = slot_len[row_slot[r]] + len_add;
+    if (len <= 0 || len > limit) continue;  // the producer flags it
     float mx = -INFINITY;
     for (int c0 = 0; c0 < len; c0 += kDecChunk, ++k) {
       const int n = min(kDecChunk, len - c0);
@@ -806,7 +817,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
 // ---- activation quantization (q8_gemm.rs:569-590) ------------------------------
 __global__ void quantize_kernel(const float* __restrict__ x, long long n4, float alpha,
                                 int8_t* __restrict__ out, uint32_t* status) {
-  pdl_enter();
+  pdl_enter_release();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n4) return;
   const float4 v = reinterpret_cast<const float4*>(x)[i];
@@ -823,7 +834,7 @@ __global__ void finalize_kernel(int cap, const int32_t* __restrict__ rows_dev,
                                 unsigned long long* __restrict__ best, int32_t* slot_prev,
                                 int32_t* slot_step, const int32_t* __restrict__ slot_limit,
                                 int32_t* step_tokens, uint8_t* done, uint32_t* status) {
-  pdl_enter();
+  pdl_enter_release();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= launch_rows(rows_dev, cap)) return;
   const int slot = row_slot[r];
@@ -895,7 +906,7 @@ __global__ void __launch_bounds__(kRowsThreads) step_rows_kernel(
   __shared__ int warp_sums[32];
   __shared__ int s_total;
   __shared__ int hist[2][kBins];
-  pdl_enter();
+  pdl_enter_release();
   const int tid = threadIdx.x;
   int32_t* row_slot = table + 4;
   int32_t* ord_self = row_slot + rmax;
@@ -975,7 +986,7 @@ __global__ void init_slots_kernel(int n, const int32_t* slots, const int32_t* li
                                   int32_t* slot_src, float* ssru_state, int layers, int max_slots,
                                   int d, const int32_t* __restrict__ page_rows, int32_t* cross_pages,
                                   int32_t* self_pages, int pages_per_slot) {
-  pdl_enter();
+  pdl_enter_release();
   const int i = blockIdx.x;
   if (i >= n) return;
   const int s = slots[i];
@@ -1014,7 +1025,7 @@ __global__ void shortlist_mask_kernel(int n, const int32_t* __restrict__ slots,
                                       int words, uint32_t* __restrict__ masks) {
   extern __shared__ uint32_t cm[];
   __shared__ int s_count;
-  pdl_enter();
+  pdl_enter_release();
   const int b = blockIdx.x;
   if (b >= n) return;
   for (int w = threadIdx.x; w < words; w += blockDim.x) {
