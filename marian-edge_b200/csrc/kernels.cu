@@ -47,7 +47,7 @@ __global__ void embed_encoder_kernel(const int32_t* __restrict__ tokens,
                                      const int8_t* __restrict__ emb, float emb_mult,
                                      float emb_scale, const float* __restrict__ positions, int d,
                                      float* __restrict__ x, const __grid_constant__ QuantOut q, uint32_t* status) {
-  pdl_enter_release();
+  pdl_enter();
   const int vec_per_row = d >> 2;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)n_tokens * vec_per_row) return;
@@ -77,7 +77,7 @@ __global__ void embed_decoder_kernel(int cap, const int32_t* __restrict__ rows_d
                                      float* __restrict__ x, const __grid_constant__ QuantOut q, uint8_t* eos_mask,
                                      const int32_t* __restrict__ self_pages, int pages_per_slot,
                                      int page_tokens, int32_t* self_row_map, uint32_t* status) {
-  pdl_enter_release();
+  pdl_enter();
   const int rows = launch_rows(rows_dev, cap);
   const int vec_per_row = d >> 2;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kLnThreads) residual_ln_kernel(
   constexpr int d = VPL * 128;
   constexpr int ld = d + 4, kVec = d / 4;
   extern __shared__ __align__(16) float tile[];  // [RPC][d + 4]
-  pdl_enter_release();
+  pdl_enter();
   const int rows = launch_rows(rows_dev, cap);
   const int row0 = blockIdx.x * RPC;
   const int nrows = min(RPC, rows - row0);
@@ -224,7 +224,7 @@ __global__ void __launch_bounds__(kLnThreads) ssru_kernel(
   constexpr int d = VPL * 128;
   constexpr int ld = d + 4, kVec = d / 4;
   extern __shared__ __align__(16) float tile[];
-  pdl_enter_release();
+  pdl_enter();
   const int rows = launch_rows(rows_dev, cap);
   const int row0 = blockIdx.x * RPC;
   const int nrows = min(RPC, rows - row0);
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(kLnWarps * 32) residual_ln_warp_kernel(
     uint32_t* status) {
   constexpr int d = VPL * 128;
   __shared__ __align__(16) float rows_s[kLnWarps][d];
-  pdl_enter_release();
+  pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kLnWarps + warp;
   if (row >= cap) return;
@@ -375,7 +375,7 @@ __global__ void __launch_bounds__(kLnWarps * 32) ssru_warp_kernel(
     uint32_t* status) {
   constexpr int d = VPL * 128;
   __shared__ __align__(16) float rows_s[kLnWarps][d];
-  pdl_enter_release();
+  pdl_enter();
   const int rows = launch_rows(rows_dev, cap);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kLnWarps + warp;
@@ -728,7 +728,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
         }
       }
     }
-    if (lane == 0) pdl_trigger();  // every copy of this CTA is issued
     // every issued copy lands before the CTA can exit: wait (bounded) for
     // the last fill of each slot
     if (lane == 0)
@@ -817,7 +816,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
 // ---- activation quantization (q8_gemm.rs:569-590) ------------------------------
 __global__ void quantize_kernel(const float* __restrict__ x, long long n4, float alpha,
                                 int8_t* __restrict__ out, uint32_t* status) {
-  pdl_enter_release();
+  pdl_enter();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n4) return;
   const float4 v = reinterpret_cast<const float4*>(x)[i];
@@ -834,7 +833,7 @@ __global__ void finalize_kernel(int cap, const int32_t* __restrict__ rows_dev,
                                 unsigned long long* __restrict__ best, int32_t* slot_prev,
                                 int32_t* slot_step, const int32_t* __restrict__ slot_limit,
                                 int32_t* step_tokens, uint8_t* done, uint32_t* status) {
-  pdl_enter_release();
+  pdl_enter();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= launch_rows(rows_dev, cap)) return;
   const int slot = row_slot[r];
@@ -906,7 +905,7 @@ __global__ void __launch_bounds__(kRowsThreads) step_rows_kernel(
   __shared__ int warp_sums[32];
   __shared__ int s_total;
   __shared__ int hist[2][kBins];
-  pdl_enter_release();
+  pdl_enter();
   const int tid = threadIdx.x;
   int32_t* row_slot = table + 4;
   int32_t* ord_self = row_slot + rmax;
@@ -986,7 +985,7 @@ __global__ void init_slots_kernel(int n, const int32_t* slots, const int32_t* li
                                   int32_t* slot_src, float* ssru_state, int layers, int max_slots,
                                   int d, const int32_t* __restrict__ page_rows, int32_t* cross_pages,
                                   int32_t* self_pages, int pages_per_slot) {
-  pdl_enter_release();
+  pdl_enter();
   const int i = blockIdx.x;
   if (i >= n) return;
   const int s = slots[i];
@@ -1025,7 +1024,7 @@ __global__ void shortlist_mask_kernel(int n, const int32_t* __restrict__ slots,
                                       int words, uint32_t* __restrict__ masks) {
   extern __shared__ uint32_t cm[];
   __shared__ int s_count;
-  pdl_enter_release();
+  pdl_enter();
   const int b = blockIdx.x;
   if (b >= n) return;
   for (int w = threadIdx.x; w < words; w += blockDim.x) {

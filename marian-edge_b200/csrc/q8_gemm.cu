@@ -290,9 +290,11 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
   const int lane = threadIdx.x & 31;
   const int num_kb = (p.k + kBK - 1) / kBK;
   const int n_tiles = (p.max_n + BN - 1) / BN;
-  // Set-up first (barriers, descriptor prefetch, TMEM): it reads nothing the
-  // predecessor writes, so it overlaps the predecessor's tail when this grid
-  // was launched early.
+  pdl_enter();
+  // The device row count is loaded before the set-up and used after it, so
+  // its latency overlaps the barrier initialization and TMEM allocation.
+  const int m_raw = p.m_dev ? *p.m_dev : p.m;
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -315,22 +317,6 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // The weights do not depend on the predecessor: in a single-linear launch
-  // the first tile's column block is known without the row count, so the
-  // producer issues its weight tiles for the first stages before waiting
-  // (expect_tx without arriving: a stage completes only once its
-  // activation tile is also requested and has landed).
-  int prefetched = 0;
-  const int n0_first = (blockIdx.x % n_tiles) * BN;
-  if (warp == 0 && lane == 0 && p.num_groups == 1 && n0_first < p.g[0].n) {
-    prefetched = min(stages, num_kb);
-    for (int kb = 0; kb < prefetched; ++kb) {
-      mbar_expect_tx(&full_bar[kb], BN * kBK);
-      tma_load_2d(smem_b + kb * BN * kBK, &p.g[0].tmap_b, kb * kBK, n0_first, &full_bar[kb]);
-    }
-  }
-  pdl_enter();
-  const int m_raw = p.m_dev ? *p.m_dev : p.m;
   const uint32_t tmem_base = tmem_base_s;
   const int m = max(0, min(m_raw, p.m));
   const int m_tiles = (m + kBM - 1) / kBM;
@@ -341,13 +327,6 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
       constexpr uint32_t kStageBytes = kBM * kBK + BN * kBK;
       int kbg = 0;
       bool ok = true;
-      if (prefetched && (int)blockIdx.x >= total) {
-        // no tile for this CTA after all: complete the prefetched stages and
-        // wait (bounded) for their copies before the CTA may exit
-        for (int kb = 0; kb < prefetched; ++kb) mbar_arrive_expect_tx(&full_bar[kb], 0);
-        for (int kb = 0; kb < prefetched; ++kb) mbar_wait(&full_bar[kb], 0, p.status);
-        prefetched = 0;
-      }
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         TileCoord c;
         if (!tile_coord<BN>(p, t, n_tiles, m_tiles, &c)) continue;
@@ -355,11 +334,6 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
         for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
           const int s = kbg % stages;
           const uint32_t phase = (kbg / stages) & 1;
-          if (kbg < prefetched) {  // weights already requested: the activations only
-            mbar_arrive_expect_tx(&full_bar[s], kBM * kBK);
-            tma_load_2d(smem_a + s * kBM * kBK, &g.tmap_a, kb * kBK, c.m0, &full_bar[s]);
-            continue;
-          }
           if (!(ok = mbar_wait(&empty_bar[s], phase ^ 1, p.status))) break;
           mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
           tma_load_2d(smem_a + s * kBM * kBK, &g.tmap_a, kb * kBK, c.m0, &full_bar[s]);
@@ -395,7 +369,6 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
         mma_commit(&tfull_bar[buf]);
         ++it;
       }
-      pdl_trigger();  // this CTA's MMAs are issued: the successor may launch
     }
   } else {
     // Epilogue warps 2 .. EPI + 1: warp % 4 selects the TMEM lane quarter
