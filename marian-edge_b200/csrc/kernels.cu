@@ -286,14 +286,24 @@ __device__ __forceinline__ float serial_sum(const float* row) {
   return sum;
 }
 
+template <int VPL>
+__device__ __forceinline__ void load_lane_chunks(const float* __restrict__ v, float4 (&out)[VPL]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) out[k] = *reinterpret_cast<const float4*>(v + 4 * (lane + 32 * k));
+}
+
 // x[k] (this lane's chunks, columns 4 * (lane + 32 k)) hold the pre-norm row;
 // row is the warp's shared-memory row buffer.  Writes out and the quantized
 // copies of global row `grow` when `store` (warp-uniform) is set.
+// gamma / beta: this lane's chunks of the LayerNorm scale and bias, loaded
+// by the caller at kernel entry (they are weights: their loads, often from
+// DRAM because the KV-cache traffic evicts them, overlap the row's).
 template <int VPL>
 __device__ __forceinline__ void ln_row(float4 (&x)[VPL], float* row, int grow,
-                                       const float* __restrict__ gamma,
-                                       const float* __restrict__ beta, float* __restrict__ out,
-                                       const QuantOut& q, uint32_t* status, bool store = true) {
+                                       const float4 (&gamma)[VPL], const float4 (&beta)[VPL],
+                                       float* __restrict__ out, const QuantOut& q, uint32_t* status,
+                                       bool store = true) {
   constexpr int d = VPL * 128;
   const int lane = threadIdx.x & 31;
   float4* r4 = reinterpret_cast<float4*>(row);
@@ -323,8 +333,8 @@ __device__ __forceinline__ void ln_row(float4 (&x)[VPL], float* row, int grow,
 #pragma unroll
   for (int k = 0; k < VPL; ++k) {
     const int col = 4 * (lane + 32 * k);
-    const float4 g = *reinterpret_cast<const float4*>(gamma + col);
-    const float4 b = *reinterpret_cast<const float4*>(beta + col);
+    const float4 g = gamma[k];
+    const float4 b = beta[k];
     float4 v;
     v.x = c[k].x * inv * g.x + b.x;
     v.y = c[k].y * inv * g.y + b.y;
@@ -346,6 +356,9 @@ __global__ void __launch_bounds__(kLnWarps * 32) residual_ln_warp_kernel(
     uint32_t* status) {
   constexpr int d = VPL * 128;
   __shared__ __align__(16) float rows_s[kLnWarps][d];
+  float4 gl[VPL], bl[VPL];
+  load_lane_chunks<VPL>(gamma, gl);
+  load_lane_chunks<VPL>(beta, bl);
   pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kLnWarps + warp;
@@ -362,7 +375,7 @@ __global__ void __launch_bounds__(kLnWarps * 32) residual_ln_warp_kernel(
     const float4 w = *reinterpret_cast<const float4*>(r + (size_t)row * ldr + col);
     x[k] = make_float4(u.x + w.x, u.y + w.y, u.z + w.z, u.w + w.w);
   }
-  ln_row<VPL>(x, rows_s[warp], row, gamma, beta, out, q, status, row < rows);
+  ln_row<VPL>(x, rows_s[warp], row, gl, bl, out, q, status, row < rows);
 }
 
 // SSRU (tensor.rs:184-218) with the warp-per-row LayerNorm above.
@@ -375,6 +388,9 @@ __global__ void __launch_bounds__(kLnWarps * 32) ssru_warp_kernel(
     uint32_t* status) {
   constexpr int d = VPL * 128;
   __shared__ __align__(16) float rows_s[kLnWarps][d];
+  float4 gl[VPL], bl[VPL];
+  load_lane_chunks<VPL>(gamma, gl);
+  load_lane_chunks<VPL>(beta, bl);
   pdl_enter();
   const int rows = launch_rows(rows_dev, cap);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -402,7 +418,7 @@ __global__ void __launch_bounds__(kLnWarps * 32) ssru_warp_kernel(
     *reinterpret_cast<float4*>(st + col) = make_float4(nx[0], nx[1], nx[2], nx[3]);
     x[k] = make_float4(o[0], o[1], o[2], o[3]);
   }
-  ln_row<VPL>(x, rows_s[warp], row, gamma, beta, out, q, status);
+  ln_row<VPL>(x, rows_s[warp], row, gl, bl, out, q, status);
 }
 
 // ---- attention (attention_into, tensor.rs:251-318) ------------------------------
@@ -603,7 +619,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
 // Decode: a persistent kernel over work items (active row, group of 4
 // heads), taken in row_order (longest rows first) round-robin by the CTAs.
 // Warp 4 is the producer: for every item it streams the group's
-// slices of the cached keys, then of the values, into a 3-slot shared-memory
+// slices of the cached keys, then of the values, into a 2-slot shared-memory
 // ring, one chunk of 32 keys per slot, with one 3-D TMA copy per 8 cache
 // rows (8 rows x 4 * HD floats of one page, through the pool's tensor map;
 // see encode_tmap_kv) completing on the slot's mbarrier, so at most 7 rows
@@ -611,7 +627,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
 // items are in flight while warps 0..3 (one per head of the group) consume
 // the current slot.  The 128-byte swizzle of the copies puts the 16-byte
 // chunk c of key row r at chunk c ^ (r % 8) of its line, so the lanes'
-// reads of different keys in the score loop fall on distinct banks.  Per head the operation order is the reference's: lane t scores
+// reads of different keys in the score loop fall on distinct banks.  Per
+// head the operation order is the reference's: lane t scores
 // key t with an in-order dot product, max, exp, a left-to-right sum by lane
 // 0, scaling, and a left-to-right weighted sum of V per output dim (lane i
 // owns dims 2i and 2i + 1).  Every mbarrier wait is bounded; on a timeout
@@ -619,7 +636,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
 // for the copies it issued.
 constexpr int kDecGroup = 4;    // heads per item
 constexpr int kDecChunk = 32;   // keys per ring slot
-constexpr int kDecSlots = 3;    // ring depth
+constexpr int kDecSlots = 2;    // ring depth (three CTAs per SM)
 constexpr int kDecThreads = (kDecGroup + 1) * 32;
 
 __device__ __forceinline__ void bulk_copy_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
@@ -649,8 +666,11 @@ __device__ __forceinline__ int swz(int t, int f, int box_floats) {
   return (t >> 3) * box_floats + cb * 256 + r * 32 + ((c ^ r) << 2) + (f & 3);
 }
 
+// Three CTAs share an SM (15 warps: four on some sub-partition, whose 16K
+// registers then allow 128 per thread), so twelve consumer warps per SM
+// overlap their dependent chains.
 template <int HD, int PT>
-__global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
+__global__ void __maxnreg__(128) attn_decode_kernel(
     const float* __restrict__ q, int ldq, const int32_t* __restrict__ rows_dev, int cap,
     const int32_t* __restrict__ row_slot,
     const int32_t* __restrict__ row_order, const int32_t* __restrict__ slot_len, int len_add,
@@ -688,6 +708,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
     // pages) instead of one per copied box.  Lane 0 issues the copies.
     int k = 0;
     bool ok = true;
+    const uint64_t stream_once = l2_policy_evict_first();  // KV pages: read once per step
     int item = blockIdx.x;
     int r_next = item < items ? item_row(item, groups, row_order) : 0;
     for (; item < items && ok; item += gridDim.x) {
@@ -723,7 +744,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
               bulk_copy_g2s(dst + (kDecChunk / 8) * kBoxFloats, q + (size_t)r * ldq + g * W, q_bytes,
                             &full_bar[sl]);
             for (int b = 0; b < nb; ++b)
-              tma_load_3d(dst + b * kBoxFloats, map, 0, rows[b], g * (W / 32), &full_bar[sl]);
+              tma_load_3d_hint(dst + b * kBoxFloats, map, 0, rows[b], g * (W / 32), &full_bar[sl],
+                               stream_once);
           }
         }
       }
@@ -741,13 +763,20 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
   const float scale = 1.0f / sqrtf((float)HD);
   const bool active = 2 * lane < HD;
   int k = 0;
+  // The next item's row, slot and key count are loaded during this item
+  // (one dependent load after each phase), off the critical path.
   int r_next = (int)blockIdx.x < items ? item_row(blockIdx.x, groups, row_order) : 0;
+  int len_next = (int)blockIdx.x < items ? slot_len[row_slot[r_next]] + len_add : 0;
   for (int item = blockIdx.x; item < items; item += gridDim.x) {
     const int r = r_next;
+    const int len = len_next;
     const int g = item % groups;
-    if (item + (int)gridDim.x < items) r_next = item_row(item + gridDim.x, groups, row_order);
-    const int len = slot_len[row_slot[r]] + len_add;
-    if (len <= 0 || len > limit) continue;  // the producer flags it
+    const bool have_next = item + (int)gridDim.x < items;
+    if (have_next) r_next = item_row(item + gridDim.x, groups, row_order);
+    if (len <= 0 || len > limit) {  // the producer flags it
+      if (have_next) len_next = slot_len[row_slot[r_next]] + len_add;
+      continue;
+    }
     float mx = -INFINITY;
     for (int c0 = 0; c0 < len; c0 += kDecChunk, ++k) {
       const int n = min(kDecChunk, len - c0);
@@ -773,6 +802,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
       __syncwarp();
       if (lane == 0) mbar_arrive_cta(&empty_bar[sl]);
     }
+    const int slot_next = have_next ? row_slot[r_next] : 0;
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     for (int j = lane; j < len; j += 32) ph[j] = exp_f32(ph[j] - mx);
     __syncwarp();
@@ -786,6 +816,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(
     inv = __shfl_sync(0xffffffffu, inv, 0);
     for (int j = lane; j < len; j += 32) ph[j] = ph[j] * inv;
     __syncwarp();
+    if (have_next) len_next = slot_len[slot_next] + len_add;
     float acc0 = 0.0f, acc1 = 0.0f;
     for (int c0 = 0; c0 < len; c0 += kDecChunk, ++k) {
       const int n = min(kDecChunk, len - c0);
@@ -1232,15 +1263,18 @@ cudaError_t launch_attn_decode_hd(const float* q, int ldq, int rows, const int32
   if (!(configured & (1ull << dev))) {
     cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD, PT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_decode_kernel<HD, PT>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               (int)cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     sms[dev] = n > 0 ? n : 148;
     configured |= 1ull << dev;
   }
-  // two CTAs per SM (the ring takes ~100 KB of shared memory per CTA)
+  // three CTAs per SM (the 2-slot ring takes ~70 KB of shared memory per CTA)
   const long long items = (long long)rows * (heads / kDecGroup);
-  const int grid = (int)std::min<long long>(items, 2LL * sms[dev]);
+  const int grid = (int)std::min<long long>(items, 3LL * sms[dev]);
   launch_pdl(attn_decode_kernel<HD, PT>, dim3(grid), dim3(kDecThreads), smem, s, q, ldq, rows_dev, rows,
              row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, *k_map, *v_map, d,
              heads, out_q, alpha, status);

@@ -70,11 +70,14 @@ __device__ __forceinline__ uint32_t pack4_s8(int q0, int q1, int q2, int q3) {
 
 // One 32-column chunk of one tile row per lane.  `ok` is this lane's row
 // validity; the call itself is warp-uniform (tcgen05.ld precedes it).
+// sbias / sscale: this chunk's 32 bias and column-scale values, staged in
+// shared memory before the accumulator was ready (nullptr: none).
 template <int BN>
 __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_t (&r)[32],
                                                bool ok, int row, int dest_row, int nb,
                                                float row_scale, uint32_t* status, float& best,
-                                               int& best_n, uint32_t* stage) {
+                                               int& best_n, uint32_t* stage, const float* sbias,
+                                               const float* sscale) {
   const int n_end = g.n;
   const int lane = threadIdx.x & 31;
   if (g.mode == kEpiArgmax) {
@@ -83,7 +86,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
     // chunks), so no per-column mask or bounds test is needed.
     if (!ok) return;
     const float uscale = g.row_scale ? __fmul_rn(row_scale, g.uniform_scale) : g.uniform_scale;
-    const float4* b4 = reinterpret_cast<const float4*>(g.bias + nb);
+    const float4* b4 = reinterpret_cast<const float4*>(sbias);
     float v[32];
 #pragma unroll
     for (int j4 = 0; j4 < 8; ++j4) {
@@ -133,16 +136,14 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
     const float us = g.uniform_scale;
 #pragma unroll
     for (int j4 = 0; j4 < 8; ++j4) {
-      float4 s4 = g.col_scale ? reinterpret_cast<const float4*>(g.col_scale + nb)[j4]
-                              : make_float4(us, us, us, us);
+      float4 s4 = sscale ? reinterpret_cast<const float4*>(sscale)[j4] : make_float4(us, us, us, us);
       if (g.row_scale) {
         s4.x = __fmul_rn(row_scale, s4.x);
         s4.y = __fmul_rn(row_scale, s4.y);
         s4.z = __fmul_rn(row_scale, s4.z);
         s4.w = __fmul_rn(row_scale, s4.w);
       }
-      const float4 b4 = g.bias ? reinterpret_cast<const float4*>(g.bias + nb)[j4]
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 b4 = sbias ? reinterpret_cast<const float4*>(sbias)[j4] : make_float4(0.f, 0.f, 0.f, 0.f);
       v[4 * j4 + 0] = dequant(static_cast<int32_t>(r[4 * j4 + 0]), s4.x, b4.x);
       v[4 * j4 + 1] = dequant(static_cast<int32_t>(r[4 * j4 + 1]), s4.y, b4.y);
       v[4 * j4 + 2] = dequant(static_cast<int32_t>(r[4 * j4 + 2]), s4.z, b4.z);
@@ -285,6 +286,10 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
   __shared__ __align__(8) uint64_t tfull_bar[2];
   __shared__ __align__(8) uint64_t tempty_bar[2];
   __shared__ uint32_t tmem_base_s;
+  // per epilogue warp: the bias and column scales of its columns of the
+  // current tile (at most 64: BN / (EPI / 4))
+  __shared__ __align__(16) float s_bias[EPI][64];
+  __shared__ __align__(16) float s_scale[EPI][64];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -325,6 +330,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
   if (warp == 0) {
     if (lane == 0) {
       constexpr uint32_t kStageBytes = kBM * kBK + BN * kBK;
+      const uint64_t keep = l2_policy_evict_last();  // weights: reused every step
       int kbg = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
@@ -337,7 +343,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
           if (!(ok = mbar_wait(&empty_bar[s], phase ^ 1, p.status))) break;
           mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
           tma_load_2d(smem_a + s * kBM * kBK, &g.tmap_a, kb * kBK, c.m0, &full_bar[s]);
-          tma_load_2d(smem_b + s * BN * kBK, &g.tmap_b, kb * kBK, c.n0, &full_bar[s]);
+          tma_load_2d_hint(smem_b + s * BN * kBK, &g.tmap_b, kb * kBK, c.n0, &full_bar[s], keep);
         }
       }
     }
@@ -383,6 +389,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
       const GemmGroup& g = p.g[c.z];
       const int buf = it & 1;
       constexpr int kShare = BN / (EPI / 4) >= 32 ? BN / (EPI / 4) : 32;
+      static_assert(kShare <= 64, "s_bias holds 64 columns per warp");
       // The per-row operands are loaded, and the bias lines of this warp's
       // columns are prefetched into L1, before the accumulator is ready, so
       // their latency overlaps the MMAs.
@@ -392,8 +399,22 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
       const float row_scale = (row_ok && g.row_scale) ? g.row_scale[row] : 1.0f;
       const int c_first = part * kShare;
       const int nb_first = c.n0 + c_first;
-      if (lane < kShare / 32 && g.bias != nullptr && g.mode != kEpiI32 && nb_first + 32 * lane < g.n)
-        asm volatile("prefetch.global.L1 [%0];" ::"l"(g.bias + nb_first + 32 * lane));
+      // This warp's bias and column scales are staged in shared memory now:
+      // their loads (often DRAM: the KV-cache traffic evicts them from L2)
+      // overlap the MMAs instead of following the accumulator.
+      float* sb = s_bias[warp - 2];
+      float* ss = s_scale[warp - 2];
+      const bool has_bias = g.bias != nullptr && g.mode != kEpiI32;
+      const bool has_scale = g.col_scale != nullptr && g.mode != kEpiI32;
+#pragma unroll
+      for (int i = 0; i < kShare / 32; ++i) {
+        const int n = nb_first + 32 * i + lane;
+        // the argmax bias is padded with -inf to whole 256-column blocks
+        const bool in = g.mode == kEpiArgmax || n < g.n;
+        if (has_bias) sb[32 * i + lane] = in ? g.bias[n] : 0.0f;
+        if (has_scale) ss[32 * i + lane] = n < g.n ? g.col_scale[n] : 0.0f;
+      }
+      __syncwarp();
       // Warp-uniform: tcgen05.ld below is .sync.aligned.
       const bool ready = __all_sync(0xffffffffu, mbar_wait(&tfull_bar[buf], (it >> 1) & 1, p.status));
       if (!ready) break;
@@ -408,7 +429,8 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
         tmem_ld_wait();
         if (c.n0 + c0 < g.n)
           epilogue_chunk<BN>(g, r, row_ok && dest_row >= 0, row, dest_row, c.n0 + c0, row_scale,
-                             p.status, best, best_n, stage);
+                             p.status, best, best_n, stage, has_bias ? sb + (c0 - c_first) : nullptr,
+                             has_scale ? ss + (c0 - c_first) : nullptr);
       }
       if (g.mode == kEpiArgmax && row_ok && dest_row >= 0 && best_n >= 0)
         atomicMax(&g.argmax[dest_row], pack_argmax(best, best_n));
@@ -466,12 +488,19 @@ cudaError_t launch_impl(GemmParams p, cudaStream_t stream) {
   if (ce != cudaSuccess) return ce;
   const int num_kb = (p.k + kBK - 1) / kBK;
   const int tiles = ((p.max_n + BN - 1) / BN) * ((p.m + kBM - 1) / kBM) * p.num_groups;
-  // Two CTAs per SM for the narrow tile when a 3-stage ring covers short K.
+  // Two CTAs per SM for the narrow tile when a 3-stage ring covers short K
+  // and the tiles outnumber the SMs; with fewer tiles, one CTA per SM and a
+  // ring as deep as K, so every k-block is requested at once (one load
+  // round trip instead of two).
   int ctas_per_sm = 1;
   int stages = MAX_STAGES;
   if (BN == 64 && num_kb <= 4) {
-    stages = 3;
-    ctas_per_sm = 2;
+    if (tiles > num_sms()) {
+      stages = 3;
+      ctas_per_sm = 2;
+    } else {
+      stages = num_kb < 3 ? 3 : num_kb;
+    }
   }
   const int grid = tiles < num_sms() * ctas_per_sm ? tiles : num_sms() * ctas_per_sm;
   p.stages = stages;
