@@ -220,7 +220,8 @@ enum {
     MC_K_LAYERNORM = 10,   /* residual + LayerNorm (+ quantized copies) */
     MC_K_SSRU = 11,        /* SSRU state update + LayerNorm */
     MC_K_FINALIZE = 12,    /* token selection bookkeeping */
-    MC_KERNEL_KINDS = 13
+    MC_K_GEMM_LN = 13,     /* output projection or FFN W2 fused with residual + LayerNorm */
+    MC_KERNEL_KINDS = 14
 };
 
 /* Enables (1) or disables (0) per-launch CUDA-event timing on the engine
@@ -269,6 +270,23 @@ mc_status mc_q8_gemm(const int8_t *a, const int8_t *w, int32_t m, int32_t n, int
 mc_status mc_q8_linear(const float *x, int32_t m, int32_t k, const int8_t *w, int32_t n,
                        float activation_mult, float weight_mult, const float *bias, float *y,
                        void *stream);
+
+/* Q8Linear::run_into followed by residual_layer_norm_into
+ * (crates/marian-cpu/src/q8_gemm.rs:380-448, tensor.rs:132-155) in one
+ * launch, as every Transformer sub-layer of the decoder ends:
+ * y = LN(linear(x) + residual) * gamma + beta with eps 1e-6, the linear as
+ * in mc_q8_linear (x [m, k] f32 quantized with activation_mult, w [d, k]
+ * int8, bias [d] nullable).  residual and y are [m, d] f32; gamma and beta
+ * [d].  y_q (nullable) also receives y quantized with y_alpha, centred
+ * (the reference's u8 minus 127), as the next linear reads it.  d must be
+ * 128, 256, 384 or 512 (else MC_INVALID_INPUT); x, residual, y, gamma and
+ * beta 16-byte aligned.  Device pointers, asynchronous on `stream`; status
+ * bits as mc_q8_linear (mc_op_status).  Bit-identical to mc_q8_linear
+ * followed by the reference's residual LayerNorm. */
+mc_status mc_q8_linear_ln(const float *x, int32_t m, int32_t k, const int8_t *w, int32_t d,
+                          float activation_mult, float weight_mult, const float *bias,
+                          const float *residual, const float *gamma, const float *beta, float *y,
+                          int8_t *y_q, float y_alpha, void *stream);
 
 /* Largest m * k accepted by mc_q8_linear_noalloc (bytes of quantized
  * activations in its fixed device scratch). */

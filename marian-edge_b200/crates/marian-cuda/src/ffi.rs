@@ -92,7 +92,7 @@ pub type mc_piece_count_fn = unsafe extern "C" fn(
 pub const MC_Q8_LINEAR_NOALLOC_MAX_ACTIVATIONS: u32 = 8 * 1024 * 1024;
 
 // Kernel classes of mc_profile_read.
-pub const MC_KERNEL_KINDS: i32 = 13;
+pub const MC_KERNEL_KINDS: i32 = 14;
 
 unsafe extern "C" {
     pub fn mc_config_default(cfg: *mut mc_config);
@@ -213,6 +213,23 @@ unsafe extern "C" {
         weight_mult: f32,
         bias: *const f32,
         y: *mut f32,
+        stream: *mut c_void,
+    ) -> mc_status;
+    pub fn mc_q8_linear_ln(
+        x: *const f32,
+        m: i32,
+        k: i32,
+        w: *const i8,
+        d: i32,
+        activation_mult: f32,
+        weight_mult: f32,
+        bias: *const f32,
+        residual: *const f32,
+        gamma: *const f32,
+        beta: *const f32,
+        y: *mut f32,
+        y_q: *mut i8,
+        y_alpha: f32,
         stream: *mut c_void,
     ) -> mc_status;
     pub fn mc_q8_linear_noalloc(

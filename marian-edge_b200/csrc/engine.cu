@@ -20,6 +20,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <deque>
 #include <string>
@@ -28,6 +29,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "linear_ln.cuh"
 #include "marian_cuda.h"
 #include "model_loader.h"
 #include "q8_gemm.cuh"
@@ -50,6 +52,8 @@ struct DevLinear {
   float scale = 1.0f;          // 1 / (alpha * weight quant_mult)
   bool per_row = false;        // col_scale holds 1 / (alpha * row multiplier[n])
   CUtensorMap tmap_b[3];       // W tensor maps for BN = 64, 128, 256
+  CUtensorMap tmap_ln;         // W tensor map for the fused LayerNorm kernel
+  bool has_ln_map = false;     // (box out / linear_ln_cluster(out) rows)
 };
 
 struct DevAttention {
@@ -228,6 +232,10 @@ struct mc_engine {
 
   std::vector<Lane> lanes;
   bool use_graphs = true;
+  // decode sub-layers end in one fused linear + residual + LayerNorm launch
+  // (linear_ln.cu) when the width allows; MARIAN_CUDA_FUSED_LN=0 selects the
+  // separate GEMM and LayerNorm kernels (same results)
+  bool fuse_ln = true;
 
   // scheduler
   std::deque<Request*> queue;
@@ -415,6 +423,11 @@ mc_status upload_linear(mc_engine* e, const std::string& wname, const char* bnam
   for (int i = 0; i < 3; ++i)
     if (!encode_tmap_i8(&L->tmap_b[i], L->w, L->out, L->in, kBNs[i]))
       return fail(e, MC_MODEL, wname + ": tensor map rejected");
+  if (const int c = linear_ln_cluster(L->out)) {
+    if (!encode_tmap_i8(&L->tmap_ln, L->w, L->out, L->in, L->out / c))
+      return fail(e, MC_MODEL, wname + ": tensor map rejected");
+    L->has_ln_map = true;
+  }
   return MC_OK;
 }
 
@@ -646,6 +659,48 @@ mc_status run_encoder(mc_engine* e, Lane& L, const AdmLayout& A, double sum_len_
   return MC_OK;
 }
 
+// A decode linear whose output feeds residual + LayerNorm: one fused launch
+// (linear_ln.cu) when the model width allows, else the GEMM into dec_proj
+// and the LayerNorm kernel.  Both give the same bits.
+mc_status linear_ln(mc_engine* e, Lane& L, int gemm_kind, const QBuf* a, const DevLinear& w,
+                    const float* residual, const float* gamma, const float* beta, int cap,
+                    const int32_t* m_dev, double m_prof, float* out, const QuantOut& q) {
+  const int d = e->d;
+  const double rows_d = m_prof * d;
+  if (e->fuse_ln && w.has_ln_map && w.out == d) {
+    LinearLnParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.tmap_a = a->tmap;
+    p.tmap_b = w.tmap_ln;
+    p.col_scale = w.per_row ? w.col_scale : nullptr;
+    p.uniform_scale = w.scale;
+    p.bias = w.bias;
+    p.residual = residual;
+    p.ldr = d;
+    p.gamma = gamma;
+    p.beta = beta;
+    p.out = out;
+    p.q = q;
+    p.cap = cap;
+    p.m_dev = m_dev;
+    p.k = w.in;
+    p.status = L.d_status;
+    const double flops = 2.0 * rows_d * w.in;
+    const double bytes = m_prof * w.in + (double)d * w.in + 16.0 * d + rows_d * (8 + q.count);
+    PROFILED(MC_K_GEMM_LN, flops, bytes, CK(launch_q8_linear_ln(p, d, L.cur)));
+    ++e->launches;
+    return MC_OK;
+  }
+  GroupSpec spec = {a, &w, kEpiF32, L.dec_proj, d, 0, nullptr, false, 0.f};
+  mc_status st = gemm(e, L, gemm_kind, cap, m_dev, m_prof, &spec, 1);
+  if (st) return st;
+  PROFILED(MC_K_LAYERNORM, 0.0, rows_d * (12 + q.count),
+           launch_residual_ln(L.dec_proj, d, residual, d, gamma, beta, cap, m_dev, d, out, q, L.d_status,
+                              L.cur));
+  ++e->launches;
+  return MC_OK;
+}
+
 // ---- one decode step over a lane's active rows -------------------------------
 // Grids cover `cap` rows; the kernels read the step's row count from the
 // lane's rows block (rows_d[0]), so the same launches serve any row count up
@@ -695,12 +750,10 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap, const std::vector<int3
                                      e->self_pages_d, e->pages_per_slot, e->page_tokens,
                                      &e->self_k_map[l], &e->self_v_map[l], d, e->heads, L.dec_o.p,
                                      a.wo.alpha, L.d_status, L.cur)));
-      GroupSpec wo = {&L.dec_o, &a.wo, kEpiF32, L.dec_proj, d, 0, nullptr, false, 0.f};
-      if ((st = gemm(e, L, MC_K_GEMM_OUT, cap, nrows, R, &wo, 1))) return st;
-      PROFILED(MC_K_LAYERNORM, 0.0, rows_d * 13,
-               launch_residual_ln(L.dec_proj, d, x, d, a.ln_g, a.ln_b, cap, nrows, d, y,
-                                  quant_out(L.dec_q, {c.wq.alpha}), L.d_status, L.cur));
-      e->launches += 2;
+      if ((st = linear_ln(e, L, MC_K_GEMM_OUT, &L.dec_o, a.wo, x, a.ln_g, a.ln_b, cap, nrows, R, y,
+                          quant_out(L.dec_q, {c.wq.alpha}))))
+        return st;
+      ++e->launches;
     } else {
       const DevSsru& s = e->dec_ssru[l];
       GroupSpec wf[2] = {
@@ -721,22 +774,17 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap, const std::vector<int3
                                    e->cross_pages_d, e->pages_per_slot, e->page_tokens,
                                    &e->cross_k_map[l], &e->cross_v_map[l], d, e->heads, L.dec_o.p,
                                    c.wo.alpha, L.d_status, L.cur)));
-    GroupSpec wo = {&L.dec_o, &c.wo, kEpiF32, L.dec_proj, d, 0, nullptr, false, 0.f};
-    if ((st = gemm(e, L, MC_K_GEMM_OUT, cap, nrows, R, &wo, 1))) return st;
-    PROFILED(MC_K_LAYERNORM, 0.0, rows_d * 13,
-             launch_residual_ln(L.dec_proj, d, x, d, c.ln_g, c.ln_b, cap, nrows, d, y,
-                                quant_out(L.dec_q, {f.w1.alpha}), L.d_status, L.cur));
+    if ((st = linear_ln(e, L, MC_K_GEMM_OUT, &L.dec_o, c.wo, x, c.ln_g, c.ln_b, cap, nrows, R, y,
+                        quant_out(L.dec_q, {f.w1.alpha}))))
+      return st;
     std::swap(x, y);
     GroupSpec w1 = {&L.dec_q[0], &f.w1, kEpiQ8, L.dec_h.p, e->ffn, 0, nullptr, true, f.w2.alpha};
     if ((st = gemm(e, L, MC_K_GEMM_FFN1, cap, nrows, R, &w1, 1))) return st;
-    GroupSpec w2 = {&L.dec_h, &f.w2, kEpiF32, L.dec_proj, d, 0, nullptr, false, 0.f};
-    if ((st = gemm(e, L, MC_K_GEMM_FFN2, cap, nrows, R, &w2, 1))) return st;
-    PROFILED(MC_K_LAYERNORM, 0.0, rows_d * (12 + dec_input_alphas(e, l + 1).size()),
-             launch_residual_ln(L.dec_proj, d, x, d, f.ln_g, f.ln_b, cap, nrows, d, y,
-                                quant_out_vec(L.dec_q, dec_input_alphas(e, l + 1)), L.d_status,
-                                L.cur));
+    if ((st = linear_ln(e, L, MC_K_GEMM_FFN2, &L.dec_h, f.w2, x, f.ln_g, f.ln_b, cap, nrows, R, y,
+                        quant_out_vec(L.dec_q, dec_input_alphas(e, l + 1)))))
+      return st;
     std::swap(x, y);
-    e->launches += 3;
+    ++e->launches;
   }
   // tied vocabulary projection + masked argmax (q8_engine.rs:749-790)
   GroupSpec voc = {&L.dec_q[0], &e->vocab, kEpiArgmax, nullptr, 0, 0, nullptr, false, 0.f};
@@ -926,6 +974,7 @@ mc_status allocate_buffers(mc_engine* e) {
     if (st) return st;
   }
   CK(prepare_q8_gemm());
+  CK(prepare_q8_linear_ln());
   CK(cudaStreamSynchronize(e->stream));
   return MC_OK;
 }
@@ -1405,6 +1454,7 @@ extern "C" mc_status mc_create(const mc_config* cfg, mc_engine** out) {
       cfg->max_length_factor > 8 || cfg->lanes > (uint32_t)kMaxLanes)
     return MC_INVALID_INPUT;
   mc_engine* e = new mc_engine();
+  if (const char* v = std::getenv("MARIAN_CUDA_FUSED_LN")) e->fuse_ln = std::strcmp(v, "0") != 0;
   e->cfg = *cfg;
   mc_status st = set_device(e);
   if (st == MC_OK) {

@@ -6,6 +6,7 @@
 #include <cmath>
 
 #include "kernels.cuh"
+#include "linear_ln.cuh"
 #include "marian_cuda.h"
 #include "q8_gemm.cuh"
 
@@ -108,6 +109,56 @@ extern "C" mc_status mc_q8_linear(const float* x, int32_t m, int32_t k, const in
     p.max_n = n;
     p.status = status;
     if (mc::launch_q8_gemm(p, bn, s) != cudaSuccess) st = MC_CUDA;
+  }
+  if (cudaFreeAsync(q, s) != cudaSuccess && st == MC_OK) st = MC_CUDA;
+  return st;
+}
+
+extern "C" mc_status mc_q8_linear_ln(const float* x, int32_t m, int32_t k, const int8_t* w, int32_t d,
+                                     float activation_mult, float weight_mult, const float* bias,
+                                     const float* residual, const float* gamma, const float* beta,
+                                     float* y, int8_t* y_q, float y_alpha, void* stream) {
+  if (m < 0 || k <= 0 || (k % 16) != 0 || !x || !w || !residual || !gamma || !beta || !y ||
+      mc::linear_ln_cluster(d) == 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(residual) & 15) != 0 || (reinterpret_cast<uintptr_t>(y) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(gamma) & 15) != 0 || (reinterpret_cast<uintptr_t>(beta) & 15) != 0 ||
+      (y_q && ((reinterpret_cast<uintptr_t>(y_q) & 3) != 0 || !std::isfinite(y_alpha) || y_alpha <= 0.0f)))
+    return MC_INVALID_INPUT;
+  if (!std::isfinite(activation_mult) || activation_mult <= 0.0f || !std::isfinite(weight_mult) ||
+      weight_mult <= 0.0f)
+    return MC_INVALID_INPUT;
+  const float inverse_scale = 1.0f / (activation_mult * weight_mult);  // q8_gemm.rs:438
+  if (!std::isfinite(inverse_scale) || inverse_scale <= 0.0f) return MC_INVALID_INPUT;
+  if (m == 0) return MC_OK;
+  uint32_t* status = op_status_word();
+  if (!status) return MC_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int8_t* q = nullptr;
+  if (cudaMallocAsync(reinterpret_cast<void**>(&q), (size_t)m * k, s) != cudaSuccess) return MC_CUDA;
+  mc::launch_quantize(x, (long long)m * k, activation_mult, q, status, s);
+  mc::LinearLnParams p;
+  std::memset(&p, 0, sizeof(p));
+  mc_status st = MC_OK;
+  const int bn = d / mc::linear_ln_cluster(d);
+  if (!mc::encode_tmap_i8(&p.tmap_a, q, (uint64_t)m, (uint64_t)k, 128) ||
+      !mc::encode_tmap_i8(&p.tmap_b, w, (uint64_t)d, (uint64_t)k, (uint32_t)bn)) {
+    st = MC_INVALID_INPUT;
+  } else {
+    p.uniform_scale = inverse_scale;
+    p.bias = bias;
+    p.residual = residual;
+    p.ldr = d;
+    p.gamma = gamma;
+    p.beta = beta;
+    p.out = y;
+    p.q.base = y_q;
+    p.q.stride = 0;
+    p.q.count = y_q ? 1 : 0;
+    p.q.alpha[0] = y_alpha;
+    p.cap = m;
+    p.k = k;
+    p.status = status;
+    if (mc::launch_q8_linear_ln(p, d, s) != cudaSuccess) st = MC_CUDA;
   }
   if (cudaFreeAsync(q, s) != cudaSuccess && st == MC_OK) st = MC_CUDA;
   return st;

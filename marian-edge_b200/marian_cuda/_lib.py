@@ -18,7 +18,7 @@ EXPORTS = [
     "mc_config_default", "mc_create", "mc_load_marian_bin", "mc_model_info_get", "mc_destroy",
     "mc_last_error", "mc_is_ready", "mc_translate_token_ids", "mc_submit", "mc_step", "mc_poll",
     "mc_trace_first_step", "mc_stream", "mc_q8_gemm", "mc_op_status", "mc_profile",
-    "mc_profile_read", "mc_launch_count", "mc_q8_linear", "mc_q8_linear_noalloc", "mc_load_shortlist",
+    "mc_profile_read", "mc_launch_count", "mc_q8_linear", "mc_q8_linear_noalloc", "mc_q8_linear_ln", "mc_load_shortlist",
     "mc_segment_text", "mc_timeline", "mc_timeline_read", "mc_inspect_marian_bin",
     "mc_encode_token_ids", "mc_replay",
 ]
@@ -27,7 +27,7 @@ EXPORTS = [
 NOALLOC_MAX_ACTIVATIONS = 8 * 1024 * 1024
 
 KERNEL_KINDS = ["embed", "gemm_qkv", "gemm_out", "gemm_ffn1", "gemm_ffn2", "gemm_crosskv",
-                "gemm_vocab", "attn_enc", "attn_self", "attn_cross", "layernorm", "ssru", "finalize"]
+                "gemm_vocab", "attn_enc", "attn_self", "attn_cross", "layernorm", "ssru", "finalize", "gemm_ln"]
 
 
 class Config(C.Structure):
@@ -111,6 +111,8 @@ def load(build_if_missing: bool = True):
     if getattr(raw, 'mc_q8_gemm', None) is not None: lib.mc_q8_gemm.argtypes = [vp, vp, i32, i32, i32, vp, vp, vp, vp, i32, i32, vp, vp]
     if getattr(raw, 'mc_op_status', None) is not None: lib.mc_op_status.argtypes = [C.POINTER(u32)]
     lib.mc_q8_linear.argtypes = [vp, i32, i32, vp, i32, C.c_float, C.c_float, vp, vp, vp]
+    lib.mc_q8_linear_ln.argtypes = [vp, i32, i32, vp, i32, C.c_float, C.c_float, vp, vp, vp, vp, vp, vp,
+                                    C.c_float, vp]
     lib.mc_q8_linear_noalloc.argtypes = [vp, i32, i32, vp, i32, C.c_float, C.c_float, vp, vp, vp,
                                          C.POINTER(u32)]
     lib.mc_profile.argtypes = [vp, i32]
