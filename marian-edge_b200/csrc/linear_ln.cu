@@ -9,22 +9,25 @@
 //
 // The LayerNorm needs whole rows, and its two sums are serial chains over
 // all d columns, so the work is split by rows AND columns: a cluster of C
-// CTAs owns one 128-row block, CTA j computing output columns
-// [j * d / C, (j + 1) * d / C) on the tensor cores:
-//   warp 0      TMA producer (A and W k-blocks into a ring, 128-byte swizzle);
+// CTAs (8 for d = 512) owns one 128-row block, CTA j computing output
+// columns [j * d / C, (j + 1) * d / C) on the tensor cores:
+//   warp 0      TMA producer (A and W k-blocks into a ring, 128-byte
+//               swizzle), started before the TMEM allocation;
 //   warp 1      TMEM allocation and tcgen05.mma.kind::i8 from one thread;
-//   warps 2..5  epilogue, one TMEM lane quarter each (one row per thread):
-//               x = (acc * scale + bias) + residual, the residual row
-//               segment having been loaded into registers while the MMAs ran.
+//   warps 2..9  epilogue, two per TMEM lane quarter (one row per thread,
+//               alternate 32-column chunks): x = (acc * scale + bias) +
+//               residual, the residual values having been loaded into
+//               registers while the MMAs ran.
 // Each CTA also owns 128 / C rows of the block for the normalization.  The
-// epilogue threads send their row's x segment to the owning CTA's exchange
-// buffer with st.async (distributed shared memory), which completes bytes
-// on the owner's mbarrier (a CTA's own rows take plain shared-memory
-// stores); once all d columns of its rows have arrived, one
-// thread per row runs the two ordered sums, and the four warps normalize
-// the rows with coalesced row-wise stores of the f32 result and its int8
-// copies.  Every mbarrier wait is bounded; the cluster barriers are passed
-// by every thread of every CTA on every path.
+// epilogue writes each row's x segment either into the CTA's own exchange
+// buffer (its own rows) or, grouped by owner, into the idle TMA ring; one
+// bulk copy per owner (cp.async.bulk shared::cta -> shared::cluster) then
+// moves each group into the owner's exchange buffer and completes its bytes
+// on the owner's mbarrier.  Once all d columns of its rows have arrived, one
+// thread per row runs the two ordered sums, and every warp of the CTA
+// normalizes the rows with coalesced row-wise stores of the f32 result and
+// its int8 copies.  Every mbarrier wait is bounded; the cluster barriers are
+// passed by every thread of every CTA on every path.
 #include "common.cuh"
 #include "linear_ln.cuh"
 #include "q8_gemm.cuh"
@@ -66,17 +69,6 @@ __device__ __forceinline__ uint32_t map_shared_rank(uint32_t addr, uint32_t rank
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
-}
-
-// 16-byte store into a cluster peer's shared memory that completes 16
-// transaction bytes on the peer's mbarrier `bar` (same CTA as addr).
-__device__ __forceinline__ void st_async_f4(uint32_t addr, float a, float b, float c, float d,
-                                            uint32_t bar) {
-  asm volatile(
-      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
-          addr),
-      "f"(a), "f"(b), "f"(c), "f"(d), "r"(bar)
-      : "memory");
 }
 
 // Bounded wait with acquire semantics at cluster scope: the bytes that
@@ -127,7 +119,7 @@ struct LlShape {
   static constexpr int XSEG = R * SLD;       // one CTA's columns of R rows (floats)
   static constexpr int TCOLS = BN <= 32 ? 32 : (BN <= 64 ? 64 : 128);  // TMEM columns
   static constexpr int STAGE = kLlBM * kLlBK + BN * kLlBK;
-  static constexpr int XBYTES = 2 * C * XSEG * 4;   // the rows, then their centred squares
+  static constexpr int XBYTES = C * XSEG * 4;       // the incoming rows
   static constexpr int STAGING = C * XSEG * 4;      // outgoing segments (in the ring)
   static constexpr int MIN_STAGES = (STAGING + STAGE - 1) / STAGE;
   static_assert(D % 128 == 0 && BN % 32 == 0 && BN <= 128 && kLlBM % C == 0 && R <= 32 && R >= 8,
@@ -163,6 +155,33 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, const void* src,
 // dependent adds, four batches unrolled so the loads of the next batches
 // are issued while the adds run (4.4 cycles per add on B200, against 4.2
 // for a chain held in registers).
+// The same order over the centred squares (x - mean) * (x - mean), the
+// reference's `var += c * c` with two roundings (about 6 cycles per add:
+// the subtract and multiply issue between the dependent adds).
+template <int D, int C>
+__device__ __forceinline__ float ordered_sq_sum(const float* seg0, float mean) {
+  using S = LlShape<D, C>;
+  constexpr int kPerSeg = S::BN / 32;
+  float sum = 0.0f;
+#pragma unroll 4
+  for (int bt = 0; bt < D / 32; ++bt) {
+    const float4* r4 = reinterpret_cast<const float4*>(seg0 + (bt / kPerSeg) * S::XSEG) + 8 * (bt % kPerSeg);
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = r4[u];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float c0 = __fsub_rn(v[u].x, mean), c1 = __fsub_rn(v[u].y, mean);
+      const float c2 = __fsub_rn(v[u].z, mean), c3 = __fsub_rn(v[u].w, mean);
+      sum = __fadd_rn(sum, __fmul_rn(c0, c0));
+      sum = __fadd_rn(sum, __fmul_rn(c1, c1));
+      sum = __fadd_rn(sum, __fmul_rn(c2, c2));
+      sum = __fadd_rn(sum, __fmul_rn(c3, c3));
+    }
+  }
+  return sum;
+}
+
 template <int D, int C>
 __device__ __forceinline__ float ordered_row_sum(const float* seg0) {
   using S = LlShape<D, C>;
@@ -199,9 +218,8 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
   uint8_t* smem_b = smem + stages * kLlBM * kLlBK;     // stages x BN * 128
   // After the last MMA the ring holds the outgoing segments [owner][R][SLD].
   float* staging = reinterpret_cast<float*>(smem);
-  // Incoming rows [source CTA][R][SLD] and their centred squares.
+  // Incoming rows [source CTA][R][SLD].
   float* xbuf = reinterpret_cast<float*>(smem_b + stages * BN * kLlBK);
-  float* sqbuf = xbuf + C * XSEG;
   __shared__ __align__(8) uint64_t full_bar[kLlMaxStages];
   __shared__ __align__(8) uint64_t empty_bar[kLlMaxStages];
   __shared__ __align__(8) uint64_t tfull_bar;
@@ -266,9 +284,22 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
     }
   }
 
+  uint32_t tmem_base = 0;
+  if (warp != 0) {
+    if (warp == 1) {
+      tmem_alloc(&tmem_base_s, S::TCOLS);
+      tmem_relinquish();
+    }
+    tc_fence_before();
+    asm volatile("bar.sync 1, %0;" ::"n"(kLlThreads - 32) : "memory");  // every warp but 0
+    tc_fence_after();
+    tmem_base = tmem_base_s;
+  }
+
   // Epilogue warps 2..9: tile row t (TMEM lane t); the warp's half h takes
-  // the 32-column chunks h, h + 2, ... of the row; its residual values are
-  // loaded now, while the MMAs run.
+  // the 32-column chunks h, h + 2, ... of the row.  Its residual values are
+  // loaded while the MMAs run (after the barrier above, which would
+  // otherwise wait for them).
   const bool epi = warp >= 2 && warp < 2 + kLlEpiWarps;
   const int quarter = warp & 3;
   const int half = (warp - 2) >> 2;
@@ -291,17 +322,6 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
         res[32 * i + 4 * j4 + 3] = v.w;
       }
     }
-  }
-  uint32_t tmem_base = 0;
-  if (warp != 0) {
-    if (warp == 1) {
-      tmem_alloc(&tmem_base_s, S::TCOLS);
-      tmem_relinquish();
-    }
-    tc_fence_before();
-    asm volatile("bar.sync 1, %0;" ::"n"(kLlThreads - 32) : "memory");  // every warp but 0
-    tc_fence_after();
-    tmem_base = tmem_base_s;
   }
   bool ready = true;
 
@@ -384,22 +404,8 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
   if (warp == 2 && lane < R)  // normalize_row's first left-to-right sum, one thread per row
     s_mean[lane] = ordered_row_sum<D, C>(xbuf + lane * SLD) / fd;
   __syncthreads();
-  // centred values c = x - mean (in place) and their squares c * c, all threads
-  for (int idx = threadIdx.x; idx < R * kVec; idx += kLlThreads) {
-    const int i = idx / kVec, c4 = idx - i * kVec;
-    const int off = (c4 / SEGV) * XSEG + i * SLD + 4 * (c4 % SEGV);
-    const float mean = s_mean[i];
-    float4* xp = reinterpret_cast<float4*>(xbuf + off);
-    const float4 xv = *xp;
-    const float4 c = make_float4(__fsub_rn(xv.x, mean), __fsub_rn(xv.y, mean), __fsub_rn(xv.z, mean),
-                                 __fsub_rn(xv.w, mean));
-    *xp = c;
-    *reinterpret_cast<float4*>(sqbuf + off) =
-        make_float4(__fmul_rn(c.x, c.x), __fmul_rn(c.y, c.y), __fmul_rn(c.z, c.z), __fmul_rn(c.w, c.w));
-  }
-  __syncthreads();
-  if (warp == 2 && lane < R) {  // the second sum: var = sum(c * c) / d
-    const float var = ordered_row_sum<D, C>(sqbuf + lane * SLD) / fd;
+  if (warp == 2 && lane < R) {  // the second sum: var = sum((x - mean)^2) / d
+    const float var = ordered_sq_sum<D, C>(xbuf + lane * SLD, s_mean[lane]) / fd;
     s_inv[lane] = 1.0f / sqrtf(var + kLlEps);
   }
   __syncthreads();
@@ -415,8 +421,10 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
 #pragma unroll 2
     for (int i = i0; i < rows_here; i += kGroups) {
       const int grow = row0 + static_cast<int>(rank) * R + i;
-      const float inv = s_inv[i];
-      const float4 c = *reinterpret_cast<const float4*>(xbuf + coff + i * SLD);
+      const float inv = s_inv[i], mean = s_mean[i];
+      const float4 xv = *reinterpret_cast<const float4*>(xbuf + coff + i * SLD);
+      const float4 c = make_float4(__fsub_rn(xv.x, mean), __fsub_rn(xv.y, mean), __fsub_rn(xv.z, mean),
+                                   __fsub_rn(xv.w, mean));
       float4 v;
       v.x = __fadd_rn(__fmul_rn(__fmul_rn(c.x, inv), g.x), b.x);
       v.y = __fadd_rn(__fmul_rn(__fmul_rn(c.y, inv), g.y), b.y);
