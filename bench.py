@@ -278,9 +278,10 @@ def reduce_job(tokens, dev_ms, wall_s, world, device):
 # by the engine's algorithmic byte count for the same launch).  The bench
 # scales it to its own launches; classes without a capture report null.
 DRAM_PER_ALGO_BYTE = {
-    "attn_cross": 165.4 / 147.3,   # 1,024 rows, 35,325 keys, 8-row TMA boxes
-    "attn_self": 165.4 / 147.3,    # same kernel and page layout
-    "gemm_vocab": 17.12 / 17.16,   # M=1,024, N=32,000, K=512
+    "attn_cross": 241.9 / 223.8,   # 1,024 rows, 54,009 keys, 8-row TMA boxes
+    "attn_self": 241.9 / 223.8,    # same kernel and page layout
+    "gemm_vocab": 18.66 / 17.17,   # M=1,024, N=32,000, K=512
+    "gemm_ln": 2.94 / 5.51,        # 1,024 rows, d=512, K=512; outputs stay in L2
     "layernorm": 4.24 / 6.82,      # 1,024 rows; outputs still in L2 at exit
 }
 
@@ -502,6 +503,12 @@ def run_cuda(args):
             name, r = max(prof.items(), key=lambda kv: kv[1]["ms"])
             roofline = class_roofline(name, r, peaks, peak_kind)
             roofline["share_of_profiled_time"] = r["ms"] / sum(v["ms"] for v in prof.values())
+            # every class beside the dominant one: the HBM-bound attention
+            # and the tensor-bound vocabulary GEMM next to the latency-bound
+            # fused linear + LayerNorm
+            roofline["classes"] = {
+                k: {key: c[key] for key in ("bound", "frac", "achieved", "unit", "avg_launch_us")}
+                for k, c in ((k, class_roofline(k, v, peaks, peak_kind)) for k, v in prof.items() if v["launches"])}
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             threads = host_threads()
