@@ -227,7 +227,7 @@ struct mc_engine {
   int32_t *cross_pages_d = nullptr, *self_pages_d = nullptr;
   std::vector<float*> cross_k, cross_v, self_k, self_v;
   // tensor maps of the pools for the decode attention (encode_tmap_kv)
-  std::vector<CUtensorMap> cross_k_map, cross_v_map, self_k_map, self_v_map;
+  std::vector<KvBoxMaps> cross_k_map, cross_v_map, self_k_map, self_v_map;
   std::vector<int32_t> free_cross, free_self, free_slots;
 
   std::vector<Lane> lanes;
@@ -934,10 +934,12 @@ mc_status allocate_buffers(mc_engine* e) {
     }
   }
   const int group_cols = 4 * (d / e->heads);
-  auto kv_maps = [&](const std::vector<float*>& pools, std::vector<CUtensorMap>* maps) {
+  auto kv_maps = [&](const std::vector<float*>& pools, std::vector<KvBoxMaps>* maps) {
     maps->resize(pools.size());
     for (size_t l = 0; l < pools.size(); ++l)
-      if (!encode_tmap_kv(&(*maps)[l], pools[l], pool_rows, d, e->page_tokens, group_cols)) return false;
+      for (int i = 0; i < 4; ++i)
+        if (!encode_tmap_kv(&(*maps)[l].box[i], pools[l], pool_rows, d, e->page_tokens, group_cols, 8 >> i))
+          return false;
     return true;
   };
   if (!kv_maps(e->cross_k, &e->cross_k_map) || !kv_maps(e->cross_v, &e->cross_v_map) ||

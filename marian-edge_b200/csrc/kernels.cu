@@ -621,9 +621,10 @@ __global__ void __launch_bounds__(kEncWarps * 32) attn_encoder_kernel(
 // Warp 4 is the producer: for every item it streams the group's
 // slices of the cached keys, then of the values, into a 2-slot shared-memory
 // ring, one chunk of 32 keys per slot, with one 3-D TMA copy per 8 cache
-// rows (8 rows x 4 * HD floats of one page, through the pool's tensor map;
-// see encode_tmap_kv) completing on the slot's mbarrier, so at most 7 rows
-// past an item's last key are read.  The copies of the next chunks and
+// rows (8 rows x 4 * HD floats of one page, through the pool's tensor maps;
+// see encode_tmap_kv) completing on the slot's mbarrier; an item's last,
+// partial group of keys is copied with a box of 4, 2 or 1 rows, so at most
+// 3 rows past its last key are read.  The copies of the next chunks and
 // items are in flight while warps 0..3 (one per head of the group) consume
 // the current slot.  The 128-byte swizzle of the copies puts the 16-byte
 // chunk c of key row r at chunk c ^ (r % 8) of its line, so the lanes'
@@ -666,6 +667,23 @@ __device__ __forceinline__ int swz(int t, int f, int box_floats) {
   return (t >> 3) * box_floats + cb * 256 + r * 32 + ((c ^ r) << 2) + (f & 3);
 }
 
+// A slot's last group of keys may come in a box of R = 4, 2 or 1 rows
+// ([column block][R rows][32 floats], line l = block * R + row, chunk c at
+// c ^ (l & 7)); keys of earlier groups are in 8-row boxes.  last_box: index
+// of the slot's last box; tail_rows: its R.
+__device__ __forceinline__ int swz_tail(int t, int f, int box_floats, int last_box, int tail_rows) {
+  const int b = t >> 3, r = t & 7, cb = f >> 5, c = (f & 31) >> 2;
+  const int rows = b == last_box ? tail_rows : 8;
+  const int line = cb * rows + r;
+  return b * box_floats + line * 32 + ((c ^ (line & 7)) << 2) + (f & 3);
+}
+
+// Rows of the box that holds the last n - 8 * ((n - 1) / 8) keys of a slot.
+__device__ __forceinline__ int tail_box_rows(int n) {
+  const int nr = n - 8 * ((n - 1) >> 3);
+  return nr <= 1 ? 1 : (nr <= 2 ? 2 : (nr <= 4 ? 4 : 8));
+}
+
 // Three CTAs share an SM (15 warps: four on some sub-partition, whose 16K
 // registers then allow 128 per thread), so twelve consumer warps per SM
 // overlap their dependent chains.
@@ -675,7 +693,7 @@ __global__ void __maxnreg__(128) attn_decode_kernel(
     const int32_t* __restrict__ row_slot,
     const int32_t* __restrict__ row_order, const int32_t* __restrict__ slot_len, int len_add,
     const int32_t* __restrict__ page_table, int pages_per_slot,
-    const __grid_constant__ CUtensorMap k_map, const __grid_constant__ CUtensorMap v_map, int d,
+    const __grid_constant__ KvBoxMaps k_maps, const __grid_constant__ KvBoxMaps v_maps, int d,
     int heads, int8_t* __restrict__ out_q, float alpha, uint32_t* status) {
   constexpr int W = kDecGroup * HD;
   constexpr int kBoxFloats = 8 * W;                         // 8 rows (a multiple of 1 KB)
@@ -691,8 +709,10 @@ __global__ void __maxnreg__(128) attn_decode_kernel(
       mbar_init(&empty_bar[s], kDecGroup);
     }
     fence_barrier_init();
-    tma_prefetch_desc(&k_map);
-    tma_prefetch_desc(&v_map);
+    for (int i = 0; i < 4; ++i) {
+      tma_prefetch_desc(&k_maps.box[i]);
+      tma_prefetch_desc(&v_maps.box[i]);
+    }
   }
   __syncthreads();
   pdl_enter();
@@ -723,9 +743,11 @@ __global__ void __maxnreg__(128) attn_decode_kernel(
         continue;
       }
       for (int pass = 0; pass < 2 && ok; ++pass) {
-        const CUtensorMap* map = pass == 0 ? &k_map : &v_map;
+        const KvBoxMaps* maps = pass == 0 ? &k_maps : &v_maps;
         for (int c0 = 0; c0 < len; c0 += kDecChunk, ++k) {
-          const int nb = (min(kDecChunk, len - c0) + 7) / 8;  // 8-row boxes
+          const int n = min(kDecChunk, len - c0);
+          const int nb = (n + 7) / 8;  // boxes: 8 rows, the last one 8, 4, 2 or 1
+          const int tail_rows = tail_box_rows(n);
           const int sl = k % kDecSlots;
           bool free_slot = true;
           if (lane == 0) free_slot = mbar_wait(&empty_bar[sl], ((k / kDecSlots) & 1) ^ 1, status);
@@ -739,13 +761,16 @@ __global__ void __maxnreg__(128) attn_decode_kernel(
           if (lane == 0) {
             float* dst = dsm + sl * kSlotFloats;
             const uint32_t box_bytes = kBoxFloats * 4, q_bytes = W * 4;
-            mbar_arrive_expect_tx(&full_bar[sl], nb * box_bytes + (pass == 0 ? q_bytes : 0));
+            const uint32_t tail_bytes = (uint32_t)tail_rows * W * 4;
+            mbar_arrive_expect_tx(&full_bar[sl], (nb - 1) * box_bytes + tail_bytes + (pass == 0 ? q_bytes : 0));
             if (pass == 0)
               bulk_copy_g2s(dst + (kDecChunk / 8) * kBoxFloats, q + (size_t)r * ldq + g * W, q_bytes,
                             &full_bar[sl]);
+            const CUtensorMap* tail_map =
+                &maps->box[tail_rows == 8 ? 0 : (tail_rows == 4 ? 1 : (tail_rows == 2 ? 2 : 3))];
             for (int b = 0; b < nb; ++b)
-              tma_load_3d_hint(dst + b * kBoxFloats, map, 0, rows[b], g * (W / 32), &full_bar[sl],
-                               stream_once);
+              tma_load_3d_hint(dst + b * kBoxFloats, b == nb - 1 ? tail_map : &maps->box[0], 0, rows[b],
+                               g * (W / 32), &full_bar[sl], stream_once);
           }
         }
       }
@@ -783,12 +808,14 @@ __global__ void __maxnreg__(128) attn_decode_kernel(
       const int sl = k % kDecSlots;
       if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[sl], (k / kDecSlots) & 1, status))) return;
       const float* base = dsm + sl * kSlotFloats;
+      const int last_box = (n - 1) >> 3, tail_rows = tail_box_rows(n);
       if (lane < n) {
         const float* qh = base + (kDecChunk / 8) * kBoxFloats + h * HD;
         float dot = 0.0f;
 #pragma unroll
         for (int i = 0; i < HD; i += 4) {
-          const float4 k4 = *reinterpret_cast<const float4*>(base + swz(lane, h * HD + i, kBoxFloats));
+          const float4 k4 = *reinterpret_cast<const float4*>(
+              base + swz_tail(lane, h * HD + i, kBoxFloats, last_box, tail_rows));
           const float4 q4 = *reinterpret_cast<const float4*>(qh + i);
           dot = dot + q4.x * k4.x;
           dot = dot + q4.y * k4.y;
@@ -825,9 +852,11 @@ __global__ void __maxnreg__(128) attn_decode_kernel(
       if (active) {
         const float* base = dsm + sl * kSlotFloats;
         const int f = h * HD + 2 * lane;
+        const int last_box = (n - 1) >> 3, tail_rows = tail_box_rows(n);
 #pragma unroll 4
         for (int t = 0; t < n; ++t) {
-          const float2 v2 = *reinterpret_cast<const float2*>(base + swz(t, f, kBoxFloats));
+          const float2 v2 = *reinterpret_cast<const float2*>(
+              base + swz_tail(t, f, kBoxFloats, last_box, tail_rows));
           const float p = ph[c0 + t];
           acc0 = acc0 + v2.x * p;
           acc1 = acc1 + v2.y * p;
@@ -1249,8 +1278,8 @@ template <int HD, int PT>
 cudaError_t launch_attn_decode_hd(const float* q, int ldq, int rows, const int32_t* rows_dev,
                                   const int32_t* row_slot, const int32_t* row_order,
                                   const int32_t* slot_len, int len_add, const int32_t* page_table,
-                                  int pages_per_slot, const CUtensorMap* k_map,
-                                  const CUtensorMap* v_map, int d, int heads, int8_t* out_q,
+                                  int pages_per_slot, const KvBoxMaps* k_maps,
+                                  const KvBoxMaps* v_maps, int d, int heads, int8_t* out_q,
                                   float alpha, uint32_t* status, cudaStream_t s) {
   constexpr int W = kDecGroup * HD;
   const size_t smem = 1024 + sizeof(float) * ((size_t)kDecSlots * ((kDecChunk / 8) * 8 * W + 256) +
@@ -1276,7 +1305,7 @@ cudaError_t launch_attn_decode_hd(const float* q, int ldq, int rows, const int32
   const long long items = (long long)rows * (heads / kDecGroup);
   const int grid = (int)std::min<long long>(items, 3LL * sms[dev]);
   launch_pdl(attn_decode_kernel<HD, PT>, dim3(grid), dim3(kDecThreads), smem, s, q, ldq, rows_dev, rows,
-             row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, *k_map, *v_map, d,
+             row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, *k_maps, *v_maps, d,
              heads, out_q, alpha, status);
   return cudaGetLastError();
 }
@@ -1285,8 +1314,8 @@ template <int HD>
 cudaError_t launch_attn_decode_pt(const float* q, int ldq, int rows, const int32_t* rows_dev,
                                   const int32_t* row_slot, const int32_t* row_order,
                                   const int32_t* slot_len, int len_add, const int32_t* page_table,
-                                  int pages_per_slot, int page_tokens, const CUtensorMap* k_map,
-                                  const CUtensorMap* v_map, int d, int heads, int8_t* out_q,
+                                  int pages_per_slot, int page_tokens, const KvBoxMaps* k_map,
+                                  const KvBoxMaps* v_map, int d, int heads, int8_t* out_q,
                                   float alpha, uint32_t* status, cudaStream_t s) {
   switch (page_tokens) {
     case 8: return launch_attn_decode_hd<HD, 8>(q, ldq, rows, rows_dev, row_slot, row_order, slot_len, len_add, page_table, pages_per_slot, k_map, v_map, d, heads, out_q, alpha, status, s);
@@ -1299,8 +1328,8 @@ cudaError_t launch_attn_decode_pt(const float* q, int ldq, int rows, const int32
 cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t* rows_dev,
                                const int32_t* row_slot, const int32_t* row_order,
                                const int32_t* slot_len, int len_add, const int32_t* page_table,
-                               int pages_per_slot, int page_tokens, const CUtensorMap* k_map,
-                               const CUtensorMap* v_map, int d, int heads, int8_t* out_q,
+                               int pages_per_slot, int page_tokens, const KvBoxMaps* k_map,
+                               const KvBoxMaps* v_map, int d, int heads, int8_t* out_q,
                                float alpha, uint32_t* status, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
   if (heads % kDecGroup != 0 || d != heads * (d / heads)) return cudaErrorInvalidValue;

@@ -70,17 +70,24 @@ cudaError_t launch_attn_encoder(const float* qkv, const int32_t* cu_seqlens,
                                 const int32_t* seq_ids, int n_seqs, int max_len, int d, int heads,
                                 int8_t* out_q, float alpha, uint32_t* status, cudaStream_t s);
 
+// A KV pool's tensor maps for the decode attention: boxes of 8, 4, 2 and 1
+// cache rows (encode_tmap_kv with group_cols = 4 * d / heads).  Full groups
+// of 8 keys use the first; a row's last, partial group uses the smallest
+// box that covers it, so at most half a box is read past its last key.
+struct alignas(64) KvBoxMaps {
+  CUtensorMap box[4];  // box rows 8, 4, 2, 1
+};
+
 // tensor.rs:251-318 with one query per row over a paged cache: keys of row r
 // are cache rows page_table[slot][j / page_tokens] * page_tokens +
 // j % page_tokens for j < slot_len[slot] + len_add, read through the
-// pools' tensor maps (encode_tmap_kv with group_cols = 4 * d / heads).
-// row_order (nullable) lists the rows in the order the kernel takes them.
-// page_tokens is 8, 16 or 32.
+// pools' tensor maps.  row_order (nullable) lists the rows in the order the
+// kernel takes them.  page_tokens is 8, 16 or 32.
 cudaError_t launch_attn_decode(const float* q, int ldq, int rows, const int32_t* rows_dev,
                                const int32_t* row_slot, const int32_t* row_order,
                                const int32_t* slot_len, int len_add, const int32_t* page_table,
-                               int pages_per_slot, int page_tokens, const CUtensorMap* k_map,
-                               const CUtensorMap* v_map, int d, int heads, int8_t* out_q,
+                               int pages_per_slot, int page_tokens, const KvBoxMaps* k_maps,
+                               const KvBoxMaps* v_maps, int d, int heads, int8_t* out_q,
                                float alpha, uint32_t* status, cudaStream_t s);
 
 // Turns the packed per-row maxima into tokens (q8_engine.rs:437-449):

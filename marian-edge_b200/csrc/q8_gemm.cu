@@ -540,14 +540,15 @@ bool encode_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
 }
 
 bool encode_tmap_kv(CUtensorMap* map, const float* base, uint64_t rows, int d, int page_tokens,
-                    int group_cols) {
+                    int group_cols, int box_rows) {
   auto fn = encode_fn();
   if (!fn || !base || rows == 0 || d % 32 != 0 || group_cols % 32 != 0 || page_tokens <= 0 ||
-      page_tokens % 8 != 0 || group_cols / 32 > 256 || (reinterpret_cast<uintptr_t>(base) & 15) != 0)
+      page_tokens % 8 != 0 || group_cols / 32 > 256 || (reinterpret_cast<uintptr_t>(base) & 15) != 0 ||
+      (box_rows != 8 && box_rows != 4 && box_rows != 2 && box_rows != 1))
     return false;
   cuuint64_t dims[3] = {32, rows, static_cast<cuuint64_t>(d / 32)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * 4, 128};
-  cuuint32_t box[3] = {32, 8, static_cast<cuuint32_t>(group_cols / 32)};
+  cuuint32_t box[3] = {32, static_cast<cuuint32_t>(box_rows), static_cast<cuuint32_t>(group_cols / 32)};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box,
                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

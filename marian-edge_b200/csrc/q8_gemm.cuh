@@ -70,13 +70,15 @@ bool encode_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
 
 // Encodes a 3-D f32 tensor map over a KV-cache pool [rows, d] (row-major)
 // for the decode attention: dims {32 floats, rows, d / 32 column blocks}
-// (strides d * 4 and 128 bytes), box {32, 8, group_cols / 32} -- eight
-// cache rows' slice of group_cols columns per copy (page_tokens, a multiple
-// of 8, keeps a box inside one page) -- with the 128-byte swizzle, which
-// lands the slice in shared memory as [column block][8 rows][32 floats]
-// with the 16-byte chunk c of row r stored at chunk c ^ r.
+// (strides d * 4 and 128 bytes), box {32, box_rows, group_cols / 32} --
+// box_rows (8, 4, 2 or 1) cache rows' slice of group_cols columns per copy
+// (page_tokens, a multiple of 8, keeps a box that starts at a multiple of 8
+// inside one page) -- with the 128-byte swizzle, which lands the slice in
+// shared memory as [column block][box_rows rows][32 floats], 16-byte chunk
+// c of 128-byte line l (l = block * box_rows + row) stored at chunk
+// c ^ (l & 7).
 bool encode_tmap_kv(CUtensorMap* map, const float* base, uint64_t rows, int d, int page_tokens,
-                    int group_cols);
+                    int group_cols, int box_rows);
 
 // Picks the N tile (64, 128 or 256) for a launch.
 int pick_bn(int m, int max_n);
