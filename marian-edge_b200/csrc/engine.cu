@@ -662,9 +662,16 @@ mc_status run_encoder(mc_engine* e, Lane& L, const AdmLayout& A, double sum_len_
 // A decode linear whose output feeds residual + LayerNorm: one fused launch
 // (linear_ln.cu) when the model width allows, else the GEMM into dec_proj
 // and the LayerNorm kernel.  Both give the same bits.
+// can_project(e, w): the fused launch can also compute linear w of its
+// normalized rows (a d x d linear, the cross-attention query).
+bool can_project(const mc_engine* e, const DevLinear& w) {
+  return e->fuse_ln && w.has_ln_map && w.out == e->d && w.in == e->d;
+}
+
 mc_status linear_ln(mc_engine* e, Lane& L, int gemm_kind, const QBuf* a, const DevLinear& w,
                     const float* residual, const float* gamma, const float* beta, int cap,
-                    const int32_t* m_dev, double m_prof, float* out, const QuantOut& q) {
+                    const int32_t* m_dev, double m_prof, float* out, const QuantOut& q,
+                    const DevLinear* proj = nullptr, float* proj_out = nullptr) {
   const int d = e->d;
   const double rows_d = m_prof * d;
   if (e->fuse_ln && w.has_ln_map && w.out == d) {
@@ -685,12 +692,25 @@ mc_status linear_ln(mc_engine* e, Lane& L, int gemm_kind, const QBuf* a, const D
     p.m_dev = m_dev;
     p.k = w.in;
     p.status = L.d_status;
-    const double flops = 2.0 * rows_d * w.in;
-    const double bytes = m_prof * w.in + (double)d * w.in + 16.0 * d + rows_d * (8 + q.count);
+    double flops = 2.0 * rows_d * w.in;
+    double bytes = m_prof * w.in + (double)d * w.in + 16.0 * d + rows_d * (8 + q.count);
+    if (proj) {  // the cross-attention query from the normalized rows, same launch
+      p.proj = 1;
+      p.tmap_b2 = proj->tmap_ln;
+      p.col_scale2 = proj->per_row ? proj->col_scale : nullptr;
+      p.uniform_scale2 = proj->scale;
+      p.bias2 = proj->bias;
+      p.out2 = proj_out;
+      p.ldo2 = d;
+      p.alpha2 = proj->alpha;
+      flops += 2.0 * rows_d * d;
+      bytes += (double)d * d + 8.0 * d + 4.0 * rows_d;
+    }
     PROFILED(MC_K_GEMM_LN, flops, bytes, CK(launch_q8_linear_ln(p, d, L.cur)));
     ++e->launches;
     return MC_OK;
   }
+  if (proj) return fail(e, MC_CUDA, "fused projection requested without the fused kernel");
   GroupSpec spec = {a, &w, kEpiF32, L.dec_proj, d, 0, nullptr, false, 0.f};
   mc_status st = gemm(e, L, gemm_kind, cap, m_dev, m_prof, &spec, 1);
   if (st) return st;
@@ -738,6 +758,7 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap, const std::vector<int3
   for (int l = 0; l < e->dec_layers; ++l) {
     const DevAttention& c = e->dec_ctx[l];
     const DevFfn& f = e->dec_ffn[l];
+    bool q_done = false;  // the cross-attention query came with the first LayerNorm
     if (e->kind == 1) {
       const DevAttention& a = e->dec_self[l];
       GroupSpec qkv[3] = {
@@ -750,9 +771,19 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap, const std::vector<int3
                                      e->self_pages_d, e->pages_per_slot, e->page_tokens,
                                      &e->self_k_map[l], &e->self_v_map[l], d, e->heads, L.dec_o.p,
                                      a.wo.alpha, L.d_status, L.cur)));
-      if ((st = linear_ln(e, L, MC_K_GEMM_OUT, &L.dec_o, a.wo, x, a.ln_g, a.ln_b, cap, nrows, R, y,
-                          quant_out(L.dec_q, {c.wq.alpha}))))
+      // the first LayerNorm's rows also feed the cross-attention query:
+      // one launch computes both when the fused kernel applies
+      if (can_project(e, c.wq) && a.wo.has_ln_map && a.wo.out == d) {
+        QuantOut none;
+        std::memset(&none, 0, sizeof(none));
+        if ((st = linear_ln(e, L, MC_K_GEMM_OUT, &L.dec_o, a.wo, x, a.ln_g, a.ln_b, cap, nrows, R, y, none,
+                            &c.wq, L.dec_qkv)))
+          return st;
+        q_done = true;
+      } else if ((st = linear_ln(e, L, MC_K_GEMM_OUT, &L.dec_o, a.wo, x, a.ln_g, a.ln_b, cap, nrows, R, y,
+                                 quant_out(L.dec_q, {c.wq.alpha})))) {
         return st;
+      }
       ++e->launches;
     } else {
       const DevSsru& s = e->dec_ssru[l];
@@ -767,8 +798,10 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap, const std::vector<int3
       ++e->launches;
     }
     std::swap(x, y);
-    GroupSpec wq = {&L.dec_q[0], &c.wq, kEpiF32, L.dec_qkv, d, 0, nullptr, false, 0.f};
-    if ((st = gemm(e, L, MC_K_GEMM_QKV, cap, nrows, R, &wq, 1))) return st;
+    if (!q_done) {
+      GroupSpec wq = {&L.dec_q[0], &c.wq, kEpiF32, L.dec_qkv, d, 0, nullptr, false, 0.f};
+      if ((st = gemm(e, L, MC_K_GEMM_QKV, cap, nrows, R, &wq, 1))) return st;
+    }
     PROFILED(MC_K_ATTN_CROSS, 4.0 * cross_keys * d, 8.0 * cross_keys * d + rows_d * 5,
              CK(launch_attn_decode(L.dec_qkv, d, cap, nrows, row_slot, order_cross, e->slot_src, 0,
                                    e->cross_pages_d, e->pages_per_slot, e->page_tokens,

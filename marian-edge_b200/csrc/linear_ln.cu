@@ -122,22 +122,43 @@ struct LlShape {
   static constexpr int XBYTES = C * XSEG * 4;       // the incoming rows
   static constexpr int STAGING = C * XSEG * 4;      // outgoing segments (in the ring)
   static constexpr int MIN_STAGES = (STAGING + STAGE - 1) / STAGE;
+  // second linear (proj): its A operand, the block's 128 normalized rows
+  // quantized, K = d in 128-byte k-blocks ([k-block][128 rows][128 B],
+  // 128-byte swizzle), and this CTA's rows of it staged for the peers
+  // ([k-block][R rows][128 B]) -- both in the idle ring after the outgoing
+  // segments; W2's [k-block][BN rows][128 B] after the exchange buffer.
+  static constexpr int KB2 = D / 128;
+  static constexpr int A2_OFF = (STAGING + 1023) / 1024 * 1024;
+  static constexpr int OUT_OFF = A2_OFF + KB2 * 16384;
+  static constexpr int PROJ_END = OUT_OFF + KB2 * R * 128;
+  static constexpr int MIN_STAGES_PROJ = (PROJ_END + STAGE - 1) / STAGE;
+  static constexpr int XBYTES_AL = (XBYTES + 1023) / 1024 * 1024;
+  static constexpr int B2_BYTES = KB2 * BN * 128;
+  static constexpr int TCOLS2 = 2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : 256);
   static_assert(D % 128 == 0 && BN % 32 == 0 && BN <= 128 && kLlBM % C == 0 && R <= 32 && R >= 8,
                 "unsupported fused LayerNorm shape");
   static_assert((XSEG * 4) % 16 == 0, "bulk copies move 16-byte multiples");
 };
 
-template <int D, int C>
+template <int D, int C, bool PROJ>
 constexpr int ll_smem_bytes(int stages) {
-  return stages * LlShape<D, C>::STAGE + LlShape<D, C>::XBYTES + 1024;
+  using S = LlShape<D, C>;
+  return stages * S::STAGE + S::XBYTES_AL + (PROJ ? S::B2_BYTES : 0) + 1024;
 }
 
 // Ring depth: up to kLlMaxStages within 218 KB of dynamic shared memory
 // (the static arrays take the rest of the 227 KB per-CTA limit).
-template <int D, int C>
+template <int D, int C, bool PROJ>
 constexpr int ll_max_stages() {
-  constexpr int fit = (218 * 1024 - LlShape<D, C>::XBYTES - 1024) / LlShape<D, C>::STAGE;
+  using S = LlShape<D, C>;
+  constexpr int fit = (218 * 1024 - S::XBYTES_AL - (PROJ ? S::B2_BYTES : 0) - 1024) / S::STAGE;
   return fit < kLlMaxStages ? fit : kLlMaxStages;
+}
+
+template <int D, int C, bool PROJ>
+constexpr int ll_min_stages() {
+  using S = LlShape<D, C>;
+  return PROJ && S::MIN_STAGES_PROJ > S::MIN_STAGES ? S::MIN_STAGES_PROJ : S::MIN_STAGES;
 }
 
 // Bulk copy of `bytes` from this CTA's shared memory to a cluster peer's,
@@ -204,9 +225,10 @@ __device__ __forceinline__ float ordered_row_sum(const float* seg0) {
   return sum;
 }
 
-template <int D, int C>
+template <int D, int C, bool PROJ>
 __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const __grid_constant__ LinearLnParams p) {
   using S = LlShape<D, C>;
+  constexpr int TCOLS = PROJ ? S::TCOLS2 : S::TCOLS;  // the second accumulator at column BN
   constexpr int BN = S::BN, R = S::R, SLD = S::SLD, XSEG = S::XSEG;
   constexpr int kLlThreads = ll_threads<D>();
   constexpr int CHUNKS = BN / 32;                 // 32-column TMEM chunks per tile row
@@ -220,10 +242,14 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
   float* staging = reinterpret_cast<float*>(smem);
   // Incoming rows [source CTA][R][SLD].
   float* xbuf = reinterpret_cast<float*>(smem_b + stages * BN * kLlBK);
+  uint8_t* a2 = smem + S::A2_OFF;                       // proj: its A operand
+  uint8_t* a2_out = smem + S::OUT_OFF;                  // proj: this CTA's rows of it
+  uint8_t* b2 = reinterpret_cast<uint8_t*>(xbuf) + S::XBYTES_AL;  // proj: W2's columns
   __shared__ __align__(8) uint64_t full_bar[kLlMaxStages];
   __shared__ __align__(8) uint64_t empty_bar[kLlMaxStages];
   __shared__ __align__(8) uint64_t tfull_bar;
   __shared__ __align__(8) uint64_t x_bar;
+  __shared__ __align__(8) uint64_t b2_bar, a2_bar, t2_bar;  // proj
   __shared__ uint32_t tmem_base_s;
   __shared__ __align__(16) float s_bias[BN];
   __shared__ __align__(16) float s_scale[BN];
@@ -231,6 +257,8 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
   __shared__ __align__(16) float s_beta[D];
   __shared__ float s_mean[R];
   __shared__ float s_inv[R];
+  __shared__ __align__(16) float s_bias2[PROJ ? BN : 1];
+  __shared__ __align__(16) float s_scale2[PROJ ? BN : 1];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -246,6 +274,10 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
   if (threadIdx.x < BN) {
     s_bias[threadIdx.x] = p.bias ? p.bias[n0 + threadIdx.x] : 0.0f;
     s_scale[threadIdx.x] = p.col_scale ? p.col_scale[n0 + threadIdx.x] : p.uniform_scale;
+    if constexpr (PROJ) {
+      s_bias2[threadIdx.x] = p.bias2 ? p.bias2[n0 + threadIdx.x] : 0.0f;
+      s_scale2[threadIdx.x] = p.col_scale2 ? p.col_scale2[n0 + threadIdx.x] : p.uniform_scale2;
+    }
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -257,6 +289,14 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
     // the owner's own arrival: the phase completes when the other C - 1
     // CTAs' segments of its R rows have landed (its own are plain stores)
     mbar_arrive_expect_tx(&x_bar, static_cast<uint32_t>((C - 1) * XSEG * 4));
+    if constexpr (PROJ) {
+      mbar_init(&b2_bar, 1);
+      mbar_init(&a2_bar, 1);
+      // the other C - 1 CTAs' R quantized rows of every k-block
+      mbar_arrive_expect_tx(&a2_bar, static_cast<uint32_t>((C - 1) * S::KB2 * R * 128));
+      mbar_init(&t2_bar, 1);
+      tma_prefetch_desc(&p.tmap_b2);
+    }
     fence_barrier_init();
     tma_prefetch_desc(&p.tmap_a);
     tma_prefetch_desc(&p.tmap_b);
@@ -281,13 +321,18 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
         tma_load_2d(smem_a + s * kLlBM * kLlBK, &p.tmap_a, kb * kLlBK, row0, &full_bar[s]);
         tma_load_2d_hint(smem_b + s * BN * kLlBK, &p.tmap_b, kb * kLlBK, n0, &full_bar[s], keep);
       }
+      if constexpr (PROJ) {  // W2's columns, needed after the LayerNorm
+        mbar_arrive_expect_tx(&b2_bar, S::B2_BYTES);
+        for (int kb = 0; kb < S::KB2; ++kb)
+          tma_load_2d_hint(b2 + kb * BN * kLlBK, &p.tmap_b2, kb * kLlBK, n0, &b2_bar, keep);
+      }
     }
   }
 
   uint32_t tmem_base = 0;
   if (warp != 0) {
     if (warp == 1) {
-      tmem_alloc(&tmem_base_s, S::TCOLS);
+      tmem_alloc(&tmem_base_s, TCOLS);
       tmem_relinquish();
     }
     tc_fence_before();
@@ -395,8 +440,9 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
   const bool got = mbar_wait_cluster(&x_bar, 0, p.status) && ready;
   // Everything bound for this CTA has arrived: its peers may leave once
   // every CTA has said so (the matching wait ends the kernel), so no bulk
-  // copy ever reads from or writes to an exited CTA.
-  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+  // copy ever reads from or writes to an exited CTA.  (With a projection
+  // the quantized rows arrive later; the arrival waits for them.)
+  if constexpr (!PROJ) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
   constexpr int kVec = D / 4;
   constexpr int SEGV = BN / 4;  // float4 per row segment
   const float fd = static_cast<float>(D);
@@ -433,45 +479,117 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
       const long long elem = (long long)grow * D + 4 * c4;
       *reinterpret_cast<float4*>(p.out + elem) = v;
       store_copies(p.q, elem, v, p.status);
+      if constexpr (PROJ) {
+        // quantize_one for W2 (finiteness reported by store_copies' test
+        // when q has copies, else here), into A2 row rank * R + i and the
+        // staged copy for the peers, both 128-byte swizzled
+        if (p.q.count == 0 && (!(fabsf(v.x) <= 3.402823466e38f) || !(fabsf(v.y) <= 3.402823466e38f) ||
+                               !(fabsf(v.z) <= 3.402823466e38f) || !(fabsf(v.w) <= 3.402823466e38f)))
+          flag_status(p.status, kStatusNonFinite);
+        const uint32_t lo = __byte_perm((uint32_t)quant_s8(v.x, p.alpha2), (uint32_t)quant_s8(v.y, p.alpha2), 0x0040);
+        const uint32_t hi = __byte_perm((uint32_t)quant_s8(v.z, p.alpha2), (uint32_t)quant_s8(v.w, p.alpha2), 0x0040);
+        const uint32_t word = __byte_perm(lo, hi, 0x5410);
+        const int byte = 4 * c4, kb = byte >> 7, cc = byte & 127;
+        const int t2 = static_cast<int>(rank) * R + i;  // the row in the block
+        *reinterpret_cast<uint32_t*>(a2 + kb * 16384 + t2 * 128 + ((((cc >> 4) ^ (t2 & 7))) << 4) + (cc & 15)) = word;
+        *reinterpret_cast<uint32_t*>(a2_out + kb * (R * 128) + i * 128 + ((((cc >> 4) ^ (i & 7))) << 4) + (cc & 15)) =
+            word;
+      }
+    }
+  }
+  if constexpr (PROJ) {
+    // ---- the second linear: exchange the quantized rows, MMA, epilogue ----
+    fence_proxy_async_smem();  // A2 and the staged rows are read by the async proxy
+    __syncthreads();
+    if (threadIdx.x == 0 && got) {
+      for (int o = 0; o < C; ++o) {
+        if (o == static_cast<int>(rank)) continue;
+        const uint32_t peer_bar = map_shared_rank(smem_u32(&a2_bar), o);
+        for (int kb = 0; kb < S::KB2; ++kb)
+          bulk_copy_to_peer(map_shared_rank(smem_u32(a2 + kb * 16384 + static_cast<int>(rank) * R * 128), o),
+                            a2_out + kb * (R * 128), R * 128, peer_bar);
+      }
+    }
+    const bool got2 = mbar_wait_cluster(&a2_bar, 0, p.status) && got;
+    asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");  // see above
+    if (warp == 1 && lane == 0 && got2 && mbar_wait(&b2_bar, 0, p.status)) {
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_i8(kLlBM, BN);
+#pragma unroll
+      for (int kb = 0; kb < S::KB2; ++kb)
+#pragma unroll
+        for (int kk = 0; kk < kLlBK / 32; ++kk)
+          mma_i8(tmem_base + BN, sdesc_k_sw128(smem_u32(a2 + kb * 16384) + kk * 32),
+                 sdesc_k_sw128(smem_u32(b2 + kb * BN * kLlBK) + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+      mma_commit(&t2_bar);
+    }
+    if (epi) {
+      const bool ready2 = __all_sync(0xffffffffu, mbar_wait(&t2_bar, 0, p.status));
+      if (ready2) {
+        tc_fence_after();
+        const uint32_t lane_base = tmem_base + BN + (static_cast<uint32_t>(quarter * 32) << 16);
+        float* orow = p.out2 + (size_t)(row_ok ? row : 0) * p.ldo2 + n0;
+#pragma unroll
+        for (int i = 0; i < MY_CHUNKS; ++i) {
+          const int c0 = 32 * (half + 2 * i);
+          if (c0 >= BN) break;
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(lane_base + c0, r);
+          tmem_ld_wait();
+          if (row_ok) {
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              float y[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int j = 4 * j4 + u;
+                y[u] = dequant(static_cast<int32_t>(r[j]), s_scale2[c0 + j], s_bias2[c0 + j]);
+              }
+              *reinterpret_cast<float4*>(orow + c0 + 4 * j4) = make_float4(y[0], y[1], y[2], y[3]);
+            }
+          }
+        }
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, S::TCOLS);
+    tmem_dealloc(tmem_base, TCOLS);
   }
   asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
 }
 
-template <int D, int C>
+template <int D, int C, bool PROJ>
 cudaError_t configure_ll() {
   static unsigned long long configured = 0;  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured & (1ull << (dev & 63)))) {
-    cudaError_t e = cudaFuncSetAttribute(q8_linear_ln_kernel<D, C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         ll_smem_bytes<D, C>(ll_max_stages<D, C>()));
+    cudaError_t e = cudaFuncSetAttribute(q8_linear_ln_kernel<D, C, PROJ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         ll_smem_bytes<D, C, PROJ>(ll_max_stages<D, C, PROJ>()));
     if (e != cudaSuccess) return e;
     configured |= 1ull << (dev & 63);
   }
   return cudaSuccess;
 }
 
-template <int D, int C>
+template <int D, int C, bool PROJ>
 cudaError_t launch_ll(LinearLnParams p, cudaStream_t stream) {
-  cudaError_t e = configure_ll<D, C>();
+  static_assert(ll_min_stages<D, C, PROJ>() <= ll_max_stages<D, C, PROJ>(), "shared memory plan");
+  cudaError_t e = configure_ll<D, C, PROJ>();
   if (e != cudaSuccess) return e;
   const int num_kb = (p.k + kLlBK - 1) / kLlBK;
   // as deep as K (within the budget), and deep enough to hold the outgoing
-  // segments after the last MMA
-  int stages = num_kb < ll_max_stages<D, C>() ? num_kb : ll_max_stages<D, C>();
-  if (stages < LlShape<D, C>::MIN_STAGES) stages = LlShape<D, C>::MIN_STAGES;
+  // segments (and, with a projection, its operand) after the last MMA
+  int stages = num_kb < ll_max_stages<D, C, PROJ>() ? num_kb : ll_max_stages<D, C, PROJ>();
+  if (stages < ll_min_stages<D, C, PROJ>()) stages = ll_min_stages<D, C, PROJ>();
   p.stages = stages;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(C, (p.cap + kLlBM - 1) / kLlBM);
   cfg.blockDim = dim3(ll_threads<D>());
-  cfg.dynamicSmemBytes = ll_smem_bytes<D, C>(p.stages);
+  cfg.dynamicSmemBytes = ll_smem_bytes<D, C, PROJ>(p.stages);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -482,8 +600,19 @@ cudaError_t launch_ll(LinearLnParams p, cudaStream_t stream) {
   attr[1].val.programmaticStreamSerializationAllowed = kProgrammaticLaunch ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  e = cudaLaunchKernelEx(&cfg, q8_linear_ln_kernel<D, C>, p);
+  e = cudaLaunchKernelEx(&cfg, q8_linear_ln_kernel<D, C, PROJ>, p);
   return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+template <int D, int C>
+cudaError_t launch_ll_any(const LinearLnParams& p, cudaStream_t stream) {
+  return p.proj ? launch_ll<D, C, true>(p, stream) : launch_ll<D, C, false>(p, stream);
+}
+
+template <int D, int C>
+cudaError_t configure_ll_both() {
+  cudaError_t e = configure_ll<D, C, false>();
+  return e == cudaSuccess ? configure_ll<D, C, true>() : e;
 }
 
 }  // namespace
@@ -499,21 +628,23 @@ int linear_ln_cluster(int d) {
 }
 
 cudaError_t prepare_q8_linear_ln() {
-  cudaError_t e = configure_ll<128, 4>();
-  if (e == cudaSuccess) e = configure_ll<256, 8>();
-  if (e == cudaSuccess) e = configure_ll<384, 4>();
-  if (e == cudaSuccess) e = configure_ll<512, 8>();
+  cudaError_t e = configure_ll_both<128, 4>();
+  if (e == cudaSuccess) e = configure_ll_both<256, 8>();
+  if (e == cudaSuccess) e = configure_ll_both<384, 4>();
+  if (e == cudaSuccess) e = configure_ll_both<512, 8>();
   return e;
 }
 
 cudaError_t launch_q8_linear_ln(const LinearLnParams& p, int d, cudaStream_t stream) {
   if (p.cap <= 0) return cudaSuccess;
-  if (p.k <= 0 || p.k % 16 != 0 || p.q.count < 0 || p.q.count > kMaxQuantOut) return cudaErrorInvalidValue;
+  if (p.k <= 0 || p.k % 16 != 0 || p.q.count < 0 || p.q.count > kMaxQuantOut ||
+      (p.proj && (!p.out2 || p.ldo2 < d)))
+    return cudaErrorInvalidValue;
   switch (d) {
-    case 128: return launch_ll<128, 4>(p, stream);
-    case 256: return launch_ll<256, 8>(p, stream);
-    case 384: return launch_ll<384, 4>(p, stream);
-    case 512: return launch_ll<512, 8>(p, stream);
+    case 128: return launch_ll_any<128, 4>(p, stream);
+    case 256: return launch_ll_any<256, 8>(p, stream);
+    case 384: return launch_ll_any<384, 4>(p, stream);
+    case 512: return launch_ll_any<512, 8>(p, stream);
     default: return cudaErrorInvalidValue;
   }
 }

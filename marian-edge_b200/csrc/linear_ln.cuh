@@ -19,6 +19,7 @@ namespace mc {
 struct alignas(64) LinearLnParams {
   CUtensorMap tmap_a;        // A [rows, K] int8, box {128, 128}, 128-byte swizzle
   CUtensorMap tmap_b;        // W [d, K] int8, box {128, d / linear_ln_cluster(d)}
+  CUtensorMap tmap_b2;       // proj: W2 [d, d] int8, box {128, d / linear_ln_cluster(d)}
   const float* col_scale;    // [d] per-column dequantization scale, or null
   float uniform_scale;       // used when col_scale is null
   const float* bias;         // [d] or null
@@ -33,6 +34,17 @@ struct alignas(64) LinearLnParams {
   int32_t k;                 // inner dimension (multiple of 16)
   int32_t stages;            // shared-memory ring depth (set by the launcher)
   uint32_t* status;          // device status word (error bits)
+  // proj != 0: the normalized rows are also the input of a second Q8 linear
+  // W2 [d, d] (the decoder's cross-attention query after its first
+  // LayerNorm): out2 = dequant(quantize(out, alpha2) x W2^T) * scale2 +
+  // bias2, computed in the same launch.
+  int32_t proj;
+  const float* col_scale2;   // [d] or null
+  float uniform_scale2;
+  const float* bias2;        // [d] or null
+  float* out2;               // [rows, ldo2]
+  int32_t ldo2;
+  float alpha2;              // W2's activation alpha
 };
 
 // CTAs per cluster for model width d (each owns d / C output columns of a
