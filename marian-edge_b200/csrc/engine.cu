@@ -54,6 +54,8 @@ struct DevLinear {
   CUtensorMap tmap_b[3];       // W tensor maps for BN = 64, 128, 256
   CUtensorMap tmap_ln;         // W tensor map for the fused LayerNorm kernel
   bool has_ln_map = false;     // (box out / linear_ln_cluster(out) rows)
+  CUtensorMap tmap_proj;       // W as the fused kernel's second linear
+  bool has_proj_map = false;   // (box out / linear_ln_cluster(in) rows)
 };
 
 struct DevAttention {
@@ -428,6 +430,13 @@ mc_status upload_linear(mc_engine* e, const std::string& wname, const char* bnam
       return fail(e, MC_MODEL, wname + ": tensor map rejected");
     L->has_ln_map = true;
   }
+  if (const int c = linear_ln_cluster(L->in)) {
+    if (L->out % c == 0 && L->out / c <= 256 && (L->out / c) % 32 == 0) {
+      if (!encode_tmap_i8(&L->tmap_proj, L->w, L->out, L->in, L->out / c))
+        return fail(e, MC_MODEL, wname + ": tensor map rejected");
+      L->has_proj_map = true;
+    }
+  }
   return MC_OK;
 }
 
@@ -662,16 +671,21 @@ mc_status run_encoder(mc_engine* e, Lane& L, const AdmLayout& A, double sum_len_
 // A decode linear whose output feeds residual + LayerNorm: one fused launch
 // (linear_ln.cu) when the model width allows, else the GEMM into dec_proj
 // and the LayerNorm kernel.  Both give the same bits.
-// can_project(e, w): the fused launch can also compute linear w of its
-// normalized rows (a d x d linear, the cross-attention query).
-bool can_project(const mc_engine* e, const DevLinear& w) {
-  return e->fuse_ln && w.has_ln_map && w.out == e->d && w.in == e->d;
+// proj_kind(e, w): how the fused launch can also compute linear w of its
+// normalized rows: 1 for a d x d linear (the cross-attention query), 2 for
+// the FFN's first linear (4d x d, ReLU, int8 output; d = 128, 256, 512),
+// 0 when it cannot.
+int proj_kind(const mc_engine* e, const DevLinear& w) {
+  if (!e->fuse_ln || !w.has_proj_map || w.in != e->d) return 0;
+  if (w.out == e->d) return 1;
+  if (w.out == 4 * e->d && (e->d == 128 || e->d == 256 || e->d == 512)) return 2;
+  return 0;
 }
 
 mc_status linear_ln(mc_engine* e, Lane& L, int gemm_kind, const QBuf* a, const DevLinear& w,
                     const float* residual, const float* gamma, const float* beta, int cap,
                     const int32_t* m_dev, double m_prof, float* out, const QuantOut& q,
-                    const DevLinear* proj = nullptr, float* proj_out = nullptr) {
+                    const DevLinear* proj = nullptr, void* proj_out = nullptr, float proj_alpha = 0.f) {
   const int d = e->d;
   const double rows_d = m_prof * d;
   if (e->fuse_ln && w.has_ln_map && w.out == d) {
@@ -694,17 +708,22 @@ mc_status linear_ln(mc_engine* e, Lane& L, int gemm_kind, const QBuf* a, const D
     p.status = L.d_status;
     double flops = 2.0 * rows_d * w.in;
     double bytes = m_prof * w.in + (double)d * w.in + 16.0 * d + rows_d * (8 + q.count);
-    if (proj) {  // the cross-attention query from the normalized rows, same launch
-      p.proj = 1;
-      p.tmap_b2 = proj->tmap_ln;
+    if (proj) {  // a second linear of the normalized rows, same launch
+      p.proj = proj_kind(e, *proj);
+      if (!p.proj) return fail(e, MC_CUDA, "fused second linear requested for an unsupported shape");
+      p.tmap_b2 = proj->tmap_proj;
       p.col_scale2 = proj->per_row ? proj->col_scale : nullptr;
       p.uniform_scale2 = proj->scale;
       p.bias2 = proj->bias;
-      p.out2 = proj_out;
-      p.ldo2 = d;
+      p.ldo2 = proj->out;
       p.alpha2 = proj->alpha;
-      flops += 2.0 * rows_d * d;
-      bytes += (double)d * d + 8.0 * d + 4.0 * rows_d;
+      if (p.proj == 1)
+        p.out2 = static_cast<float*>(proj_out);
+      else
+        p.out2q = static_cast<int8_t*>(proj_out);
+      p.alpha3 = proj_alpha;
+      flops += 2.0 * m_prof * proj->out * d;
+      bytes += (double)proj->out * d + 8.0 * proj->out + m_prof * proj->out * (p.proj == 1 ? 4 : 1);
     }
     PROFILED(MC_K_GEMM_LN, flops, bytes, CK(launch_q8_linear_ln(p, d, L.cur)));
     ++e->launches;
@@ -773,7 +792,7 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap, const std::vector<int3
                                      a.wo.alpha, L.d_status, L.cur)));
       // the first LayerNorm's rows also feed the cross-attention query:
       // one launch computes both when the fused kernel applies
-      if (can_project(e, c.wq) && a.wo.has_ln_map && a.wo.out == d) {
+      if (proj_kind(e, c.wq) == 1 && a.wo.has_ln_map && a.wo.out == d) {
         QuantOut none;
         std::memset(&none, 0, sizeof(none));
         if ((st = linear_ln(e, L, MC_K_GEMM_OUT, &L.dec_o, a.wo, x, a.ln_g, a.ln_b, cap, nrows, R, y, none,
@@ -807,12 +826,24 @@ mc_status run_decode_step(mc_engine* e, Lane& L, int cap, const std::vector<int3
                                    e->cross_pages_d, e->pages_per_slot, e->page_tokens,
                                    &e->cross_k_map[l], &e->cross_v_map[l], d, e->heads, L.dec_o.p,
                                    c.wo.alpha, L.d_status, L.cur)));
-    if ((st = linear_ln(e, L, MC_K_GEMM_OUT, &L.dec_o, c.wo, x, c.ln_g, c.ln_b, cap, nrows, R, y,
-                        quant_out(L.dec_q, {f.w1.alpha}))))
+    // the second LayerNorm's rows also feed the FFN's first linear: one
+    // launch computes both when the fused kernel applies
+    const bool ffn_fused = proj_kind(e, f.w1) == 2 && c.wo.has_ln_map && c.wo.out == d;
+    if (ffn_fused) {
+      QuantOut none;
+      std::memset(&none, 0, sizeof(none));
+      if ((st = linear_ln(e, L, MC_K_GEMM_OUT, &L.dec_o, c.wo, x, c.ln_g, c.ln_b, cap, nrows, R, y, none,
+                          &f.w1, L.dec_h.p, f.w2.alpha)))
+        return st;
+    } else if ((st = linear_ln(e, L, MC_K_GEMM_OUT, &L.dec_o, c.wo, x, c.ln_g, c.ln_b, cap, nrows, R, y,
+                               quant_out(L.dec_q, {f.w1.alpha})))) {
       return st;
+    }
     std::swap(x, y);
-    GroupSpec w1 = {&L.dec_q[0], &f.w1, kEpiQ8, L.dec_h.p, e->ffn, 0, nullptr, true, f.w2.alpha};
-    if ((st = gemm(e, L, MC_K_GEMM_FFN1, cap, nrows, R, &w1, 1))) return st;
+    if (!ffn_fused) {
+      GroupSpec w1 = {&L.dec_q[0], &f.w1, kEpiQ8, L.dec_h.p, e->ffn, 0, nullptr, true, f.w2.alpha};
+      if ((st = gemm(e, L, MC_K_GEMM_FFN1, cap, nrows, R, &w1, 1))) return st;
+    }
     if ((st = linear_ln(e, L, MC_K_GEMM_FFN2, &L.dec_h, f.w2, x, f.ln_g, f.ln_b, cap, nrows, R, y,
                         quant_out_vec(L.dec_q, dec_input_alphas(e, l + 1)))))
       return st;

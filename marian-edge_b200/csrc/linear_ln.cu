@@ -133,32 +133,49 @@ struct LlShape {
   static constexpr int PROJ_END = OUT_OFF + KB2 * R * 128;
   static constexpr int MIN_STAGES_PROJ = (PROJ_END + STAGE - 1) / STAGE;
   static constexpr int XBYTES_AL = (XBYTES + 1023) / 1024 * 1024;
-  static constexpr int B2_BYTES = KB2 * BN * 128;
-  static constexpr int TCOLS2 = 2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : 256);
   static_assert(D % 128 == 0 && BN % 32 == 0 && BN <= 128 && kLlBM % C == 0 && R <= 32 && R >= 8,
                 "unsupported fused LayerNorm shape");
   static_assert((XSEG * 4) % 16 == 0, "bulk copies move 16-byte multiples");
 };
 
-template <int D, int C, bool PROJ>
+// Second-linear variants: PK = 0 none, 1 a d-wide f32 linear (the
+// cross-attention query), 2 the FFN's first linear (4d wide, ReLU, int8
+// output quantized for the second).
+template <int D, int C, int PK>
+struct LlPlan {
+  using S = LlShape<D, C>;
+  static constexpr int BN2 = PK == 2 ? 4 * S::BN : S::BN;     // second-linear columns per CTA
+  static constexpr int CHUNK = BN2 * 128;                     // one k-block of its weights
+  // resident weight k-blocks: all of them (PK 1); two, with k-block 2 loaded
+  // into the exchange buffer once it is read and k-block 3 into the ring's
+  // outgoing segments once they are delivered (PK 2)
+  static constexpr int B2_RES = PK == 0 ? 0 : (PK == 1 ? S::KB2 * CHUNK : 2 * CHUNK);
+  static constexpr int TC1 = S::TCOLS;
+  static constexpr int TCOLS = PK == 0 ? TC1 : (S::BN + BN2 <= 64 ? 64 : (S::BN + BN2 <= 128 ? 128 : (S::BN + BN2 <= 256 ? 256 : 512)));
+  static_assert(PK != 2 || (S::KB2 <= 4 && BN2 <= 256 && S::XBYTES_AL >= CHUNK && S::STAGING >= CHUNK),
+                "FFN projection shape");
+};
+
+template <int D, int C, int PK>
 constexpr int ll_smem_bytes(int stages) {
   using S = LlShape<D, C>;
-  return stages * S::STAGE + S::XBYTES_AL + (PROJ ? S::B2_BYTES : 0) + 1024;
+  return stages * S::STAGE + S::XBYTES_AL + LlPlan<D, C, PK>::B2_RES + 1024;
 }
 
-// Ring depth: up to kLlMaxStages within 218 KB of dynamic shared memory
-// (the static arrays take the rest of the 227 KB per-CTA limit).
-template <int D, int C, bool PROJ>
+// Ring depth: up to kLlMaxStages within the dynamic shared memory that the
+// static arrays leave of the 227 KB per-CTA limit.
+template <int D, int C, int PK>
 constexpr int ll_max_stages() {
   using S = LlShape<D, C>;
-  constexpr int fit = (218 * 1024 - S::XBYTES_AL - (PROJ ? S::B2_BYTES : 0) - 1024) / S::STAGE;
+  constexpr int budget = (PK == 2 ? 220 : 218) * 1024;
+  constexpr int fit = (budget - S::XBYTES_AL - LlPlan<D, C, PK>::B2_RES - 1024) / S::STAGE;
   return fit < kLlMaxStages ? fit : kLlMaxStages;
 }
 
-template <int D, int C, bool PROJ>
+template <int D, int C, int PK>
 constexpr int ll_min_stages() {
   using S = LlShape<D, C>;
-  return PROJ && S::MIN_STAGES_PROJ > S::MIN_STAGES ? S::MIN_STAGES_PROJ : S::MIN_STAGES;
+  return PK != 0 && S::MIN_STAGES_PROJ > S::MIN_STAGES ? S::MIN_STAGES_PROJ : S::MIN_STAGES;
 }
 
 // Bulk copy of `bytes` from this CTA's shared memory to a cluster peer's,
@@ -225,10 +242,13 @@ __device__ __forceinline__ float ordered_row_sum(const float* seg0) {
   return sum;
 }
 
-template <int D, int C, bool PROJ>
+template <int D, int C, int PK>
 __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const __grid_constant__ LinearLnParams p) {
   using S = LlShape<D, C>;
-  constexpr int TCOLS = PROJ ? S::TCOLS2 : S::TCOLS;  // the second accumulator at column BN
+  using P = LlPlan<D, C, PK>;
+  constexpr bool PROJ = PK != 0;
+  constexpr int TCOLS = P::TCOLS;  // the second linear's accumulator at column BN
+  constexpr int BN2 = P::BN2;
   constexpr int BN = S::BN, R = S::R, SLD = S::SLD, XSEG = S::XSEG;
   constexpr int kLlThreads = ll_threads<D>();
   constexpr int CHUNKS = BN / 32;                 // 32-column TMEM chunks per tile row
@@ -244,12 +264,19 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
   float* xbuf = reinterpret_cast<float*>(smem_b + stages * BN * kLlBK);
   uint8_t* a2 = smem + S::A2_OFF;                       // proj: its A operand
   uint8_t* a2_out = smem + S::OUT_OFF;                  // proj: this CTA's rows of it
-  uint8_t* b2 = reinterpret_cast<uint8_t*>(xbuf) + S::XBYTES_AL;  // proj: W2's columns
+  uint8_t* b2 = reinterpret_cast<uint8_t*>(xbuf) + S::XBYTES_AL;  // proj: W2's resident k-blocks
+  // k-block kb of the second linear's weights (PK 2: k-block 2 reuses the
+  // exchange buffer, k-block 3 the ring's outgoing segments)
+  auto b2_chunk = [&](int kb) -> uint8_t* {
+    if (PK == 2 && kb == 2) return reinterpret_cast<uint8_t*>(xbuf);
+    if (PK == 2 && kb == 3) return smem;
+    return b2 + kb * P::CHUNK;
+  };
   __shared__ __align__(8) uint64_t full_bar[kLlMaxStages];
   __shared__ __align__(8) uint64_t empty_bar[kLlMaxStages];
   __shared__ __align__(8) uint64_t tfull_bar;
   __shared__ __align__(8) uint64_t x_bar;
-  __shared__ __align__(8) uint64_t b2_bar, a2_bar, t2_bar;  // proj
+  __shared__ __align__(8) uint64_t b2_bar[4], a2_bar, t2_bar;  // proj
   __shared__ uint32_t tmem_base_s;
   __shared__ __align__(16) float s_bias[BN];
   __shared__ __align__(16) float s_scale[BN];
@@ -257,8 +284,8 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
   __shared__ __align__(16) float s_beta[D];
   __shared__ float s_mean[R];
   __shared__ float s_inv[R];
-  __shared__ __align__(16) float s_bias2[PROJ ? BN : 1];
-  __shared__ __align__(16) float s_scale2[PROJ ? BN : 1];
+  __shared__ __align__(16) float s_bias2[PROJ ? BN2 : 1];
+  __shared__ __align__(16) float s_scale2[PK == 1 ? BN2 : 1];  // PK 2: read from global when per column
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -274,9 +301,12 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
   if (threadIdx.x < BN) {
     s_bias[threadIdx.x] = p.bias ? p.bias[n0 + threadIdx.x] : 0.0f;
     s_scale[threadIdx.x] = p.col_scale ? p.col_scale[n0 + threadIdx.x] : p.uniform_scale;
-    if constexpr (PROJ) {
-      s_bias2[threadIdx.x] = p.bias2 ? p.bias2[n0 + threadIdx.x] : 0.0f;
-      s_scale2[threadIdx.x] = p.col_scale2 ? p.col_scale2[n0 + threadIdx.x] : p.uniform_scale2;
+  }
+  const int n0_2 = static_cast<int>(rank) * BN2;  // the second linear's first column
+  if constexpr (PROJ) {
+    for (int i = threadIdx.x; i < BN2; i += kLlThreads) {
+      s_bias2[i] = p.bias2 ? p.bias2[n0_2 + i] : 0.0f;
+      if constexpr (PK == 1) s_scale2[i] = p.col_scale2 ? p.col_scale2[n0_2 + i] : p.uniform_scale2;
     }
   }
   if (threadIdx.x == 0) {
@@ -290,7 +320,7 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
     // CTAs' segments of its R rows have landed (its own are plain stores)
     mbar_arrive_expect_tx(&x_bar, static_cast<uint32_t>((C - 1) * XSEG * 4));
     if constexpr (PROJ) {
-      mbar_init(&b2_bar, 1);
+      for (int i = 0; i < 4; ++i) mbar_init(&b2_bar[i], 1);
       mbar_init(&a2_bar, 1);
       // the other C - 1 CTAs' R quantized rows of every k-block
       mbar_arrive_expect_tx(&a2_bar, static_cast<uint32_t>((C - 1) * S::KB2 * R * 128));
@@ -321,10 +351,11 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
         tma_load_2d(smem_a + s * kLlBM * kLlBK, &p.tmap_a, kb * kLlBK, row0, &full_bar[s]);
         tma_load_2d_hint(smem_b + s * BN * kLlBK, &p.tmap_b, kb * kLlBK, n0, &full_bar[s], keep);
       }
-      if constexpr (PROJ) {  // W2's columns, needed after the LayerNorm
-        mbar_arrive_expect_tx(&b2_bar, S::B2_BYTES);
-        for (int kb = 0; kb < S::KB2; ++kb)
-          tma_load_2d_hint(b2 + kb * BN * kLlBK, &p.tmap_b2, kb * kLlBK, n0, &b2_bar, keep);
+      if constexpr (PROJ) {  // the second linear's resident k-blocks, needed after the LayerNorm
+        for (int kb = 0; kb < (PK == 2 ? (S::KB2 < 2 ? S::KB2 : 2) : S::KB2); ++kb) {
+          mbar_arrive_expect_tx(&b2_bar[kb], P::CHUNK);
+          tma_load_2d_hint(b2_chunk(kb), &p.tmap_b2, kb * kLlBK, n0_2, &b2_bar[kb], keep);
+        }
       }
     }
   }
@@ -499,55 +530,103 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
   }
   if constexpr (PROJ) {
     // ---- the second linear: exchange the quantized rows, MMA, epilogue ----
-    fence_proxy_async_smem();  // A2 and the staged rows are read by the async proxy
+    fence_proxy_async_smem();  // A2, the staged rows and the read exchange buffer
     __syncthreads();
-    if (threadIdx.x == 0 && got) {
-      for (int o = 0; o < C; ++o) {
-        if (o == static_cast<int>(rank)) continue;
-        const uint32_t peer_bar = map_shared_rank(smem_u32(&a2_bar), o);
-        for (int kb = 0; kb < S::KB2; ++kb)
-          bulk_copy_to_peer(map_shared_rank(smem_u32(a2 + kb * 16384 + static_cast<int>(rank) * R * 128), o),
-                            a2_out + kb * (R * 128), R * 128, peer_bar);
-      }
+    // one thread per (peer, k-block) piece issues its bulk copy
+    constexpr int kPieces = (C - 1) * S::KB2;
+    static_assert(kPieces < kLlThreads, "one thread per outgoing piece");
+    if (threadIdx.x < kPieces && got) {
+      const int j = threadIdx.x / S::KB2, kb = threadIdx.x % S::KB2;
+      const int o = j < static_cast<int>(rank) ? j : j + 1;
+      bulk_copy_to_peer(map_shared_rank(smem_u32(a2 + kb * 16384 + static_cast<int>(rank) * R * 128), o),
+                        a2_out + kb * (R * 128), R * 128, map_shared_rank(smem_u32(&a2_bar), o));
+    }
+    const uint64_t keep = l2_policy_evict_last();
+    if (PK == 2 && S::KB2 > 2 && threadIdx.x == kPieces) {
+      // the exchange buffer has been read: weight k-block 2 goes there
+      mbar_arrive_expect_tx(&b2_bar[2], P::CHUNK);
+      tma_load_2d_hint(b2_chunk(2), &p.tmap_b2, 2 * kLlBK, n0_2, &b2_bar[2], keep);
     }
     const bool got2 = mbar_wait_cluster(&a2_bar, 0, p.status) && got;
     asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");  // see above
-    if (warp == 1 && lane == 0 && got2 && mbar_wait(&b2_bar, 0, p.status)) {
-      tc_fence_after();
-      constexpr uint32_t idesc = idesc_i8(kLlBM, BN);
-#pragma unroll
-      for (int kb = 0; kb < S::KB2; ++kb)
+    if (PK == 2 && S::KB2 > 3 && threadIdx.x == kPieces) {
+      // every peer has received this CTA's outgoing segments (they sent
+      // their quantized rows after that): weight k-block 3 goes there
+      mbar_arrive_expect_tx(&b2_bar[3], P::CHUNK);
+      tma_load_2d_hint(b2_chunk(3), &p.tmap_b2, 3 * kLlBK, n0_2, &b2_bar[3], keep);
+    }
+    if (warp == 1 && lane == 0 && got2) {
+      constexpr uint32_t idesc = idesc_i8(kLlBM, BN2);
+      bool ok = true;
+      for (int kb = 0; kb < S::KB2 && ok; ++kb) {
+        if (!(ok = mbar_wait(&b2_bar[kb], 0, p.status))) break;
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kLlBK / 32; ++kk)
           mma_i8(tmem_base + BN, sdesc_k_sw128(smem_u32(a2 + kb * 16384) + kk * 32),
-                 sdesc_k_sw128(smem_u32(b2 + kb * BN * kLlBK) + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-      mma_commit(&t2_bar);
+                 sdesc_k_sw128(smem_u32(b2_chunk(kb)) + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+      }
+      if (ok) mma_commit(&t2_bar);
     }
     if (epi) {
       const bool ready2 = __all_sync(0xffffffffu, mbar_wait(&t2_bar, 0, p.status));
       if (ready2) {
         tc_fence_after();
         const uint32_t lane_base = tmem_base + BN + (static_cast<uint32_t>(quarter * 32) << 16);
-        float* orow = p.out2 + (size_t)(row_ok ? row : 0) * p.ldo2 + n0;
+        if constexpr (PK == 1) {
+          float* orow = p.out2 + (size_t)(row_ok ? row : 0) * p.ldo2 + n0_2;
 #pragma unroll
-        for (int i = 0; i < MY_CHUNKS; ++i) {
-          const int c0 = 32 * (half + 2 * i);
-          if (c0 >= BN) break;
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(lane_base + c0, r);
-          tmem_ld_wait();
-          if (row_ok) {
+          for (int i = 0; i < MY_CHUNKS; ++i) {
+            const int c0 = 32 * (half + 2 * i);
+            if (c0 >= BN2) break;
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(lane_base + c0, r);
+            tmem_ld_wait();
+            if (row_ok) {
+#pragma unroll
+              for (int j4 = 0; j4 < 8; ++j4) {
+                float y[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  const int j = 4 * j4 + u;
+                  y[u] = dequant(static_cast<int32_t>(r[j]), s_scale2[c0 + j], s_bias2[c0 + j]);
+                }
+                *reinterpret_cast<float4*>(orow + c0 + 4 * j4) = make_float4(y[0], y[1], y[2], y[3]);
+              }
+            }
+          }
+        } else {
+          // the FFN's first linear: bias, ReLU, quantized with the second
+          // linear's alpha (the GEMM's int8 epilogue); half h of the
+          // quarter takes columns [h * BN2 / 2, (h + 1) * BN2 / 2)
+          int8_t* orow = p.out2q + (size_t)(row_ok ? row : 0) * p.ldo2 + n0_2;
+          float amax = 0.0f;
+#pragma unroll 1
+          for (int c0 = half * (BN2 / 2); c0 < (half + 1) * (BN2 / 2); c0 += 32) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(lane_base + c0, r);
+            tmem_ld_wait();
+            uint32_t w[8];
 #pragma unroll
             for (int j4 = 0; j4 < 8; ++j4) {
-              float y[4];
+              int qv[4];
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
                 const int j = 4 * j4 + u;
-                y[u] = dequant(static_cast<int32_t>(r[j]), s_scale2[c0 + j], s_bias2[c0 + j]);
+                const float sc = p.col_scale2 ? p.col_scale2[n0_2 + c0 + j] : p.uniform_scale2;
+                const float v = fmaxf(dequant(static_cast<int32_t>(r[j]), sc, s_bias2[c0 + j]), 0.0f);
+                amax = fmaxf(amax, v);
+                qv[u] = quant_s8(v, p.alpha3);
               }
-              *reinterpret_cast<float4*>(orow + c0 + 4 * j4) = make_float4(y[0], y[1], y[2], y[3]);
+              w[j4] = __byte_perm(__byte_perm((uint32_t)qv[0], (uint32_t)qv[1], 0x0040),
+                                  __byte_perm((uint32_t)qv[2], (uint32_t)qv[3], 0x0040), 0x5410);
+            }
+            if (row_ok) {
+              *reinterpret_cast<uint4*>(orow + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+              *reinterpret_cast<uint4*>(orow + c0 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
             }
           }
+          if (row_ok && !(amax <= 3.402823466e38f)) flag_status(p.status, kStatusNonFinite);
         }
       }
     }
@@ -561,35 +640,35 @@ __global__ void __launch_bounds__(ll_threads<D>(), 1) q8_linear_ln_kernel(const 
   asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
 }
 
-template <int D, int C, bool PROJ>
+template <int D, int C, int PK>
 cudaError_t configure_ll() {
   static unsigned long long configured = 0;  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured & (1ull << (dev & 63)))) {
-    cudaError_t e = cudaFuncSetAttribute(q8_linear_ln_kernel<D, C, PROJ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         ll_smem_bytes<D, C, PROJ>(ll_max_stages<D, C, PROJ>()));
+    cudaError_t e = cudaFuncSetAttribute(q8_linear_ln_kernel<D, C, PK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         ll_smem_bytes<D, C, PK>(ll_max_stages<D, C, PK>()));
     if (e != cudaSuccess) return e;
     configured |= 1ull << (dev & 63);
   }
   return cudaSuccess;
 }
 
-template <int D, int C, bool PROJ>
+template <int D, int C, int PK>
 cudaError_t launch_ll(LinearLnParams p, cudaStream_t stream) {
-  static_assert(ll_min_stages<D, C, PROJ>() <= ll_max_stages<D, C, PROJ>(), "shared memory plan");
-  cudaError_t e = configure_ll<D, C, PROJ>();
+  static_assert(ll_min_stages<D, C, PK>() <= ll_max_stages<D, C, PK>(), "shared memory plan");
+  cudaError_t e = configure_ll<D, C, PK>();
   if (e != cudaSuccess) return e;
   const int num_kb = (p.k + kLlBK - 1) / kLlBK;
   // as deep as K (within the budget), and deep enough to hold the outgoing
-  // segments (and, with a projection, its operand) after the last MMA
-  int stages = num_kb < ll_max_stages<D, C, PROJ>() ? num_kb : ll_max_stages<D, C, PROJ>();
-  if (stages < ll_min_stages<D, C, PROJ>()) stages = ll_min_stages<D, C, PROJ>();
+  // segments (and, with a second linear, its operand) after the last MMA
+  int stages = num_kb < ll_max_stages<D, C, PK>() ? num_kb : ll_max_stages<D, C, PK>();
+  if (stages < ll_min_stages<D, C, PK>()) stages = ll_min_stages<D, C, PK>();
   p.stages = stages;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(C, (p.cap + kLlBM - 1) / kLlBM);
   cfg.blockDim = dim3(ll_threads<D>());
-  cfg.dynamicSmemBytes = ll_smem_bytes<D, C, PROJ>(p.stages);
+  cfg.dynamicSmemBytes = ll_smem_bytes<D, C, PK>(p.stages);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -600,19 +679,34 @@ cudaError_t launch_ll(LinearLnParams p, cudaStream_t stream) {
   attr[1].val.programmaticStreamSerializationAllowed = kProgrammaticLaunch ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  e = cudaLaunchKernelEx(&cfg, q8_linear_ln_kernel<D, C, PROJ>, p);
+  e = cudaLaunchKernelEx(&cfg, q8_linear_ln_kernel<D, C, PK>, p);
   return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+// The FFN variant (PK 2) exists for d = 128, 256 and 512 (its 4d-wide
+// columns per CTA must fit one MMA: 4 * d / C <= 256).
+template <int D, int C>
+constexpr bool ll_has_ffn() {
+  return 4 * (D / C) <= 256 && LlShape<D, C>::KB2 <= 4;
 }
 
 template <int D, int C>
 cudaError_t launch_ll_any(const LinearLnParams& p, cudaStream_t stream) {
-  return p.proj ? launch_ll<D, C, true>(p, stream) : launch_ll<D, C, false>(p, stream);
+  if (p.proj == 1) return launch_ll<D, C, 1>(p, stream);
+  if (p.proj == 2) {
+    if constexpr (ll_has_ffn<D, C>()) return launch_ll<D, C, 2>(p, stream);
+    return cudaErrorInvalidValue;
+  }
+  return launch_ll<D, C, 0>(p, stream);
 }
 
 template <int D, int C>
-cudaError_t configure_ll_both() {
-  cudaError_t e = configure_ll<D, C, false>();
-  return e == cudaSuccess ? configure_ll<D, C, true>() : e;
+cudaError_t configure_ll_all() {
+  cudaError_t e = configure_ll<D, C, 0>();
+  if (e == cudaSuccess) e = configure_ll<D, C, 1>();
+  if constexpr (ll_has_ffn<D, C>())
+    if (e == cudaSuccess) e = configure_ll<D, C, 2>();
+  return e;
 }
 
 }  // namespace
@@ -628,17 +722,18 @@ int linear_ln_cluster(int d) {
 }
 
 cudaError_t prepare_q8_linear_ln() {
-  cudaError_t e = configure_ll_both<128, 4>();
-  if (e == cudaSuccess) e = configure_ll_both<256, 8>();
-  if (e == cudaSuccess) e = configure_ll_both<384, 4>();
-  if (e == cudaSuccess) e = configure_ll_both<512, 8>();
+  cudaError_t e = configure_ll_all<128, 4>();
+  if (e == cudaSuccess) e = configure_ll_all<256, 8>();
+  if (e == cudaSuccess) e = configure_ll_all<384, 4>();
+  if (e == cudaSuccess) e = configure_ll_all<512, 8>();
   return e;
 }
 
 cudaError_t launch_q8_linear_ln(const LinearLnParams& p, int d, cudaStream_t stream) {
   if (p.cap <= 0) return cudaSuccess;
   if (p.k <= 0 || p.k % 16 != 0 || p.q.count < 0 || p.q.count > kMaxQuantOut ||
-      (p.proj && (!p.out2 || p.ldo2 < d)))
+      (p.proj == 1 && (!p.out2 || p.ldo2 < d)) || (p.proj == 2 && (!p.out2q || p.ldo2 < 4 * d)) ||
+      p.proj < 0 || p.proj > 2)
     return cudaErrorInvalidValue;
   switch (d) {
     case 128: return launch_ll_any<128, 4>(p, stream);

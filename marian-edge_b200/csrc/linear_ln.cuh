@@ -35,16 +35,21 @@ struct alignas(64) LinearLnParams {
   int32_t stages;            // shared-memory ring depth (set by the launcher)
   uint32_t* status;          // device status word (error bits)
   // proj != 0: the normalized rows are also the input of a second Q8 linear
-  // W2 [d, d] (the decoder's cross-attention query after its first
-  // LayerNorm): out2 = dequant(quantize(out, alpha2) x W2^T) * scale2 +
-  // bias2, computed in the same launch.
+  // W2 in the same launch, A2 = quantize(out, alpha2):
+  //   proj 1: W2 [d, d] (the decoder's cross-attention query after its first
+  //           LayerNorm), out2 = dequant(A2 x W2^T) * scale2 + bias2, f32;
+  //   proj 2: W2 [4d, d] (the FFN's first linear after the second
+  //           LayerNorm), out2q = quantize(ReLU(dequant(A2 x W2^T) * scale2 +
+  //           bias2), alpha3), int8 (d = 128, 256 or 512).
   int32_t proj;
-  const float* col_scale2;   // [d] or null
+  const float* col_scale2;   // [N2] or null
   float uniform_scale2;
-  const float* bias2;        // [d] or null
-  float* out2;               // [rows, ldo2]
-  int32_t ldo2;
+  const float* bias2;        // [N2] or null
+  float* out2;               // proj 1: [rows, ldo2] f32
+  int8_t* out2q;             // proj 2: [rows, ldo2] int8
+  int32_t ldo2;              // elements
   float alpha2;              // W2's activation alpha
+  float alpha3;              // proj 2: the next linear's activation alpha
 };
 
 // CTAs per cluster for model width d (each owns d / C output columns of a
