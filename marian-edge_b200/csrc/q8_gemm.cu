@@ -509,6 +509,213 @@ cudaError_t launch_impl(GemmParams p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// ---- the vocabulary argmax, weight-stationary ---------------------------------
+// The tied vocabulary projection (N = 32,000) with its masked argmax at
+// decode row counts: the generic persistent kernel above loads both
+// operands for every 128 x 256 tile (48 KB per k-block), and at 1,000 tiles
+// over 148 CTAs that traffic, not the MMAs, sets its time.  Here each CTA
+// keeps one 256-id block of the weight table resident in shared memory (all
+// of K: 128 KB at d = 512) and streams the activations' 128-row blocks past
+// it through a ring of 16 KB k-blocks, so a CTA loads 128 KB of weights and
+// the activations once (640 KB in all at 1,024 rows, against ~1.3 MB per
+// CTA for the tiled order).  Roles and the epilogue are the generic
+// kernel's: warp 0 TMA, warp 1 TMEM + MMA (double-buffered accumulators, so
+// one row block's epilogue overlaps the next one's MMAs), 16 epilogue warps
+// with the masked-argmax epilogue.
+constexpr int kArgBN = 256;
+constexpr int kArgEpi = 16;
+constexpr int kArgStages = 4;
+
+template <int MAX_KB>
+__global__ void __launch_bounds__(threads_for<kArgEpi>(), 1) q8_argmax_kernel(const __grid_constant__ GemmParams p) {
+  constexpr int BN = kArgBN, EPI = kArgEpi;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int num_kb = (p.k + kBK - 1) / kBK;  // <= MAX_KB (checked by the launcher)
+  uint8_t* smem_b = smem;                          // resident weights: num_kb x BN x 128 B
+  uint8_t* smem_a = smem + MAX_KB * BN * kBK;      // activation ring: kArgStages x 16 KB
+  __shared__ __align__(8) uint64_t full_bar[kArgStages];
+  __shared__ __align__(8) uint64_t empty_bar[kArgStages];
+  __shared__ __align__(8) uint64_t bfull_bar, bempty_bar;
+  __shared__ __align__(8) uint64_t tfull_bar[2];
+  __shared__ __align__(8) uint64_t tempty_bar[2];
+  __shared__ uint32_t tmem_base_s;
+  __shared__ __align__(16) float s_bias[EPI][64];
+  __shared__ __align__(16) float s_scale[EPI][64];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const GemmGroup& g = p.g[0];
+  const int n_tiles = (p.max_n + BN - 1) / BN;
+  pdl_enter();
+  const int m_raw = p.m_dev ? *p.m_dev : p.m;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kArgStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&bfull_bar, 1);
+    mbar_init(&bempty_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], EPI);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&g.tmap_a);
+    tma_prefetch_desc(&g.tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_s, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_s;
+  const int m = max(0, min(m_raw, p.m));
+  const int m_tiles = (m + kBM - 1) / kBM;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t keep = l2_policy_evict_last();  // weights: reused every step
+      int kbg = 0, jt = 0;
+      bool ok = true;
+      for (int j = blockIdx.x; j < n_tiles && ok; j += gridDim.x, ++jt) {
+        // the previous block's MMAs are done with the resident weights
+        if (!(ok = mbar_wait(&bempty_bar, (jt & 1) ^ 1, p.status))) break;
+        mbar_arrive_expect_tx(&bfull_bar, num_kb * BN * kBK);
+        for (int kb = 0; kb < num_kb; ++kb)
+          tma_load_2d_hint(smem_b + kb * BN * kBK, &g.tmap_b, kb * kBK, j * BN, &bfull_bar, keep);
+        for (int mt = 0; mt < m_tiles && ok; ++mt)
+          for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
+            const int s = kbg % kArgStages;
+            const uint32_t phase = (kbg / kArgStages) & 1;
+            if (!(ok = mbar_wait(&empty_bar[s], phase ^ 1, p.status))) break;
+            mbar_arrive_expect_tx(&full_bar[s], kBM * kBK);
+            tma_load_2d(smem_a + s * kBM * kBK, &g.tmap_a, kb * kBK, mt * kBM, &full_bar[s]);
+          }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(kBM, BN);
+      int kbg = 0, it = 0, jt = 0;
+      bool ok = true;
+      for (int j = blockIdx.x; j < n_tiles && ok; j += gridDim.x, ++jt) {
+        if (!(ok = mbar_wait(&bfull_bar, jt & 1, p.status))) break;
+        for (int mt = 0; mt < m_tiles && ok; ++mt, ++it) {
+          const int buf = it & 1;
+          if (!(ok = mbar_wait(&tempty_bar[buf], ((it >> 1) & 1) ^ 1, p.status))) break;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + buf * BN;
+          for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
+            const int s = kbg % kArgStages;
+            const uint32_t phase = (kbg / kArgStages) & 1;
+            if (!(ok = mbar_wait(&full_bar[s], phase, p.status))) break;
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(smem_a + s * kBM * kBK);
+            const uint32_t b_addr = smem_u32(smem_b + kb * BN * kBK);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 32; ++kk)
+              mma_i8(d_tmem, sdesc_k_sw128(a_addr + kk * 32), sdesc_k_sw128(b_addr + kk * 32), idesc,
+                     (kb > 0 || kk > 0) ? 1u : 0u);
+            mma_commit(&empty_bar[s]);
+          }
+          if (ok) mma_commit(&tfull_bar[buf]);
+        }
+        if (ok) mma_commit(&bempty_bar);  // every MMA of this block has read the weights
+      }
+    }
+  } else {
+    // the generic kernel's epilogue in its argmax mode, per (row block, id block)
+    const int quarter = warp & 3;
+    const int part = (warp - 2) >> 2;
+    constexpr int kShare = BN / (EPI / 4);  // 64 columns per warp
+    float* sb = s_bias[warp - 2];
+    float* ss = s_scale[warp - 2];
+    const bool has_scale = g.col_scale != nullptr;
+    int it = 0;
+    bool ok = true;
+    for (int j = blockIdx.x; j < n_tiles && ok; j += gridDim.x) {
+      const int n0 = j * BN;
+      const int nb_first = n0 + part * kShare;
+      // this block's bias (-inf padded past N) and column scales for the warp
+#pragma unroll
+      for (int i = 0; i < kShare / 32; ++i) {
+        const int n = nb_first + 32 * i + lane;
+        sb[32 * i + lane] = g.bias ? g.bias[n] : 0.0f;
+        if (has_scale) ss[32 * i + lane] = n < g.n ? g.col_scale[n] : 0.0f;
+      }
+      __syncwarp();
+      for (int mt = 0; mt < m_tiles; ++mt, ++it) {
+        const int buf = it & 1;
+        const int row = mt * kBM + quarter * 32 + lane;
+        const bool row_ok = row < m;
+        const bool ready = __all_sync(0xffffffffu, mbar_wait(&tfull_bar[buf], (it >> 1) & 1, p.status));
+        if (!ready) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float best = -INFINITY;
+        int best_n = -1;
+        const uint32_t lane_base = tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+        for (int c0 = part * kShare; c0 < (part + 1) * kShare; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(lane_base + c0, r);
+          tmem_ld_wait();
+          if (n0 + c0 < g.n)
+            epilogue_chunk<BN>(g, r, row_ok, row, row, n0 + c0, 1.0f, p.status, best, best_n, nullptr,
+                               g.bias ? sb + (c0 - part * kShare) : nullptr,
+                               has_scale ? ss + (c0 - part * kShare) : nullptr);
+        }
+        if (row_ok && best_n >= 0) atomicMax(&g.argmax[row], pack_argmax(best, best_n));
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[buf]);
+      }
+      __syncwarp();  // the staged bias is rewritten for the next block
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+template <int MAX_KB>
+constexpr int argmax_smem_bytes() {
+  return MAX_KB * kArgBN * kBK + kArgStages * kBM * kBK + 1024;
+}
+
+template <int MAX_KB>
+cudaError_t configure_argmax() {
+  static unsigned long long configured = 0;  // one bit per device ordinal
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1ull << (dev & 63)))) {
+    cudaError_t e = cudaFuncSetAttribute(q8_argmax_kernel<MAX_KB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         argmax_smem_bytes<MAX_KB>());
+    if (e != cudaSuccess) return e;
+    configured |= 1ull << (dev & 63);
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_argmax(const GemmParams& p, cudaStream_t stream) {
+  constexpr int MAX_KB = 4;
+  cudaError_t e = configure_argmax<MAX_KB>();
+  if (e != cudaSuccess) return e;
+  const int n_tiles = (p.max_n + kArgBN - 1) / kArgBN;
+  const int grid = n_tiles < num_sms() ? n_tiles : num_sms();
+  launch_pdl(q8_argmax_kernel<MAX_KB>, dim3(grid), dim3(threads_for<kArgEpi>()), argmax_smem_bytes<MAX_KB>(),
+             stream, p);
+  return cudaGetLastError();
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -569,11 +776,17 @@ cudaError_t prepare_q8_gemm() {
   cudaError_t e = configure_impl<256, 3, 16>();
   if (e == cudaSuccess) e = configure_impl<128, 4, 16>();
   if (e == cudaSuccess) e = configure_impl<64, 7, 8>();
+  if (e == cudaSuccess) e = configure_argmax<4>();
   return e;
 }
 
 cudaError_t launch_q8_gemm(const GemmParams& p, int bn, cudaStream_t stream) {
   if (p.m <= 0 || p.num_groups <= 0) return cudaSuccess;
+  // a single vocabulary argmax with K <= 512: the weight-stationary kernel
+  // (its tensor map has the BN = 256 box)
+  if (bn == 256 && p.num_groups == 1 && p.g[0].mode == kEpiArgmax && p.k <= 4 * kBK && !p.g[0].row_map &&
+      !p.g[0].row_scale)
+    return launch_argmax(p, stream);
   switch (bn) {
     case 256: return launch_impl<256, 3, 16>(p, stream);
     case 128: return launch_impl<128, 4, 16>(p, stream);
