@@ -46,8 +46,13 @@ GRAPH_B = ModelShape(512, 8, 2048, 6, 2, "selfattn")
 # Small shapes keep CPU-only tests fast; they exercise every code path.
 TINY_SSRU = ModelShape(128, 4, 256, 2, 2, "ssru", vocab=512)
 TINY_SELF = ModelShape(128, 4, 256, 2, 2, "selfattn", vocab=512)
+# FFN 4d at d = 128 and d = 256: the fused kernel's FFN variant at its other
+# two widths (clusters of 4 and 8 CTAs of 32 columns).
+TINY_SELF_FFN4 = ModelShape(128, 4, 512, 2, 2, "selfattn", vocab=512)
+MID_SELF = ModelShape(256, 4, 1024, 2, 2, "selfattn", vocab=1024)
 
-SHAPES = {"graph_r": GRAPH_R, "graph_b": GRAPH_B, "tiny_ssru": TINY_SSRU, "tiny_self": TINY_SELF}
+SHAPES = {"graph_r": GRAPH_R, "graph_b": GRAPH_B, "tiny_ssru": TINY_SSRU, "tiny_self": TINY_SELF,
+          "tiny_self_ffn4": TINY_SELF_FFN4, "mid_self": MID_SELF}
 
 _Q8_STD = float(np.sqrt((255.0 ** 2 - 1.0) / 12.0))  # std of U{-127..127}
 

@@ -125,7 +125,7 @@ def _engine_run(mb, batch, fused):
     return got, off, tr
 
 
-@pytest.mark.parametrize("name", ["graph_b", "graph_r", "tiny_self"])
+@pytest.mark.parametrize("name", ["graph_b", "graph_r", "tiny_self", "tiny_self_ffn4", "mid_self"])
 def test_engine_fused_and_separate_layernorm_agree_bit_for_bit(name):
     mb = W.synthetic_model(W.SHAPES[name], seed=3)
     rng = np.random.Generator(np.random.PCG64(44))
@@ -136,3 +136,25 @@ def test_engine_fused_and_separate_layernorm_agree_bit_for_bit(name):
     np.testing.assert_array_equal(a_off, b_off)
     np.testing.assert_array_equal(a_tok, b_tok)
     np.testing.assert_array_equal(a_tr["decoder_state_step0"], b_tr["decoder_state_step0"])
+
+
+@pytest.mark.parametrize("name", ["tiny_self_ffn4", "mid_self"])
+def test_engine_with_fused_second_linears_matches_oracle(name):
+    # d = 128 (clusters of 4) and d = 256 (clusters of 8) with FFN 4d: every
+    # decoder sub-layer end runs fused, two of them with a second linear.
+    # The oracle runs reference-legal sub-batches (limits.rs:3-7).
+    mb = W.synthetic_model(W.SHAPES[name], seed=5)
+    om = O.OracleModel(mb)
+    full = W.short_batch(n=48, vocab=W.SHAPES[name].vocab, seed=9)
+    with CudaEngine(mb, max_inflight=256, max_encode_tokens=8192) as eng:
+        got, got_off = eng.translate_token_ids(full.tokens, full.offsets, full.max_out, full.force_len)
+    for grp in W.legal_cpu_batches(full):
+        b = W.subset(full, grp)
+        ref, ref_off, tr = om.translate(b.tokens, b.offsets, b.max_out, b.force_len, trace=True)
+        for j, row in enumerate(grp):
+            g, r = got[got_off[row]:got_off[row + 1]], ref[ref_off[j]:ref_off[j + 1]]
+            if len(g) == len(r) and np.array_equal(g, r):
+                continue
+            m = min(len(g), len(r))
+            k = next(i for i in range(m + 1) if i == m or g[i] != r[i])
+            assert k < 256 and tr["top2_gap"][j, k] < 1e-3, f"row {row} diverges at step {k}"
