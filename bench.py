@@ -280,7 +280,7 @@ def reduce_job(tokens, dev_ms, wall_s, world, device):
 DRAM_PER_ALGO_BYTE = {
     "attn_cross": 231.5 / 223.8,   # 1,024 rows, 54,009 keys, tail boxes of 4/2/1 rows
     "attn_self": 231.5 / 223.8,    # same kernel and page layout
-    "gemm_vocab": 18.66 / 17.17,   # M=1,024, N=32,000, K=512
+    "gemm_vocab": 17.12 / 17.17,   # M=1,024, N=32,000, K=512, weight-stationary
     "gemm_ln": 12.54 / 24.43,      # one layer's three fused launches, 1,024 rows, d=512
     "layernorm": 4.24 / 6.82,      # 1,024 rows; outputs still in L2 at exit
 }
