@@ -43,22 +43,30 @@ __device__ __forceinline__ unsigned long long pack_argmax(float v, int32_t n) {
   return (static_cast<unsigned long long>(ord) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(n));
 }
 
-// Per-warp staging tile for coalesced stores: 32 rows x 33 words (the odd
+// Per-warp staging tile for coalesced stores: 32 rows x stage_ld words.
+// With 16 epilogue warps (one CTA per SM) lane i writes row i with 16-byte
+// stores; at a stride of 36 words every 8 lanes cover the 32 banks once, so
+// each store and each 16-byte read of 4 rows x 128 B takes the minimum 4
+// shared-memory wavefronts.  With 8 (two CTAs per SM, where shared memory
+// is short) the stride is 33 words and the stores are 4-byte: the odd
 // stride keeps both the row-wise writes and the column-wise reads of the 32
-// lanes on distinct banks).
-constexpr int kStageLd = 33;
+// lanes on distinct banks.
+template <int EPI>
+constexpr int stage_ld() {
+  return EPI == 16 ? 36 : 33;
+}
 template <int EPI>
 constexpr int staging_bytes() {
-  return EPI * 32 * kStageLd * 4;
+  return EPI * 32 * stage_ld<EPI>() * 4;
 }
 
-// round(x * alpha) for the int8 store: ties-to-even, saturated to
-// [-128, 127] by the conversion; the caller bounds x * alpha below at -127
-// (unnecessary after ReLU).  NaN cannot reach here (see the Q8 epilogue).
-__device__ __forceinline__ int cvt_rni_sat_s8(float x) {
-  int r;
-  asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
+// rint(t) for t in [-127, 127], in the low byte of the result (two's
+// complement): t + 1.5 * 2^23 lies in [2^23, 2^24), where adjacent floats
+// are 1 apart, so the round-to-nearest-even addition rounds t to an integer
+// and the sum's bit pattern is 0x4B400000 + rint(t).  Two full-rate
+// floating-point operations (with the clamp) instead of a conversion.
+__device__ __forceinline__ int round_to_low_byte(float t) {
+  return __float_as_int(__fadd_rn(t, 12582912.0f));
 }
 
 // Low bytes of four ints -> one word (byte i = q[i]).
@@ -72,7 +80,7 @@ __device__ __forceinline__ uint32_t pack4_s8(int q0, int q1, int q2, int q3) {
 // validity; the call itself is warp-uniform (tcgen05.ld precedes it).
 // sbias / sscale: this chunk's 32 bias and column-scale values, staged in
 // shared memory before the accumulator was ready (nullptr: none).
-template <int BN>
+template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_t (&r)[32],
                                                bool ok, int row, int dest_row, int nb,
                                                float row_scale, uint32_t* status, float& best,
@@ -173,8 +181,15 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
                            (uintptr_t)(g.col_off + nb) * 4) & 15) == 0;
     if (full && aligned) {
       // stage the 32x32 block, then each instruction stores 4 rows x 128 B
+      constexpr int ld = stage_ld<EPI>();
+      if constexpr (ld % 4 == 0) {
+        float4* mine = reinterpret_cast<float4*>(stage + lane * ld);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) stage[lane * kStageLd + j] = __float_as_uint(v[j]);
+        for (int j4 = 0; j4 < 8; ++j4) mine[j4] = make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) stage[lane * ld + j] = __float_as_uint(v[j]);
+      }
       __syncwarp();
       const int sub = lane >> 3, c4 = (lane & 7) * 4;
 #pragma unroll
@@ -182,11 +197,17 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
         const int rr = it * 4 + sub;
         const int drow = __shfl_sync(0xffffffffu, dest_row, rr);
         const bool rok = __shfl_sync(0xffffffffu, ok ? 1 : 0, rr) != 0;
-        const uint32_t* srow = stage + rr * kStageLd + c4;
+        const uint32_t* srow = stage + rr * ld + c4;
+        float4 val;
+        if constexpr (ld % 4 == 0) {
+          val = *reinterpret_cast<const float4*>(srow);
+        } else {
+          val = make_float4(__uint_as_float(srow[0]), __uint_as_float(srow[1]), __uint_as_float(srow[2]),
+                            __uint_as_float(srow[3]));
+        }
         if (rok) {
           float* o = static_cast<float*>(g.out) + (size_t)drow * g.ldo + g.col_off + nb + c4;
-          *reinterpret_cast<float4*>(o) = make_float4(__uint_as_float(srow[0]), __uint_as_float(srow[1]),
-                                                      __uint_as_float(srow[2]), __uint_as_float(srow[3]));
+          *reinterpret_cast<float4*>(o) = val;
         }
       }
       __syncwarp();
@@ -200,7 +221,8 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
     // [-127, 127].  v comes from an integer accumulator times a finite scale
     // plus a finite bias (the loader rejects non-finite payloads and
     // scales), so it is finite unless it overflowed to +-inf, which the
-    // running |v| maximum detects.
+    // running |v| maximum detects.  Rows past m and columns past n get
+    // values too; the stores below skip them.
     uint32_t q4[8];
     float amax = 0.0f;
     const float al = g.alpha;
@@ -212,9 +234,9 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
       for (int u = 0; u < 4; ++u) {
         const int j = 4 * w + u;
         amax = fmaxf(amax, fabsf(v[j]));
-        float t = __fmul_rn(v[j], al);
+        float t = fminf(__fmul_rn(v[j], al), 127.0f);
         if (lower) t = fmaxf(t, -127.0f);
-        qv[u] = (ok && nb + j < n_end) ? cvt_rni_sat_s8(t) : 0;
+        qv[u] = round_to_low_byte(t);  // clamping before rounding = rounding before clamping
       }
       q4[w] = pack4_s8(qv[0], qv[1], qv[2], qv[3]);
     }
@@ -223,9 +245,11 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
     const bool aligned = ((reinterpret_cast<uintptr_t>(g.out) | (uintptr_t)g.ldo |
                            (uintptr_t)(g.col_off + nb)) & 3) == 0;
     if (full && aligned) {
-      // stage 32 rows x 32 bytes, then each instruction stores 4 rows x 32 B
-#pragma unroll
-      for (int w = 0; w < 8; ++w) stage[lane * 9 + w] = q4[w];
+      // stage 32 rows x 32 bytes (row stride 12 words), then each
+      // instruction stores 4 rows x 32 B
+      uint4* mine = reinterpret_cast<uint4*>(stage + lane * 12);
+      mine[0] = make_uint4(q4[0], q4[1], q4[2], q4[3]);
+      mine[1] = make_uint4(q4[4], q4[5], q4[6], q4[7]);
       __syncwarp();
       const int sub = lane >> 3, w = lane & 7;
 #pragma unroll
@@ -235,7 +259,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
         const bool rok = __shfl_sync(0xffffffffu, ok ? 1 : 0, rr) != 0;
         if (rok) {
           int8_t* o = static_cast<int8_t*>(g.out) + (size_t)drow * g.ldo + g.col_off + nb + 4 * w;
-          *reinterpret_cast<uint32_t*>(o) = stage[rr * 9 + w];
+          *reinterpret_cast<uint32_t*>(o) = stage[rr * 12 + w];
         }
       }
       __syncwarp();
@@ -381,7 +405,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
     // (rows), (warp - 2) / 4 the share of the tile's columns.
     const int quarter = warp & 3;
     const int part = (warp - 2) >> 2;
-    uint32_t* stage = staging + (warp - 2) * 32 * kStageLd;
+    uint32_t* stage = staging + (warp - 2) * 32 * stage_ld<EPI>();
     int it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       TileCoord c;
@@ -428,7 +452,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), EPI == 8 ? 2 : 1) q8_gemm_
         tmem_ld_32x32b_x32(lane_base + c0, r);
         tmem_ld_wait();
         if (c.n0 + c0 < g.n)
-          epilogue_chunk<BN>(g, r, row_ok && dest_row >= 0, row, dest_row, c.n0 + c0, row_scale,
+          epilogue_chunk<BN, EPI>(g, r, row_ok && dest_row >= 0, row, dest_row, c.n0 + c0, row_scale,
                              p.status, best, best_n, stage, has_bias ? sb + (c0 - c_first) : nullptr,
                              has_scale ? ss + (c0 - c_first) : nullptr);
       }
@@ -666,7 +690,7 @@ __global__ void __launch_bounds__(threads_for<kArgEpi>(), 1) q8_argmax_kernel(co
           tmem_ld_32x32b_x32(lane_base + c0, r);
           tmem_ld_wait();
           if (n0 + c0 < g.n)
-            epilogue_chunk<BN>(g, r, row_ok, row, row, n0 + c0, 1.0f, p.status, best, best_n, nullptr,
+            epilogue_chunk<BN, EPI>(g, r, row_ok, row, row, n0 + c0, 1.0f, p.status, best, best_n, nullptr,
                                g.bias ? sb + (c0 - part * kShare) : nullptr,
                                has_scale ? ss + (c0 - part * kShare) : nullptr);
         }
