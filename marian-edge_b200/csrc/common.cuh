@@ -234,22 +234,29 @@ __host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
 // ---- Q8 arithmetic shared by every kernel (q8_gemm.rs:569-590, 438-446) ------
 // Quantize one activation: round-half-even, clamp to [-127, 127].  The value
 // is stored centred (signed), i.e. the reference's u8 minus its zero point.
+// rint(t) for t in [-127, 127], in the low byte of the result (two's
+// complement): t + 1.5 * 2^23 lies in [2^23, 2^24), where adjacent floats
+// are 1 apart, so the round-to-nearest-even addition rounds t to an integer
+// and the sum's bit pattern is 0x4B400000 + rint(t).  One full-rate
+// floating-point addition instead of a rounding and a conversion, which
+// share one narrow pipe.
+__device__ __forceinline__ int rint_low_byte(float t) {
+  return __float_as_int(__fadd_rn(t, 12582912.0f));
+}
+
+// rint(v * alpha) clamped to [-127, 127] in the low byte (clamping first and
+// rounding after gives the same value); a non-finite v gives an unspecified
+// byte, so callers report it.
+__device__ __forceinline__ int quantize_low_byte(float v, float alpha) {
+  return rint_low_byte(fminf(fmaxf(__fmul_rn(v, alpha), -127.0f), 127.0f));
+}
+
 __device__ __forceinline__ int8_t quantize_one(float v, float alpha, uint32_t* status) {
   if (!isfinite(v)) {
     flag_status(status, kStatusNonFinite);
     return 0;
   }
-  float s = rintf(__fmul_rn(v, alpha));
-  s = fminf(fmaxf(s, -127.0f), 127.0f);
-  return static_cast<int8_t>(static_cast<int>(s));
-}
-
-// quantize_one without the finiteness check (the caller checks a block of
-// values at once): rint(v * alpha) clamped to [-127, 127].  A NaN converts
-// to 0 and is reported by the caller.
-__device__ __forceinline__ int quantize_rte_clamped(float v, float alpha) {
-  const int q = __float2int_rn(__fmul_rn(v, alpha));  // saturating conversion
-  return q < -127 ? -127 : (q > 127 ? 127 : q);
+  return static_cast<int8_t>(quantize_low_byte(v, alpha));
 }
 
 // acc as f32 * scale + bias, two roundings (no fused multiply-add).

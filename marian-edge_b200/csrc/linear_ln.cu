@@ -89,13 +89,10 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t phase,
   return false;
 }
 
-// quantize_one (common.cuh) for four values and every copy: rint(v * alpha)
-// saturated by the conversion, then raised to -127; a non-finite value
-// converts to 0 and is reported once for the four.
+// quantize_one (common.cuh) for four values and every copy, the result in
+// the low byte; a non-finite value is reported once for the four.
 __device__ __forceinline__ int quant_s8(float v, float alpha) {
-  int r;
-  asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(__fmul_rn(v, alpha)));
-  return r < -127 ? -127 : r;
+  return quantize_low_byte(v, alpha);
 }
 
 __device__ __forceinline__ void store_copies(const QuantOut& q, long long elem, float4 v,

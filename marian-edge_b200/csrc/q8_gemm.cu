@@ -60,15 +60,6 @@ constexpr int staging_bytes() {
   return EPI * 32 * stage_ld<EPI>() * 4;
 }
 
-// rint(t) for t in [-127, 127], in the low byte of the result (two's
-// complement): t + 1.5 * 2^23 lies in [2^23, 2^24), where adjacent floats
-// are 1 apart, so the round-to-nearest-even addition rounds t to an integer
-// and the sum's bit pattern is 0x4B400000 + rint(t).  Two full-rate
-// floating-point operations (with the clamp) instead of a conversion.
-__device__ __forceinline__ int round_to_low_byte(float t) {
-  return __float_as_int(__fadd_rn(t, 12582912.0f));
-}
-
 // Low bytes of four ints -> one word (byte i = q[i]).
 __device__ __forceinline__ uint32_t pack4_s8(int q0, int q1, int q2, int q3) {
   const uint32_t lo = __byte_perm((uint32_t)q0, (uint32_t)q1, 0x0040);
@@ -236,7 +227,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmGroup& g, const uint32_
         amax = fmaxf(amax, fabsf(v[j]));
         float t = fminf(__fmul_rn(v[j], al), 127.0f);
         if (lower) t = fmaxf(t, -127.0f);
-        qv[u] = round_to_low_byte(t);  // clamping before rounding = rounding before clamping
+        qv[u] = rint_low_byte(t);  // clamping before rounding = rounding before clamping
       }
       q4[w] = pack4_s8(qv[0], qv[1], qv[2], qv[3]);
     }
