@@ -23,6 +23,11 @@ The same JSON line also carries, unless --no-configs:
     pseudo-sentence end every 8..64 tokens, split by the library's
     segment_text into segments of at most 128 tokens with EOS, sorted by
     length and dealt round-robin over the N replicas;
+  * config2_gemm -- config 2: the Q8 GEMM operator over (K, N) in
+    {(512, 1536), (512, 2048), (2048, 512), (512, 32000)} x M in
+    {1, 7, 64, 333, 1024, 4096}, microseconds per launch back to back with
+    operands from HBM, against the int8 tensor rate (M >= 64) or the HBM
+    copy rate (weight streaming, M <= 7);
   * latency_ms -- config 4's latency: 20,000 requests replayed with Poisson
     arrivals at 2,000 req/s, and again near capacity, by the library's own
     arrival loop (mc_replay), p50/p99 from arrival to last token.
@@ -68,7 +73,7 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-latency", action="store_true")
-    p.add_argument("--no-configs", action="store_true", help="skip the config 3 and config 5 lines")
+    p.add_argument("--no-configs", action="store_true", help="skip the config 2, 3 and 5 lines")
     p.add_argument("--workload", default="stream", choices=["stream", "longtext"])
     p.add_argument("--docs", type=int, default=500, help="longtext workload: documents per GPU per step")
     p.add_argument("--longtext-docs", type=int, default=400, help="config 5: global documents")
@@ -365,6 +370,77 @@ def measure_encoder(args, eng, lib, L, model_bytes, peaks, peak_kind, rank, worl
     return out
 
 
+GEMM_SHAPES = [(512, 1536), (512, 2048), (2048, 512), (512, 32000)]  # (K, N)
+GEMM_ROWS = [1, 7, 64, 333, 1024, 4096]
+L2_BYTES = 126 << 20
+
+
+def measure_gemm(lib, peaks, peak_kind, iters=20):
+    """Config 2: the Q8 GEMM operator (mc_q8_gemm, f32 epilogue with per-row
+    and per-column scales and a bias) over the (K, N) x M grid.  Weights and
+    activations cycle through copies totalling more than twice the L2, so
+    every timed launch reads its operands from HBM.  A spin kernel ahead of
+    the timed launches keeps the stream busy while the host enqueues them,
+    so CUDA events around `iters` launches time them back to back on the
+    device rather than the host's call rate."""
+    import torch
+    dev = torch.device("cuda")
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2)
+    points = []
+    for k, n in GEMM_SHAPES:
+        nw = max(2, -(-2 * L2_BYTES // (n * k)))
+        w = torch.randint(-127, 128, (nw, n, k), dtype=torch.int8, device=dev, generator=gen)
+        col_scale = torch.rand(n, device=dev, generator=gen) * 0.019 + 0.001
+        bias = torch.rand(n, device=dev, generator=gen) * 0.2 - 0.1
+        for m in GEMM_ROWS:
+            na = max(2, -(-2 * L2_BYTES // (m * k)))
+            a = torch.randint(-127, 128, (na, m, k), dtype=torch.int8, device=dev, generator=gen)
+            row_scale = torch.rand(m, device=dev, generator=gen) * 0.019 + 0.001
+            out = torch.empty((m, n), dtype=torch.float32, device=dev)
+
+            a0, w0, rs, cs, bs, o = (a.data_ptr(), w.data_ptr(), row_scale.data_ptr(), col_scale.data_ptr(),
+                                     bias.data_ptr(), out.data_ptr())
+
+            def launch(i):
+                st = lib.mc_q8_gemm(a0 + (i % na) * m * k, w0 + (i % nw) * n * k, m, n, k, rs, cs, bs, None, 0, 1,
+                                    o, sp)
+                if st != 0:
+                    raise RuntimeError(f"mc_q8_gemm failed ({st}) at M={m} K={k} N={n}")
+
+            for i in range(3):
+                launch(i)
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            torch.cuda._sleep(4_000_000)  # ~2 ms of device time: longer than enqueueing the launches
+            start.record(stream)
+            for i in range(3, 3 + iters):
+                launch(i)
+            end.record(stream)
+            torch.cuda.synchronize()
+            sec = start.elapsed_time(end) / 1000.0 / iters
+            ops = 2.0 * m * n * k
+            nbytes = m * k + n * k + 8 * n + 4 * m + 4 * m * n
+            tensor = m >= 64  # the configuration's own rule: weight streaming below 64 rows
+            tensor_frac = ops / sec / 1e12 / (2.0 * peaks["bf16_tflops"])
+            hbm_frac = nbytes / sec / 1e9 / peaks["hbm_gbs"]
+            # frac follows the rule; both are given, since at large M x N the
+            # f32 output's bytes, not the MMAs, set the floor
+            points.append({"k": k, "n": n, "m": m, "us": sec * 1e6, "tops": ops / sec / 1e12,
+                           "gbs": nbytes / sec / 1e9, "bound": "tensor" if tensor else "hbm",
+                           "frac": tensor_frac if tensor else hbm_frac, "tensor_frac": tensor_frac,
+                           "hbm_frac": hbm_frac})
+            del a, row_scale, out
+        del w
+    torch.cuda.empty_cache()
+    return {"workload": "config 2: mc_q8_gemm, int8 A [M,K] x int8 W [N,K], f32 out with per-row and "
+                        "per-column scales and bias; operands cycled through > 2 x L2 of copies",
+            "unit": "us per launch", "peak_source": f"{peak_kind}: 2 x bf16 dense TFLOP/s (int8) for M >= 64, "
+                                                    "HBM copy GB/s below", "points": points}
+
+
 def measure_longtext(args, eng, stream, model_bytes, rank, world, barrier):
     """Config 5 as strong scaling: a fixed global document set dealt over
     the replicas by length bucket."""
@@ -496,6 +572,8 @@ def run_cuda(args):
                                                    world)
     if not args.no_latency and rank == 0 and args.workload == "stream":
         extra["latency_ms"] = measure_latency(args, eng)
+    if not args.no_configs and rank == 0 and args.workload == "stream":
+        extra["config2_gemm"] = measure_gemm(lib, peaks, peak_kind)
 
     if rank == 0:
         roofline = None
