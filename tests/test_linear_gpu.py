@@ -69,3 +69,20 @@ def test_non_finite_activation_is_reported():
     w = np.ones((3, 16), np.int8)
     _, bits = run_linear(x, w, 1.0, 1.0)
     assert bits & 1
+
+
+def test_quantization_ties_and_clamps_reference_vector():
+    # q8_gemm.rs:609-617: multiplier 1 quantizes
+    # [-200, -127.6, -126.5, -1.5, -0.5, 0.5, 1.5, 126.5, 127.6, 200] to the u8
+    # values [0, 0, 1, 125, 127, 127, 129, 253, 254, 254] (ties to even,
+    # clamped to +-127 around the zero point 127).  An identity weight matrix
+    # with both multipliers 1 returns the centred integers as the outputs.
+    x = np.zeros((1, 16), np.float32)
+    x[0, :10] = [-200.0, -127.6, -126.5, -1.5, -0.5, 0.5, 1.5, 126.5, 127.6, 200.0]
+    w = np.eye(16, dtype=np.int8)
+    got, bits = run_linear(x, w, 1.0, 1.0)
+    assert bits == 0
+    u8 = np.array([0, 0, 1, 125, 127, 127, 129, 253, 254, 254], np.float32)
+    np.testing.assert_array_equal(got[0, :10], u8 - 127.0)
+    np.testing.assert_array_equal(got[0, 10:], 0.0)
+    np.testing.assert_array_equal(O.quantize_u8(x[0, :10], 1.0), u8.astype(np.uint8))
