@@ -127,6 +127,9 @@ struct Lane {
   bool own_stream = false;
   cudaStream_t enc_stream = nullptr; // encoder passes of admissions
   cudaEvent_t enc_done = nullptr;    // the last admission's encoder pass is complete
+  // encoder attention buckets side by side (see launch_encoder_buckets)
+  cudaEvent_t enc_fork = nullptr, enc_join = nullptr;
+  bool enc_alone = false;  // the pass being enqueued has no decode step beside it
   cudaStream_t cur = nullptr;        // stream the launch helpers use
   uint32_t* d_status = nullptr;      // error bits of this lane's kernels
 
@@ -610,6 +613,37 @@ AdmLayout adm_layout(int T, int B, int pps) {
 }
 
 // ---- encoder pass over packed admitted sources ------------------------------
+
+// The encoder attention over the pass's length buckets (disjoint sequences,
+// so independent): one launch per bucket, shared memory sized to its
+// longest sequence.  When no decode step runs beside the pass (and outside
+// profiling) the shorter buckets run on the lane's idle decode stream,
+// forked from the encoder stream after the QKV projection and joined back
+// before the output projection, so the few long sequences' CTAs run beside
+// the many short ones instead of after them.  Beside decode steps the
+// buckets stay on the encoder stream: more encoder CTAs at once would hold
+// SMs that the latency-bound decode chain waits for.
+cudaError_t launch_encoder_buckets(mc_engine* e, Lane& L, const int32_t* cu, const int32_t* seq_ids, int d,
+                                   float alpha) {
+  const int nb = (int)L.buckets.size();
+  const bool fork = !e->profiling && L.enc_alone && nb > 1 && L.cur != L.stream;
+  cudaError_t err = cudaSuccess;
+  if (fork && ((err = cudaEventRecord(L.enc_fork, L.cur)) != cudaSuccess ||
+               (err = cudaStreamWaitEvent(L.stream, L.enc_fork, 0)) != cudaSuccess))
+    return err;
+  for (int i = 0; i < nb; ++i) {
+    const Lane::Bucket& bk = L.buckets[i];
+    cudaStream_t s = (fork && i < nb - 1) ? L.stream : L.cur;
+    err = launch_attn_encoder(L.enc_qkv, cu, seq_ids + bk.offset, bk.count, bk.max_len, d, e->heads, L.enc_o.p,
+                              alpha, L.d_status, s);
+    if (err != cudaSuccess) return err;
+  }
+  if (fork && ((err = cudaEventRecord(L.enc_join, L.stream)) != cudaSuccess ||
+               (err = cudaStreamWaitEvent(L.cur, L.enc_join, 0)) != cudaSuccess))
+    return err;
+  return cudaSuccess;
+}
+
 mc_status run_encoder(mc_engine* e, Lane& L, const AdmLayout& A, double sum_len_sq) {
   const int d = e->d;
   const int T = A.T;
@@ -630,12 +664,8 @@ mc_status run_encoder(mc_engine* e, Lane& L, const AdmLayout& A, double sum_len_
         {&L.enc_q[1], &a.wk, kEpiF32, L.enc_qkv, 3 * d, d, nullptr, false, 0.f},
         {&L.enc_q[2], &a.wv, kEpiF32, L.enc_qkv, 3 * d, 2 * d, nullptr, false, 0.f}};
     if ((st = gemm(e, L, MC_K_GEMM_QKV, T, nullptr, T, qkv, 3))) return st;
-    PROFILED(MC_K_ATTN_ENC, 4.0 * sum_len_sq * d, rows_d * (12 + 1), {
-      for (const auto& bk : L.buckets)
-        CK(launch_attn_encoder(L.enc_qkv, adm + A.cu, adm + A.seq_ids + bk.offset, bk.count,
-                               bk.max_len, d, e->heads, L.enc_o.p, a.wo.alpha, L.d_status,
-                               L.cur));
-    });
+    PROFILED(MC_K_ATTN_ENC, 4.0 * sum_len_sq * d, rows_d * (12 + 1),
+             CK(launch_encoder_buckets(e, L, adm + A.cu, adm + A.seq_ids, d, a.wo.alpha)));
     e->launches += L.buckets.size();
     GroupSpec wo = {&L.enc_o, &a.wo, kEpiF32, L.enc_proj, d, 0, nullptr, false, 0.f};
     if ((st = gemm(e, L, MC_K_GEMM_OUT, T, nullptr, T, &wo, 1))) return st;
@@ -894,6 +924,8 @@ mc_engine::~mc_engine() {
     if (L.own_stream && L.stream) cudaStreamDestroy(L.stream);
     if (L.enc_stream) cudaStreamDestroy(L.enc_stream);
     if (L.enc_done) cudaEventDestroy(L.enc_done);
+    if (L.enc_fork) cudaEventDestroy(L.enc_fork);
+    if (L.enc_join) cudaEventDestroy(L.enc_join);
   }
   for (cudaEvent_t ev : event_pool) cudaEventDestroy(ev);
   for (void* p : allocations) cudaFree(p);
@@ -1035,6 +1067,8 @@ mc_status allocate_buffers(mc_engine* e) {
     }
     CK(cudaStreamCreateWithPriority(&L.enc_stream, cudaStreamNonBlocking, prio_low));
     CK(cudaEventCreateWithFlags(&L.enc_done, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&L.enc_fork, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&L.enc_join, cudaEventDisableTiming));
     L.cur = L.stream;
     mc_status st = allocate_lane(e, L);
     if (st) return st;
@@ -1241,6 +1275,9 @@ mc_status admit(mc_engine* e, Lane& L, int cap) {
   L.enc_in_flight = true;
   L.cur = s;
   CK(cudaMemcpyAsync(L.adm_d, L.adm_h, A.end * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+  L.enc_alone = true;
+  for (const Lane& X : e->lanes)
+    if (!X.active.empty() || !X.inflight.empty()) L.enc_alone = false;
   mc_status st = run_encoder(e, L, A, sum_len_sq);
   L.cur = L.stream;
   if (st) return st;
